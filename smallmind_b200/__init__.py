@@ -1,0 +1,16 @@
+"""SmallMind.Cuda — B200-native (sm_100a) quantized decode/prefill path for SmallMind.
+
+The product is ``libsmallmind_cuda.so`` (C-ABI: include/smallmind_cuda.h).  This
+package is its host-side mirror of the reference operator API; it has no CPU
+compute path.
+"""
+from ._lib import (LAYOUT_INTENDED, LAYOUT_REFERENCE, PTR_DEVICE, PTR_HOST, ShapeError, SmallMindCudaError,
+                   last_error, lib)
+from .api import (CudaContext, CudaModel, CudaWeightTensor, InferenceSession, KVCache, QuantScheme, attention,
+                  rmsnorm, rope, silu_mul)
+
+__all__ = [
+    "CudaContext", "CudaModel", "CudaWeightTensor", "InferenceSession", "KVCache", "QuantScheme", "attention",
+    "rmsnorm", "rope", "silu_mul", "LAYOUT_INTENDED", "LAYOUT_REFERENCE", "PTR_HOST", "PTR_DEVICE", "ShapeError",
+    "SmallMindCudaError", "last_error", "lib",
+]

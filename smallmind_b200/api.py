@@ -1,0 +1,312 @@
+"""Host-side mirror of the reference's operator API for the quantized hot path.
+
+``CudaWeightTensor`` implements the reference ``IWeightTensor`` contract
+(src/SmallMind.Quantization/Abstractions/IWeightTensor.cs:7-42): ``Rows``,
+``Cols``, ``Scheme``, ``MatMul(activations, output, m, k, n)`` and
+``ToFloat32()``, with the reference's ArgumentException rules surfaced as
+``ValueError`` (``ShapeError``).  ``CudaModel`` / ``InferenceSession`` mirror the
+generation loop around it (TransformerModel.Forward, InferenceSession
+.GenerateNextTokenAsync) on the device-resident model and HBM KV cache.
+
+Everything runs in libsmallmind_cuda.so; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from enum import IntEnum
+
+import numpy as np
+
+from . import _lib as L
+
+
+class QuantScheme(IntEnum):
+    """IWeightTensor.cs:47-72."""
+    F32 = 0
+    F16 = 1
+    Q8_0 = 2
+    Q4_0 = 3
+    Q4_1 = 4
+    Q5_0 = 5
+    Q4_K = 6
+    Q6_K = 7
+
+
+def _p(a: np.ndarray):
+    if not a.flags["C_CONTIGUOUS"]:
+        raise ValueError("arrays must be C-contiguous")
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class CudaContext:
+    """One device + one CUDA stream (sm_ctx)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        L.check(L.lib().sm_ctx_create(device, C.byref(h)), "sm_ctx_create")
+        self.handle = h
+        self.device = device
+
+    def sync(self):
+        L.check(L.lib().sm_stream_sync(self.handle), "sm_stream_sync")
+
+    def set_stream(self, stream_ptr: int | None):
+        L.check(L.lib().sm_ctx_set_stream(self.handle, C.c_void_p(stream_ptr or 0)), "sm_ctx_set_stream")
+
+    def launch_count(self) -> int:
+        v = C.c_int64()
+        L.check(L.lib().sm_ctx_launch_count(self.handle, C.byref(v)))
+        return v.value
+
+    def device_status(self) -> int:
+        return L.lib().sm_ctx_device_status(self.handle)
+
+    def close(self):
+        if self.handle:
+            L.lib().sm_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaWeightTensor:
+    """IWeightTensor on the GPU (Q8WeightTensor / Q4WeightTensor / Q4KWeightTensor / Q6KWeightTensor).
+
+    ``layout`` LAYOUT_INTENDED (default): Rows = out features N, Cols = in
+    features K, MatMul computes output = activations x weights^T.
+    ``layout`` LAYOUT_REFERENCE: the reference kernels as written, Rows = K,
+    Cols = N, MatMul computes C = A x B.
+    """
+
+    def __init__(self, ctx: CudaContext, scheme: int, rows: int, cols: int, data: np.ndarray,
+                 scales: np.ndarray | None = None, block_size: int = 64, layout: int = L.LAYOUT_INTENDED):
+        data = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        sc = None if scales is None else np.ascontiguousarray(scales, np.float32)
+        h = C.c_void_p()
+        L.check(L.lib().sm_weight_upload(ctx.handle, int(scheme), rows, cols, block_size, _p(data), data.size,
+                                         _p(sc) if sc is not None else None, 0 if sc is None else sc.size,
+                                         layout, C.byref(h)), "sm_weight_upload")
+        self.ctx, self.handle = ctx, h
+        self._rows, self._cols, self._scheme, self.layout = rows, cols, QuantScheme(scheme), layout
+
+    @classmethod
+    def from_qtensor(cls, ctx: CudaContext, t, layout: int = L.LAYOUT_INTENDED) -> "CudaWeightTensor":
+        """From any object with scheme/rows/cols/data/scales/block_size (e.g. a packed host tensor)."""
+        return cls(ctx, t.scheme, t.rows, t.cols, t.data, t.scales, t.block_size, layout)
+
+    # IWeightTensor.cs:12-22
+    @property
+    def Rows(self) -> int:
+        return self._rows
+
+    @property
+    def Cols(self) -> int:
+        return self._cols
+
+    @property
+    def Scheme(self) -> QuantScheme:
+        return self._scheme
+
+    def nbytes(self) -> int:
+        v = C.c_size_t()
+        L.check(L.lib().sm_weight_nbytes(self.handle, C.byref(v)))
+        return v.value
+
+    def MatMul(self, activations: np.ndarray, output: np.ndarray, m: int, k: int, n: int) -> None:
+        """IWeightTensor.MatMul (IWeightTensor.cs:33); output is overwritten."""
+        a = np.ascontiguousarray(activations, np.float32).reshape(-1)
+        if a.size < m * k:
+            raise L.ShapeError(-2, f"activations.Length {a.size} < m*k {m * k}")
+        if output.dtype != np.float32 or not output.flags["C_CONTIGUOUS"] or output.size < m * n:
+            raise L.ShapeError(-2, f"output.Length {output.size} < m*n {m * n}")
+        L.check(L.lib().sm_matmul(self.handle, _p(a), _p(output), m, k, n, L.PTR_HOST), "MatMul")
+
+    def matmul_device(self, a_ptr: int, c_ptr: int, m: int) -> None:
+        """Device-pointer variant (asynchronous on the context stream)."""
+        k = self._cols if self.layout == L.LAYOUT_INTENDED else self._rows
+        n = self._rows if self.layout == L.LAYOUT_INTENDED else self._cols
+        L.check(L.lib().sm_matmul(self.handle, C.c_void_p(a_ptr), C.c_void_p(c_ptr), m, k, n, L.PTR_DEVICE),
+                "matmul_device")
+
+    def ToFloat32(self) -> np.ndarray:
+        """IWeightTensor.ToFloat32 (IWeightTensor.cs:41): bit-exact dequantization."""
+        out = np.empty(self._rows * self._cols, np.float32)
+        L.check(L.lib().sm_dequant(self.handle, _p(out), L.PTR_HOST), "ToFloat32")
+        return out
+
+    def close(self):
+        if self.handle:
+            L.lib().sm_weight_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------- ops
+def rmsnorm(ctx: CudaContext, x: np.ndarray, gamma: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """RMSNormOps.RMSNorm (RMSNormOps.cs:28-220)."""
+    x = np.ascontiguousarray(x, np.float32)
+    g = np.ascontiguousarray(gamma, np.float32)
+    rows = x.size // g.size
+    y = np.empty_like(x)
+    L.check(L.lib().sm_op_rmsnorm(ctx.handle, _p(x), _p(g), _p(y), rows, g.size, eps, L.PTR_HOST), "rmsnorm")
+    return y
+
+
+def rope(ctx: CudaContext, x: np.ndarray, n_heads: int, head_dim: int, positions, theta: float = 10000.0,
+         max_seq: int = 2048) -> np.ndarray:
+    """RotaryEmbedding.ApplyInPlace (RotaryEmbedding.cs:69-121) on token rows [rows][n_heads*head_dim]."""
+    x = np.ascontiguousarray(x, np.float32).copy()
+    pos = np.ascontiguousarray(positions, np.int32)
+    L.check(L.lib().sm_op_rope(ctx.handle, _p(x), pos.size, n_heads, head_dim, _p(pos), theta, max_seq,
+                               L.PTR_HOST), "rope")
+    return x
+
+
+def silu_mul(ctx: CudaContext, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """ActivationOps.FusedSiLUMul (ActivationOps.cs:565-580)."""
+    g = np.ascontiguousarray(gate, np.float32)
+    u = np.ascontiguousarray(up, np.float32)
+    out = np.empty_like(g)
+    L.check(L.lib().sm_op_silu_mul(ctx.handle, _p(g), _p(u), _p(out), g.size, L.PTR_HOST), "silu_mul")
+    return out
+
+
+def attention(ctx: CudaContext, q, k, v, T: int, S: int, n_heads: int, n_kv: int, head_dim: int) -> np.ndarray:
+    """Causal GQA attention with the reference's Pade softmax (MultiHeadAttention.cs:676-744, 810-844)."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    out = np.empty((T, n_heads * head_dim), np.float32)
+    L.check(L.lib().sm_attention(ctx.handle, _p(q), _p(k), _p(v), _p(out), T, S, n_heads, n_kv, head_dim,
+                                 L.PTR_HOST), "attention")
+    return out
+
+
+# ---------------------------------------------------------------- model
+ROLE_OF = {"wq": L.ROLE_WQ, "wk": L.ROLE_WK, "wv": L.ROLE_WV, "wo": L.ROLE_WO, "w_gate": L.ROLE_W_GATE,
+           "w_up": L.ROLE_W_UP, "w_down": L.ROLE_W_DOWN}
+
+
+class CudaModel:
+    """new TransformerModel(ModelConfig) (TransformerModel.cs:163-259) resident on one GPU."""
+
+    def __init__(self, ctx: CudaContext, cfg: dict):
+        self.ctx, self.cfg = ctx, dict(cfg)
+        c = L.ModelConfig(cfg["vocab_size"], cfg["hidden"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"],
+                          cfg["head_dim"], cfg["ffn_hidden"], cfg["max_context"], cfg.get("norm_eps", 1e-5),
+                          cfg.get("rope_theta", 10000.0))
+        h = C.c_void_p()
+        L.check(L.lib().sm_model_create(ctx.handle, C.byref(c), C.byref(h)), "sm_model_create")
+        self.handle = h
+        self._weights = []  # keeps borrowed weights alive
+
+    def set_weight(self, layer: int, name: str, w: CudaWeightTensor):
+        role = L.ROLE_OUTPUT if name == "output" else ROLE_OF[name]
+        L.check(L.lib().sm_model_set_weight(self.handle, layer, role, w.handle), f"set_weight {name}")
+        self._weights.append(w)
+
+    def set_vector(self, layer: int, name: str, data: np.ndarray):
+        role = {"attn_norm": L.ROLE_ATTN_NORM, "ffn_norm": L.ROLE_FFN_NORM, "token_embd": L.ROLE_TOKEN_EMBD,
+                "out_norm": L.ROLE_OUT_NORM}[name]
+        d = np.ascontiguousarray(data, np.float32).reshape(-1)
+        L.check(L.lib().sm_model_set_vector(self.handle, layer, role, _p(d), d.size), f"set_vector {name}")
+
+    def finalize(self):
+        L.check(L.lib().sm_model_finalize(self.handle), "sm_model_finalize")
+
+    @classmethod
+    def from_host(cls, ctx: CudaContext, host_model) -> "CudaModel":
+        """Upload a packed host model (token_embd, out_norm, output, layers[...] dicts)."""
+        m = cls(ctx, host_model.cfg)
+        m.set_vector(0, "token_embd", host_model.token_embd)
+        m.set_vector(0, "out_norm", host_model.out_norm)
+        m.set_weight(0, "output", CudaWeightTensor.from_qtensor(ctx, host_model.output))
+        for li, layer in enumerate(host_model.layers):
+            m.set_vector(li, "attn_norm", layer["attn_norm"])
+            m.set_vector(li, "ffn_norm", layer["ffn_norm"])
+            for n in ROLE_OF:
+                m.set_weight(li, n, CudaWeightTensor.from_qtensor(ctx, layer[n]))
+        m.finalize()
+        return m
+
+    def nbytes(self) -> int:
+        v = C.c_size_t()
+        L.check(L.lib().sm_model_nbytes(self.handle, C.byref(v)))
+        return v.value
+
+    def close(self):
+        if self.handle:
+            L.lib().sm_model_destroy(self.handle)
+            self.handle = None
+
+
+class KVCache:
+    """HBM KV cache for many sequences (sm_kv)."""
+
+    def __init__(self, model: CudaModel, max_seqs: int, max_tokens: int):
+        h = C.c_void_p()
+        L.check(L.lib().sm_kv_create(model.handle, max_seqs, max_tokens, C.byref(h)), "sm_kv_create")
+        self.model, self.handle = model, h
+        self.max_seqs, self.max_tokens = max_seqs, max_tokens
+
+    def reset(self, seq: int):
+        L.check(L.lib().sm_kv_reset(self.handle, seq), "sm_kv_reset")
+
+    def length(self, seq: int) -> int:
+        v = C.c_int()
+        L.check(L.lib().sm_kv_length(self.handle, seq, C.byref(v)), "sm_kv_length")
+        return v.value
+
+    def prefill(self, seq: int, tokens, want_logits: bool = True):
+        toks = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.model.cfg["vocab_size"], np.float32) if want_logits else None
+        nxt = np.zeros(1, np.int32)
+        L.check(L.lib().sm_prefill(self.model.handle, self.handle, seq, _p(toks), toks.size,
+                                   _p(logits) if want_logits else None, _p(nxt)), "sm_prefill")
+        return int(nxt[0]), logits
+
+    def decode(self, seq_ids, tokens, want_logits: bool = True):
+        s = np.ascontiguousarray(seq_ids, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        n = s.size
+        logits = np.empty((n, self.model.cfg["vocab_size"]), np.float32) if want_logits else None
+        nxt = np.zeros(n, np.int32)
+        L.check(L.lib().sm_decode(self.model.handle, self.handle, _p(s), _p(t), n,
+                                  _p(logits) if want_logits else None, _p(nxt), L.PTR_HOST), "sm_decode")
+        return nxt, logits
+
+    def decode_device(self, seq_ptr: int, tok_ptr: int, n: int, logits_ptr: int | None, next_ptr: int | None):
+        """All-device step (no host sync): inputs/outputs are device pointers."""
+        L.check(L.lib().sm_decode(self.model.handle, self.handle, C.c_void_p(seq_ptr), C.c_void_p(tok_ptr), n,
+                                  C.c_void_p(logits_ptr or 0), C.c_void_p(next_ptr or 0), L.PTR_DEVICE),
+                "sm_decode")
+
+    def close(self):
+        if self.handle:
+            L.lib().sm_kv_destroy(self.handle)
+            self.handle = None
+
+
+class InferenceSession:
+    """Greedy generation loop (InferenceSession.GenerateNextTokenAsync, TopK = 1) over one sequence slot."""
+
+    def __init__(self, kv: KVCache, seq: int = 0):
+        self.kv, self.seq = kv, seq
+
+    def generate(self, prompt_ids, max_new_tokens: int, return_logits: bool = False):
+        self.kv.reset(self.seq)
+        nxt, logits = self.kv.prefill(self.seq, prompt_ids, want_logits=return_logits)
+        out, all_logits = [nxt], [logits] if return_logits else []
+        for _ in range(max_new_tokens - 1):
+            t, lg = self.kv.decode([self.seq], [out[-1]], want_logits=return_logits)
+            out.append(int(t[0]))
+            if return_logits:
+                all_logits.append(lg[0])
+        return (out, all_logits) if return_logits else out
