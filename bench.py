@@ -1,0 +1,400 @@
+"""Benchmark of the SmallMind quantized decode path on B200.
+
+Workload (BASELINE config 3/5): TinyLlama-1.1B-shaped LLaMA, random-init
+N(0, 0.02), Q4_K_M-style mix (Q4_K for Q/K/O/gate/up, Q6_K for V/down/head),
+fp32 embedding.  Each GPU holds a full replica and decodes its own sequence
+(sequence sharding, no collectives; scaling "weak").  A step is one greedy
+decode token per sequence after a 2048-token prompt, so the context grows
+2048 -> 2048+W+K.  The weights (667 MB per token) are larger than L2, so no
+flush is needed between steps.
+
+Printed JSON (rank 0): value = decode tokens/s summed over GPUs, device-timed
+(CUDA events on the library's stream, max over ranks); e2e = the same loop
+through the host-pointer C-ABI (token H2D + next token D2H every step);
+roofline = the Q4_K GEMV (the dominant kernel) against measured HBM bandwidth;
+cpu_baseline = the CPU oracle (C++ restatement of the reference algorithm) on a
+bounded sample of the same workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TINYLLAMA = dict(vocab_size=32000, hidden=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64,
+                 ffn_hidden=5632, max_context=2048 + 512, norm_eps=1e-5, rope_theta=10000.0)
+PROMPT = 2048
+SCHEMES = dict(wq="Q4_K", wk="Q4_K", wv="Q6_K", wo="Q4_K", w_gate="Q4_K", w_up="Q4_K", w_down="Q6_K", output="Q6_K")
+METRIC = "decode tok/s (bs1, bs64) + Q4_K GEMV HBM GB/s vs peak; prefill tok/s"
+BYTES = {"Q4_K": 144 / 256, "Q6_K": 210 / 256, "Q8_0": 1.0 + 4 / 32, "Q4_0": 0.5 + 4 / 32}
+
+
+def linear_shapes(c):
+    H, F, V = c["hidden"], c["ffn_hidden"], c["vocab_size"]
+    qd, kd = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
+    return {"wq": (qd, H), "wk": (kd, H), "wv": (kd, H), "wo": (H, qd), "w_gate": (F, H), "w_up": (F, H),
+            "w_down": (H, F), "output": (V, H)}
+
+
+def weight_bytes_per_token(c):
+    sh = linear_shapes(c)
+    tot = 0.0
+    for n, (r, k) in sh.items():
+        mult = 1 if n == "output" else c["n_layers"]
+        tot += mult * r * k * BYTES[SCHEMES[n]]
+    return tot
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, out_path):
+        self.out_path = out_path
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.out_path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self, device):
+        try:
+            rows = [l.split(",") for l in open(self.out_path).read().strip().splitlines()]
+        except Exception:
+            return None
+        rows = [[x.strip() for x in r] for r in rows if len(r) >= 9 and r[0].strip() == str(device)]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- model build on the GPU
+def build_gpu_model(sm, ctx, cfg, seed=1234):
+    import ctypes as C
+
+    import torch
+    from smallmind_b200 import _lib as L
+    lib = L.lib()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    model = sm.CudaModel(ctx, cfg)
+    weights = {}
+
+    def make(name, rows, cols):
+        sch = int(getattr(sm.QuantScheme, SCHEMES[name]))
+        n = rows * cols
+        src = torch.randn(n, generator=gen, device="cuda") * 0.02
+        nbytes = {6: n // 256 * 144, 7: n // 256 * 210, 2: n, 3: n // 2}[sch]
+        data = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        scales = torch.empty(max(1, n // 32), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        L.check(lib.sm_quantize(ctx.handle, sch, src.data_ptr(), n, 32, data.data_ptr(), scales.data_ptr()),
+                "quantize")
+        h = C.c_void_p()
+        L.check(lib.sm_weight_upload_device(ctx.handle, sch, rows, cols, 32, data.data_ptr(), nbytes,
+                                            scales.data_ptr() if sch in (2, 3) else None,
+                                            n // 32 if sch in (2, 3) else 0, L.LAYOUT_INTENDED, C.byref(h)),
+                "upload")
+        w = sm.CudaWeightTensor.__new__(sm.CudaWeightTensor)
+        w.ctx, w.handle, w._rows, w._cols = ctx, h, rows, cols
+        w._scheme, w.layout = sm.QuantScheme(sch), L.LAYOUT_INTENDED
+        return w
+
+    sh = linear_shapes(cfg)
+    emb = (torch.randn(cfg["vocab_size"] * cfg["hidden"], generator=gen, device="cuda") * 0.02).cpu().numpy()
+    model.set_vector(0, "token_embd", emb)
+    ones = np.ones(cfg["hidden"], np.float32)
+    model.set_vector(0, "out_norm", ones)
+    weights["output"] = [make("output", *sh["output"])]
+    model.set_weight(0, "output", weights["output"][0])
+    for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+        weights[n] = []
+    for l in range(cfg["n_layers"]):
+        model.set_vector(l, "attn_norm", ones)
+        model.set_vector(l, "ffn_norm", ones)
+        for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+            w = make(n, *sh[n])
+            weights[n].append(w)
+            model.set_weight(l, n, w)
+    model.finalize()
+    return model, weights
+
+
+def time_gemv(sm, ctx, ws, torch, reps=5):
+    """Device time of the M=1 GEMV over a rotating set of layer weights (> L2)."""
+    K, N = ws[0].Cols, ws[0].Rows
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    st = torch.cuda.current_stream()
+    for w in ws:  # warm
+        w.matmul_device(x.data_ptr(), y.data_ptr(), 1)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        for w in ws:
+            w.matmul_device(x.data_ptr(), y.data_ptr(), 1)
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(ws))
+    alg = ws[0].Rows * ws[0].Cols * BYTES[ws[0].Scheme.name] + 4 * (K + N)
+    return ms, alg
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle)
+def cpu_decode_sample(cfg, ctx_len, steps, threads):
+    from oracle import oracle as O
+    schemes = {k: getattr(O, v) for k, v in SCHEMES.items()}
+    t0 = time.time()
+    host = O.make_model(cfg, schemes, seed=1234, threads=threads)
+    build_s = time.time() - t0
+    dec = O.KVDecoder(host, threads=threads)
+    rs = np.random.RandomState(0)
+    dec.kv[:] = rs.standard_normal(dec.kv.size).astype(np.float32)  # synthetic cache of ctx_len positions
+    dec.pos = ctx_len
+    tok = 1
+    dec.step([tok])  # warm
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lg = dec.step([tok])
+        tok = int(np.argmax(lg))
+    dt = time.perf_counter() - t0
+    return steps / dt, dt, build_s
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = max(5, min(args.steps, 30))
+    tps, dt, build_s = cpu_decode_sample(TINYLLAMA, PROMPT, steps, threads)
+    sample = (f"{steps} greedy decode steps of the TinyLlama-shaped Q4_K_M model at context {PROMPT} "
+              f"(synthetic KV cache), C++ restatement of the reference algorithm, {threads} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(tps, 4), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": 1, "ms_per_step": round(1000 * dt / steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "TinyLlama-1.1B-shaped Q4_K_M decode, bs1, ctx 2048", "global_batch": 1,
+                   "seq_len": PROMPT, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------- ours
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import smallmind_b200 as sm
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    cfg = dict(TINYLLAMA)
+    ctx = sm.CudaContext(local)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    torch.cuda.set_stream(stream)
+
+    model, weights = build_gpu_model(sm, ctx, cfg)
+    max_tok = PROMPT + args.warmup + args.steps + 8
+    kv = sm.KVCache(model, 1, max_tok)
+    rs = np.random.RandomState(100 + rank)
+    prompt = rs.randint(0, cfg["vocab_size"], PROMPT).astype(np.int32)
+
+    # prefill (device time of one 2048-token prompt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    t0_tok, _ = kv.prefill(0, prompt, want_logits=False)
+    e1.record(stream)
+    e1.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+
+    seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tok = torch.tensor([t0_tok], dtype=torch.int32, device="cuda")
+    launches0 = ctx.launch_count()
+    for _ in range(args.warmup):
+        kv.decode_device(seq.data_ptr(), tok.data_ptr(), 1, None, tok.data_ptr())
+    stream.synchronize()
+    launches_w = ctx.launch_count()
+
+    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
+                                       else "_work", f"clocks_rank{rank}.csv"))
+    os.makedirs(os.path.dirname(clocks.out_path), exist_ok=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            kv.decode_device(seq.data_ptr(), tok.data_ptr(), 1, None, tok.data_ptr())
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    launches_timed = ctx.launch_count() - launches_w
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms / 1000.0)
+
+    # e2e: host-pointer C-ABI, token in / next token out every step
+    kv2 = sm.KVCache(model, 1, max_tok)
+    nxt, _ = kv2.prefill(0, prompt, want_logits=False)
+    for _ in range(min(3, args.warmup)):
+        t, _ = kv2.decode([0], [nxt], want_logits=False)
+        nxt = int(t[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        t, _ = kv2.decode([0], [nxt], want_logits=False)
+        nxt = int(t[0])
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    kv2.close()
+
+    # roofline: the Q4_K GEMV (gate, 2048 -> 5632) and Q6_K (down) over rotating layer weights
+    hbm, peak_kind = peaks()
+    g_ms, g_bytes = time_gemv(sm, ctx, weights["w_gate"], torch)
+    d_ms, d_bytes = time_gemv(sm, ctx, weights["w_down"], torch)
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_q4k_traffic.json")) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        pass
+
+    # bs64 decode (short context) and per-token bytes
+    bs = 64
+    kv3 = sm.KVCache(model, bs, 64)
+    for s in range(bs):
+        kv3.prefill(s, rs.randint(0, cfg["vocab_size"], 16).astype(np.int32), want_logits=False)
+    seqs = torch.arange(bs, dtype=torch.int32, device="cuda")
+    toks = torch.randint(0, cfg["vocab_size"], (bs,), dtype=torch.int32, device="cuda")
+    for _ in range(2):
+        kv3.decode_device(seqs.data_ptr(), toks.data_ptr(), bs, None, toks.data_ptr())
+    stream.synchronize()
+    e0.record(stream)
+    n64 = 8
+    for _ in range(n64):
+        kv3.decode_device(seqs.data_ptr(), toks.data_ptr(), bs, None, toks.data_ptr())
+    e1.record(stream)
+    e1.synchronize()
+    bs64_tps = bs * n64 / (e0.elapsed_time(e1) / 1000.0)
+    kv3.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        steps = 20
+        tps, dt, _ = cpu_decode_sample(cfg, PROMPT, steps, os.cpu_count() or 1)
+        cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{steps} decode steps at context {PROMPT} (synthetic KV cache), same model shape, "
+                         f"C++ restatement of the reference algorithm"}
+
+    if rank == 0:
+        clk = clocks.summary(local)
+        wbytes = weight_bytes_per_token(cfg)
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, "
+            "random token ids)",
+            "config": {"workload": "TinyLlama-1.1B-shaped Q4_K_M decode, bs1 per GPU, ctx 2048",
+                       "model": "TinyLlama-1.1B-shaped (H2048 L22 32q/4kv FFN5632 V32000)", "global_batch": world,
+                       "seq_len": PROMPT, "parallelism": f"replica x{world} (sequence sharding)",
+                       "l2": "no flush: 667 MB of weights per step > 126 MB L2"},
+            "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "achieved": round(g_bytes / (g_ms * 1e-3) / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(g_bytes / (g_ms * 1e-3) / 1e9 / hbm, 4),
+                         "traffic": traffic, "kernel": "gemv_rows_kernel<Q4_K,1> 2048->5632",
+                         "peak_kind": peak_kind},
+            "gemv": {"q4k_2048x5632_us": round(g_ms * 1000, 2), "q6k_5632x2048_us": round(d_ms * 1000, 2),
+                     "q6k_gbs": round(d_bytes / (d_ms * 1e-3) / 1e9, 1)},
+            "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
+            "bs64_decode_tok_s": round(bs64_tps, 1),
+            "prefill_tok_s": round(PROMPT / (prefill_ms / 1000.0), 1),
+            "gpu_launches": int(launches_timed),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -89,6 +89,7 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
   const int64_t n = (int64_t)rows * cols;
   if ((scheme == SM_Q4_K || scheme == SM_Q6_K) && cols % 256)
     return fail(SM_ERR_SHAPE, "weight_upload: Columns must be divisible by block size (256)");
+  // reference layout: Rows = K is also walked in 256-element blocks (FusedQ4KMatMul.cs:118)
   if ((scheme == SM_Q4_K || scheme == SM_Q6_K) && layout == SM_LAYOUT_REFERENCE && rows % 256)
     return fail(SM_ERR_SHAPE, "weight_upload: reference-layout K-quant needs K (rows) divisible by 256");
   if (nbytes != packed_bytes(scheme, n)) return fail(SM_ERR_SHAPE, "weight_upload: data length does not match shape");

@@ -37,9 +37,13 @@ def main():
             out["scales"] = t.scales
         # reference-literal orientation: B = K x N; K-quant blocks (k/256)*N + n
         if scheme in (O.Q4_K, O.Q6_K):
-            lit = O.reorder_kquant_blocks_to_literal(t)
-            out["literal_data"] = lit.data
-            out["y_literal"] = O.matmul(lit, a, m, cols, rows, mode=0)
+            # the reference's Q4KTensor/Q6KTensor need Cols (= N here) % 256 == 0 too
+            lk, ln = 512, 256
+            tl = O.quantize(O.fill_normal(ln * lk, 2000 + scheme, 0.02), scheme, ln, lk)
+            lit = O.reorder_kquant_blocks_to_literal(tl)
+            a3 = np.random.RandomState(20 + scheme).randn(m, lk).astype(np.float32)
+            out.update(literal_data=lit.data, a_literal=a3, lit_k=lk, lit_n=ln,
+                       y_literal=O.matmul(lit, a3, m, lk, ln, mode=0))
         else:
             # literal B[K][N] with the same bytes read as a K x N tensor (rows=cols_int, cols=rows_int)
             a2 = np.random.RandomState(10 + scheme).randn(m, rows).astype(np.float32)

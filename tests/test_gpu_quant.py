@@ -42,10 +42,11 @@ def test_matmul_golden_both_orientations(ctx, name):
     w.MatMul(a, out, m, cols, rows)
     assert rel_err(out, g["y_intended"]) <= TOL
     if name in ("q4_k", "q6_k"):
-        wl = sm.CudaWeightTensor(ctx, int(g["scheme"]), cols, rows, g["literal_data"], None, bs,
+        lk, ln = int(g["lit_k"]), int(g["lit_n"])
+        wl = sm.CudaWeightTensor(ctx, int(g["scheme"]), lk, ln, g["literal_data"], None, bs,
                                  layout=sm.LAYOUT_REFERENCE)
-        out2 = np.empty((m, rows), np.float32)
-        wl.MatMul(a, out2, m, cols, rows)
+        out2 = np.empty((m, ln), np.float32)
+        wl.MatMul(g["a_literal"], out2, m, lk, ln)
         assert rel_err(out2, g["y_literal"]) <= TOL
     else:
         wl = sm.CudaWeightTensor(ctx, int(g["scheme"]), rows, cols, g["data"], sc, bs, layout=sm.LAYOUT_REFERENCE)
