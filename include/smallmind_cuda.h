@@ -154,6 +154,19 @@ SM_API int sm_attention_decode(sm_ctx* ctx, const float* q, const float* k_cache
                                float* out, const int* lens_dev, int B, int max_ctx, int n_heads, int n_kv,
                                int head_dim);
 
+/* Same computation as sm_attention_decode, for callers that cannot let the
+ * library allocate device memory (hosts that reserve their whole device budget
+ * up front, or run where another allocator owns the device).  No counterpart in
+ * the reference: it has no device memory at all.  Working memory comes from a
+ * fixed 16 MiB static device array held by every GPU that loads the library; sizes
+ * needing more (B * n_heads * (max_ctx + 66 * ceil(max_ctx/64)) floats) return
+ * SM_ERR_SHAPE.  The first call on a device looks up the array's address and
+ * should come before any stream capture.  Calls share the array: calls that
+ * overlap on the GPU race and must be serialised.  Device pointers only. */
+SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
+                                       float* out, const int* lens_dev, int B, int max_ctx, int n_heads, int n_kv,
+                                       int head_dim);
+
 /* ---------------------------------------------------------------- model */
 /* ModelConfig fields used by the LLaMA path (ModelConfig.cs:14-136). */
 typedef struct sm_model_config {

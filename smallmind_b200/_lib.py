@@ -56,6 +56,7 @@ SIGNATURES = {
     "sm_op_silu_mul": (i, [vp, vp, vp, vp, i, i]),
     "sm_attention": (i, [vp, vp, vp, vp, vp, i, i, i, i, i, i]),
     "sm_attention_decode": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, i]),
+    "sm_attention_decode_noalloc": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, i]),
     "sm_model_create": (i, [vp, C.POINTER(ModelConfig), PP]),
     "sm_model_set_weight": (i, [vp, i, i, vp]),
     "sm_model_set_vector": (i, [vp, i, i, vp, sz]),

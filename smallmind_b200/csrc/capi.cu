@@ -34,6 +34,17 @@ struct sm_weight {
   DevWeight w;
 };
 
+namespace sm {
+// Read-only view of a context for entry points defined in other files.
+int ctx_view(sm_ctx* ctx, int* device, cudaStream_t* stream, int64_t** launches) {
+  if (!ctx) return fail(SM_ERR_INVALID_ARG, "null ctx");
+  *device = ctx->device;
+  *stream = ctx->stream;
+  *launches = &ctx->launches;
+  return SM_OK;
+}
+}  // namespace sm
+
 namespace {
 
 struct DeviceGuard {

@@ -105,6 +105,9 @@ struct LaunchCounter {
   }
 };
 
+// capi.cu: device, stream and launch counter of a context
+int ctx_view(sm_ctx* ctx, int* device, cudaStream_t* stream, int64_t** launches);
+
 // ---------------------------------------------------------------- kernel entry points (host wrappers)
 // quant.cu
 int launch_dequant(const DevWeight& w, float* out, cudaStream_t st);
