@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemv1.cuh"
 
 // ---------------------------------------------------------------- errors
 namespace sm {
@@ -603,6 +604,97 @@ __global__ void decode_commit_kernel(const int* __restrict__ seq, int* __restric
   if (kv_len[s] < max_tokens) kv_len[s] += 1;
 }
 
+// One-row step (bs1 decode): fused launches built on the M = 1 GEMV.  Per layer:
+// [RMSNorm + Q|K|V] -> RoPE + KV append -> attention -> [O-proj + residual]
+// -> [RMSNorm + gate/up + SiLU-gate] -> [down-proj + residual].
+bool m1_supported(const sm_model* m) {
+  const auto& c = m->cfg;
+  for (const auto& L : m->layers) {
+    for (int r : {SM_ROLE_WQ, SM_ROLE_WK, SM_ROLE_WV, SM_ROLE_W_GATE, SM_ROLE_W_UP})
+      if (!gemv1_supports(*L.w[r], c.hidden)) return false;
+    if (!gemv1_supports(*L.w[SM_ROLE_WO], m->qd()) || !gemv1_supports(*L.w[SM_ROLE_W_DOWN], c.ffn_hidden))
+      return false;
+  }
+  return gemv1_supports(*m->output, c.hidden);
+}
+
+int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
+  const auto& c = m->cfg;
+  Work& w = m->work;
+  cudaStream_t st = m->ctx->stream;
+  const int H = c.hidden, qd = m->qd(), kd = m->kd(), QS = m->qkv_stride();
+  const int hd = c.head_dim, mt = kv->max_tokens;
+  const int64_t head_stride = (int64_t)mt * hd;
+  const int64_t seq_stride = head_stride * c.n_kv_heads;
+  if (!prefill_head_only) {
+    SM_TRY(launch_embed(m->embd, w.tok(), w.x, 1, H, st));
+    ++nl;
+    for (int l = 0; l < c.n_layers; ++l) {
+      const sm_model::Layer& L = m->layers[l];
+      float* kc = kv->k + kv->layer_stride() * l;
+      float* vc = kv->v + kv->layer_stride() * l;
+      GemvArgs qkv;
+      qkv.K = H;
+      qkv.x = w.x;
+      qkv.gamma = L.attn_norm;
+      qkv.eps = c.norm_eps;
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WQ], nullptr, w.qkv, GEMV_STORE));
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WK], nullptr, w.qkv + qd, GEMV_STORE));
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WV], nullptr, w.qkv + qd + kd, GEMV_STORE));
+      SM_TRY(launch_gemv1(qkv, st, &nl));
+      SM_TRY(launch_rope_qk_append(w.qkv, 1, QS, c.n_heads, c.n_kv_heads, hd, w.pos(), w.seq(), m->sin_t, m->cos_t,
+                                   kc, vc, mt, st));
+      ++nl;
+      SM_TRY(launch_attention_decode(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd, w.lens(),
+                                     w.seq(), 1, c.n_heads, c.n_kv_heads, hd, w.attn_scratch, w.attn_scratch_floats,
+                                     st, &nl));
+      GemvArgs o;
+      o.K = qd;
+      o.x = w.att;
+      SM_TRY(gemv1_segment(o, *L.w[SM_ROLE_WO], nullptr, w.x, GEMV_ADD));
+      SM_TRY(launch_gemv1(o, st, &nl));
+      GemvArgs gu;
+      gu.K = H;
+      gu.x = w.x;
+      gu.gamma = L.ffn_norm;
+      gu.eps = c.norm_eps;
+      if (L.w[SM_ROLE_W_GATE]->scheme == L.w[SM_ROLE_W_UP]->scheme) {
+        SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_GATE], L.w[SM_ROLE_W_UP], w.g, GEMV_GLU));
+        SM_TRY(launch_gemv1(gu, st, &nl));
+      } else {
+        SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_GATE], nullptr, w.g, GEMV_STORE));
+        SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_UP], nullptr, w.u, GEMV_STORE));
+        SM_TRY(launch_gemv1(gu, st, &nl));
+        SM_TRY(launch_silu_mul(w.g, w.u, w.g, c.ffn_hidden, st));
+        ++nl;
+      }
+      GemvArgs dn;
+      dn.K = c.ffn_hidden;
+      dn.x = w.g;
+      SM_TRY(gemv1_segment(dn, *L.w[SM_ROLE_W_DOWN], nullptr, w.x, GEMV_ADD));
+      SM_TRY(launch_gemv1(dn, st, &nl));
+    }
+  }
+  return SM_OK;
+}
+
+// LM head of one row x_row: RMSNorm fused into the GEMV, then argmax.
+int head_m1(sm_model* m, const float* x_row, int& nl) {
+  const auto& c = m->cfg;
+  Work& w = m->work;
+  cudaStream_t st = m->ctx->stream;
+  GemvArgs hd;
+  hd.K = c.hidden;
+  hd.x = x_row;
+  hd.gamma = m->out_norm;
+  hd.eps = c.norm_eps;
+  SM_TRY(gemv1_segment(hd, *m->output, nullptr, w.logits, GEMV_STORE));
+  SM_TRY(launch_gemv1(hd, st, &nl));
+  SM_TRY(launch_argmax(w.logits, 1, c.vocab_size, w.amax(), st));
+  ++nl;
+  return SM_OK;
+}
+
 // The transformer stack over `rows` token rows whose tok/seq/pos/lens are in
 // work.ints.  prefill: all rows belong to one sequence (prefill_seq) at
 // positions pos0..pos0+rows-1; otherwise one row per sequence (decode).
@@ -610,6 +702,11 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
   const auto& c = m->cfg;
   Work& w = m->work;
   cudaStream_t st = m->ctx->stream;
+  const bool m1 = m1_supported(m);
+  if (m1 && rows == 1 && !prefill) {
+    SM_TRY(forward_m1(m, kv, false, nl));
+    return head_m1(m, w.x, nl);
+  }
   const int H = c.hidden, F = c.ffn_hidden, qd = m->qd(), kd = m->kd(), QS = m->qkv_stride();
   const int hd = c.head_dim, mt = kv->max_tokens;
   SM_TRY(launch_embed(m->embd, w.tok(), w.x, rows, H, st));
@@ -651,6 +748,7 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
   // final norm + LM head: last row only for prefill (what the loop reads), every row for decode
   const int first = prefill ? rows - 1 : 0;
   const int nrows = prefill ? 1 : rows;
+  if (m1 && nrows == 1) return head_m1(m, w.x + (size_t)first * H, nl);
   SM_TRY(launch_rmsnorm(w.x + (size_t)first * H, m->out_norm, w.h, nrows, H, c.norm_eps, st));
   ++nl;
   SM_TRY(launch_matmul(*m->output, w.h, w.logits, nrows, c.vocab_size, 0, st, &nl));

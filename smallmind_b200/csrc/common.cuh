@@ -31,8 +31,9 @@ int fail(int code, const std::string& msg);
 // ---------------------------------------------------------------- device weight
 // Device layout of a packed weight.  Q8_0/Q4_0/Q4_K keep the reference bytes
 // as uploaded.  Q6_K blocks (210 B, only 2-byte aligned) are re-laid for
-// 128-bit loads: a 208 B body per block [ql 128 | qh 64 | int8 scales 16] in
-// `data`, and the fp16 super-scale d of every block in `aux` (same block order).
+// 128-bit loads: a 208 B body per block [ql 128 | qh' 64 | int8 scales 16] in
+// `data` (qh' is the high-bit plane re-packed, see q6k_relayout_kernel), and
+// the fp16 super-scale d of every block in `aux` (same block order).
 struct DevWeight {
   int scheme = 0;
   int layout = 0;

@@ -12,6 +12,7 @@
 // are written in (MatMulF32Q8.cs:61-79, FusedQ4KMatMul.cs:122,127).  Kept for
 // op-level parity; one thread per output column.
 #include "common.cuh"
+#include "gemv1.cuh"
 
 namespace sm {
 namespace {
@@ -119,7 +120,8 @@ struct Decoder<SM_Q6_K> {
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       const int low4 = (lq[e >> 3] >> (4 * (e & 7))) & 0xF;
-      const int high2 = (hq[e >> 4] >> (2 * (e & 15))) & 3;
+      const int ee = e & 15;  // re-packed high plane (q6k_relayout_kernel)
+      const int high2 = (hq[e >> 4] >> (8 * ((ee & 7) >> 1) + ((ee >> 3) << 2) + ((ee & 1) << 1))) & 3;
       const int q = low4 | (high2 << 4);
       o.w[e] = __fmul_rn(e < 16 ? s0 : s1, (float)(q - 32));
     }
@@ -303,6 +305,13 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     SM_CUDA_TRY(cudaGetLastError());
     if (n_launch) ++*n_launch;
     return SM_OK;
+  }
+  if (M == 1 && gemv1_supports(W, K)) {
+    GemvArgs a;
+    a.K = K;
+    a.x = x;
+    SM_TRY(gemv1_segment(a, W, nullptr, y, accumulate ? GEMV_ADD : GEMV_STORE));
+    return launch_gemv1(a, st, n_launch);
   }
   const bool fast = kq || (K % 32 == 0 && (W.scheme == SM_F32 || W.block_size % 32 == 0));
   if (!fast) {

@@ -1,0 +1,32 @@
+// Launch interface of the M = 1 decode GEMV (gemv1.cu).
+#pragma once
+#include "common.cuh"
+
+namespace sm {
+
+constexpr int GEMV_MAX_SEG = 4;
+enum { GEMV_STORE = 0, GEMV_ADD = 1, GEMV_GLU = 2 };
+
+struct GemvSeg {
+  int fmt = 0, rows = 0, bs = 0, mode = 0;
+  const uint8_t* data = nullptr;
+  const void* aux = nullptr;
+  const uint8_t* data2 = nullptr;  // GLU: the up-projection weight (same scheme and shape)
+  const void* aux2 = nullptr;
+  float* y = nullptr;
+  int group_begin = 0;
+};
+
+struct GemvArgs {
+  GemvSeg seg[GEMV_MAX_SEG];
+  int nseg = 0, ngroups = 0, K = 0;
+  const float* x = nullptr;
+  const float* gamma = nullptr;  // non-null: RMSNorm x first (eps below)
+  float eps = 1e-5f;
+};
+
+bool gemv1_supports(const DevWeight& w, int K);
+int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y, int mode);
+int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch);
+
+}  // namespace sm

@@ -44,7 +44,15 @@ __global__ void dequant_q4k_kernel(const uint8_t* __restrict__ src, int64_t nblo
   }
 }
 
-// Q6KTensor.cs:80-125 on the device layout (208 B body + separate d).
+// Q6KTensor.cs:80-125 on the device layout (208 B body + separate d; the high
+// 2-bit plane is re-packed, see q6k_relayout_kernel).
+__device__ __forceinline__ int q6k_high2(const uint8_t* qhp, int v) {
+  const int t = v >> 4, e = v & 15;
+  const int b = (e & 7) >> 1;
+  const int shift = ((e >> 3) << 2) + ((e & 1) << 1);
+  return (qhp[4 * t + b] >> shift) & 3;
+}
+
 __global__ void dequant_q6k_kernel(const uint8_t* __restrict__ body, const uint16_t* __restrict__ dv, int64_t nblocks,
                                    float* __restrict__ out) {
   const int v = threadIdx.x;  // 256 threads, one per element
@@ -55,8 +63,7 @@ __global__ void dequant_q6k_kernel(const uint8_t* __restrict__ body, const uint1
     const float s = __fmul_rn(d, (float)scale);
     const uint8_t qlb = blk[v >> 1];
     const int low4 = (v & 1) ? (qlb >> 4) : (qlb & 0xF);
-    const int high2 = (blk[128 + (v >> 2)] >> ((v & 3) * 2)) & 3;
-    const int q = low4 | (high2 << 4);
+    const int q = low4 | (q6k_high2(blk + 128, v) << 4);
     out[b * 256 + v] = __fmul_rn(s, (float)(q - 32));
   }
 }
@@ -66,13 +73,28 @@ __global__ void dequant_f32_kernel(const float* __restrict__ w, int64_t n, float
     out[i] = w[i];
 }
 
-// Q6_K reference block (210 B) -> device body (208 B) + d.
+// Q6_K reference block (210 B) -> device body (208 B) + d.  The body keeps ql
+// (128 B) and the int8 scales (16 B, at 192) as they are; the high-bit plane is
+// re-packed so that one 32-bit word covers 16 consecutive elements 16t..16t+15
+// and byte b of it holds the 2-bit highs of elements 16t+2b, 16t+2b+1,
+// 16t+8+2b, 16t+9+2b (bits 0-1, 2-3, 4-5, 6-7).  Byte b then lines up with
+// byte b of the matching ql words, so the GEMV builds four 6-bit values with a
+// few shifts and masks per 32-bit word.
 __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ body,
                                     uint16_t* __restrict__ dv, int64_t nblocks) {
   for (int64_t b = blockIdx.x; b < nblocks; b += gridDim.x) {
     const uint8_t* s = src + b * Q6K_BLOCK_BYTES;
     uint8_t* o = body + b * Q6K_BODY_BYTES;
-    for (int i = threadIdx.x; i < Q6K_BODY_BYTES; i += blockDim.x) o[i] = s[i];
+    for (int i = threadIdx.x; i < Q6K_BODY_BYTES; i += blockDim.x) {
+      if (i < 128 || i >= 192) {
+        o[i] = s[i];
+      } else {
+        const int idx = i - 128, t = idx >> 2, bb = idx & 3;
+        auto h = [&](int v) { return (s[128 + (v >> 2)] >> (2 * (v & 3))) & 3; };
+        const int v0 = 16 * t + 2 * bb;
+        o[i] = (uint8_t)(h(v0) | (h(v0 + 1) << 2) | (h(v0 + 8) << 4) | (h(v0 + 9) << 6));
+      }
+    }
     if (threadIdx.x == 0) dv[b] = (uint16_t)s[208] | ((uint16_t)s[209] << 8);
   }
 }
