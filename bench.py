@@ -244,10 +244,10 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
 
     model, weights = build_gpu_model(sm, ctx, cfg)
-    max_tok = PROMPT + args.warmup + args.steps + 8
+    max_tok = args.prompt + args.warmup + args.steps + 8
     kv = sm.KVCache(model, 1, max_tok)
     rs = np.random.RandomState(100 + rank)
-    prompt = rs.randint(0, cfg["vocab_size"], PROMPT).astype(np.int32)
+    prompt = rs.randint(0, cfg["vocab_size"], args.prompt).astype(np.int32)
 
     # prefill (device time of one 2048-token prompt)
     torch.cuda.synchronize()
@@ -289,6 +289,13 @@ def run_ours(args):
         ms = float(t.item())
     ms_per_step = ms / args.steps
     value = world * args.steps / (ms / 1000.0)
+    if args.decode_only:
+        if rank == 0:
+            print(json.dumps({"decode_only": True, "value": round(value, 2), "ms_per_step": round(ms_per_step, 4),
+                              "prompt": args.prompt, "gpu_launches": int(launches_timed)}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     # e2e: host-pointer C-ABI, token in / next token out every step
     kv2 = sm.KVCache(model, 1, max_tok)
@@ -370,7 +377,7 @@ def run_ours(args):
                      "q6k_gbs": round(d_bytes / (d_ms * 1e-3) / 1e9, 1)},
             "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
             "bs64_decode_tok_s": round(bs64_tps, 1),
-            "prefill_tok_s": round(PROMPT / (prefill_ms / 1000.0), 1),
+            "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
             "gpu_launches": int(launches_timed),
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -387,6 +394,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="time only the device decode loop (profiling runs: no e2e, GEMV, bs64 or CPU legs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -8,6 +8,8 @@
 // + combine; prefill = a max pass and an exp/PV pass over key tiles.
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace sm {
@@ -298,6 +300,157 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(
   }
 }
 
+// ---------------------------------------------------------------- decode, one launch
+// A thread-block cluster of CL CTAs per (sequence, kv head).  Each CTA scores
+// its slice of the context for the G query heads of the group (scores stay in
+// shared memory), the CTAs exchange their slice maxima through distributed
+// shared memory so every CTA exponentiates against the exact global row max
+// (the Pade exp of the reference is not multiplicative), and the partial sums
+// and e.V accumulators are reduced into CTA rank 0 the same way.  No global
+// scratch, one launch.
+constexpr int CL = 16;          // CTAs per cluster (non-portable size)
+constexpr int CT = 256;         // threads per CTA
+constexpr int CMAXG = 8;        // q heads per kv head
+
+template <int HD>
+__global__ void __launch_bounds__(CT) decode_cluster_kernel(
+    const float* __restrict__ q, int q_stride, const float* __restrict__ kc, const float* __restrict__ vc,
+    int64_t seq_stride, int64_t row_stride, int64_t head_stride, const int* __restrict__ lens,
+    const int* __restrict__ seq_map, int nH, int nKv, float scale, float* __restrict__ out, int out_stride,
+    int chunk_cap) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int g = blockIdx.y, b = blockIdx.z;
+  const int G = nH / nKv;
+  extern __shared__ float sm_[];
+  float* qs = sm_;                        // [CMAXG][HD]
+  float* sc = qs + CMAXG * HD;            // [CMAXG][chunk_cap]
+  float* pacc = sc + CMAXG * chunk_cap;   // [CMAXG][HD]  this CTA's e.V
+  float* stat = pacc + CMAXG * HD;        // [CMAXG] slice max, [CMAXG] slice sum
+  float* part = stat + 2 * CMAXG;         // [CT/HD][CMAXG][HD]
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int len = lens[b];
+  const int per = (len + CL - 1) / CL;
+  const int j0 = min(len, rank * per), j1 = min(len, j0 + per);
+  const int n = j1 - j0;
+  for (int t = threadIdx.x; t < G * HD; t += CT) {
+    const int h = t / HD, d = t - h * HD;
+    qs[h * HD + d] = q[(int64_t)b * q_stride + (g * G + h) * HD + d];
+  }
+  __syncthreads();
+  const int64_t sbase = (int64_t)(seq_map ? seq_map[b] : b) * seq_stride + (int64_t)g * head_stride;
+  const float* kb = kc + sbase;
+  const float* vb = vc + sbase;
+  // scores: 8 lanes per key (8 dims each), 32 keys per pass
+  const int sub = threadIdx.x & 7, slot = threadIdx.x >> 3;
+  constexpr int DPL = HD / 8;
+  float lmax[CMAXG];
+#pragma unroll
+  for (int h = 0; h < CMAXG; ++h) lmax[h] = -FLT_MAX;
+  const int passes = (n + 31) / 32;
+  for (int p = 0; p < passes; ++p) {
+    const int jj = p * 32 + slot;
+    const bool valid = jj < n;
+    float kv[DPL];
+    if (valid) {
+      const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * row_stride + sub * DPL);
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) {
+        const float4 t = __ldg(kp + i);
+        kv[4 * i] = t.x; kv[4 * i + 1] = t.y; kv[4 * i + 2] = t.z; kv[4 * i + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) kv[i] = 0.f;
+    }
+#pragma unroll
+    for (int h = 0; h < CMAXG; ++h) {
+      if (h >= G) break;
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) s = fmaf(qs[h * HD + sub * DPL + i], kv[i], s);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (valid) {
+        if (sub == 0) sc[h * chunk_cap + jj] = s;
+        lmax[h] = fmaxf(lmax[h], __fmul_rn(s, scale));
+      }
+    }
+  }
+  // slice max per head
+  {
+    float* wred = part;  // reuse [CT/32][CMAXG]
+#pragma unroll
+    for (int h = 0; h < CMAXG; ++h) {
+      const float m = warp_max(lmax[h]);
+      if ((threadIdx.x & 31) == 0) wred[(threadIdx.x >> 5) * CMAXG + h] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x < CMAXG) {
+      float m = -FLT_MAX;
+      for (int w = 0; w < CT / 32; ++w) m = fmaxf(m, wred[w * CMAXG + threadIdx.x]);
+      stat[threadIdx.x] = m;
+    }
+  }
+  cluster.sync();
+  // global max of each head from every CTA's slice max (distributed shared memory)
+  __shared__ float gmax[CMAXG];
+  if (threadIdx.x < G) {
+    float m = -FLT_MAX;
+    for (int r = 0; r < CL; ++r) m = fmaxf(m, cluster.map_shared_rank(stat, r)[threadIdx.x]);
+    gmax[threadIdx.x] = m;
+  }
+  __syncthreads();
+  // e = FastExp(s*scale - max) in place, then e.V
+  for (int t = threadIdx.x; t < G * n; t += CT) {
+    const int h = t / n, jj = t - h * n;
+    sc[h * chunk_cap + jj] = pade_exp(__fsub_rn(__fmul_rn(sc[h * chunk_cap + jj], scale), gmax[h]));
+  }
+  __syncthreads();
+  constexpr int PH = CT / HD;
+  const int d = threadIdx.x % HD, ph = threadIdx.x / HD;
+  float acc[CMAXG];
+#pragma unroll
+  for (int h = 0; h < CMAXG; ++h) acc[h] = 0.f;
+  for (int jj = ph; jj < n; jj += PH) {
+    const float v = __ldg(vb + (int64_t)(j0 + jj) * row_stride + d);
+#pragma unroll
+    for (int h = 0; h < CMAXG; ++h)
+      if (h < G) acc[h] = fmaf(sc[h * chunk_cap + jj], v, acc[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < CMAXG; ++h)
+    if (h < G) part[(ph * CMAXG + h) * HD + d] = acc[h];
+  __syncthreads();
+  for (int t = threadIdx.x; t < G * HD; t += CT) {
+    const int h = t / HD, dd = t - h * HD;
+    float s = 0.f;
+    for (int p = 0; p < PH; ++p) s += part[(p * CMAXG + h) * HD + dd];
+    pacc[h * HD + dd] = s;
+  }
+  if (threadIdx.x < G) {
+    float s = 0.f;
+    for (int jj = 0; jj < n; ++jj) s += sc[threadIdx.x * chunk_cap + jj];
+    stat[CMAXG + threadIdx.x] = s;
+  }
+  cluster.sync();
+  // rank 0 reduces the slices and writes out = (sum e.V) / (sum e)
+  if (rank == 0) {
+    for (int t = threadIdx.x; t < G * HD; t += CT) {
+      const int h = t / HD, dd = t - h * HD;
+      float s = 0.f, tot = 0.f;
+      for (int r = 0; r < CL; ++r) {
+        s += cluster.map_shared_rank(pacc, r)[h * HD + dd];
+        tot += cluster.map_shared_rank(stat, r)[CMAXG + h];
+      }
+      out[(int64_t)b * out_stride + (g * G + h) * HD + dd] = s * __fdiv_rn(1.f, tot);
+    }
+  }
+  cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+}
+
 }  // namespace
 
 size_t attention_decode_scratch_floats(int B, int nH, int max_ctx) {
@@ -328,6 +481,70 @@ int launch_attention_decode(const float* q, int q_stride, const float* kc, const
   SM_CUDA_TRY(cudaGetLastError());
   if (n_launch) *n_launch += 3;
   return SM_OK;
+}
+
+// Single-launch cluster variant (no scratch).  Returns SM_ERR_UNSUPPORTED when
+// the shape does not fit it (caller falls back to launch_attention_decode).
+int launch_attention_decode_cluster(const float* q, int q_stride, const float* kc, const float* vc,
+                                    int64_t seq_stride, int64_t row_stride, int64_t head_stride, int max_ctx,
+                                    float* out, int out_stride, const int* lens, const int* seq_map, int B, int nH,
+                                    int nKv, int hd, cudaStream_t st, int* n_launch) {
+  if (hd != 64 || nH % nKv) return SM_ERR_UNSUPPORTED;
+  if (nH / nKv <= CMAXG) {
+    const int chunk_cap = (max_ctx + CL - 1) / CL;
+    const size_t smem = sizeof(float) * (CMAXG * 64 * 2 + CMAXG * (size_t)chunk_cap + 2 * CMAXG + (CT / 64) * CMAXG * 64);
+    if (smem <= 200 * 1024) {
+      auto kern = decode_cluster_kernel<64>;
+      static bool attr_set[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      static int cluster_ok[64] = {};  // 0 unknown, 1 usable, -1 not schedulable on this device
+      if (dev < 64 && !attr_set[dev]) {
+        SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set[dev] = true;
+      }
+      if (dev >= 64) return SM_ERR_UNSUPPORTED;
+      if (cluster_ok[dev] == 0) {
+        cudaLaunchConfig_t probe = {};
+        probe.gridDim = dim3(CL, 1, 1);
+        probe.blockDim = dim3(CT);
+        probe.dynamicSmemBytes = 200 * 1024 / 4;
+        cudaLaunchAttribute pa[1];
+        pa[0].id = cudaLaunchAttributeClusterDimension;
+        pa[0].val.clusterDim.x = CL;
+        pa[0].val.clusterDim.y = 1;
+        pa[0].val.clusterDim.z = 1;
+        probe.attrs = pa;
+        probe.numAttrs = 1;
+        int nclusters = 0;
+        cudaError_t oe = cudaOccupancyMaxActiveClusters(&nclusters, (void*)kern, &probe);
+        cluster_ok[dev] = (oe == cudaSuccess && nclusters > 0) ? 1 : -1;
+        if (oe != cudaSuccess) cudaGetLastError();
+      }
+      if (cluster_ok[dev] < 0 || smem > 200 * 1024 / 4) return SM_ERR_UNSUPPORTED;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(CL, nKv, B);
+      cfg.blockDim = dim3(CT);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = CL;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      const float scale = 1.0f / sqrtf((float)hd);
+      SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, q_stride, kc, vc, seq_stride, row_stride, head_stride, lens,
+                                     seq_map, nH, nKv, scale, out, out_stride, chunk_cap));
+      if (n_launch) *n_launch += 1;
+      return SM_OK;
+    }
+  }
+  return SM_ERR_UNSUPPORTED;
 }
 
 int launch_attention_prefill(const float* q, int q_stride, const float* k, const float* v, int64_t row_stride,

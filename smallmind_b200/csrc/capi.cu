@@ -475,10 +475,17 @@ SM_API int sm_attention_decode(sm_ctx* ctx, const float* q, const float* kc, con
   if (B <= 0 || max_ctx <= 0 || nH % nKv) return fail(SM_ERR_SHAPE, "attention_decode: bad shape");
   DeviceGuard g(ctx->device);
   cudaStream_t st = ctx->stream;
+  int nl = 0;
+  const int64_t hstride = (int64_t)max_ctx * hd;
+  int crc = launch_attention_decode_cluster(q, nH * hd, kc, vc, hstride * nKv, hd, hstride, max_ctx, out, nH * hd,
+                                            lens_dev, nullptr, B, nH, nKv, hd, st, &nl);
+  if (crc != SM_ERR_UNSUPPORTED) {
+    ctx->launches += nl;
+    return crc;
+  }
   const size_t sf = attention_decode_scratch_floats(B, nH, max_ctx);
   TempBuf scratch;
   SM_TRY(scratch.alloc(sf * sizeof(float), st));
-  int nl = 0;
   const int64_t head_stride = (int64_t)max_ctx * hd;
   int rc = launch_attention_decode(q, nH * hd, kc, vc, head_stride * nKv, hd, head_stride, max_ctx, out, nH * hd,
                                    lens_dev, nullptr, B, nH, nKv, hd, (float*)scratch.p, sf, st, &nl);
@@ -638,16 +645,25 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       qkv.x = w.x;
       qkv.gamma = L.attn_norm;
       qkv.eps = c.norm_eps;
-      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WQ], nullptr, w.qkv, GEMV_STORE));
-      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WK], nullptr, w.qkv + qd, GEMV_STORE));
-      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WV], nullptr, w.qkv + qd + kd, GEMV_STORE));
+      // RoPE and the KV-cache append are fused into the Q|K|V epilogue
+      qkv.pos = w.pos();
+      qkv.seq = w.seq();
+      qkv.sin_t = m->sin_t;
+      qkv.cos_t = m->cos_t;
+      qkv.head_dim = hd;
+      qkv.n_kv = c.n_kv_heads;
+      qkv.max_ctx = mt;
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WQ], nullptr, w.qkv, GEMV_ROPE_Q));
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WK], nullptr, kc, GEMV_ROPE_K_CACHE));
+      SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WV], nullptr, vc, GEMV_V_CACHE));
       SM_TRY(launch_gemv1(qkv, st, &nl));
-      SM_TRY(launch_rope_qk_append(w.qkv, 1, QS, c.n_heads, c.n_kv_heads, hd, w.pos(), w.seq(), m->sin_t, m->cos_t,
-                                   kc, vc, mt, st));
-      ++nl;
-      SM_TRY(launch_attention_decode(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd, w.lens(),
-                                     w.seq(), 1, c.n_heads, c.n_kv_heads, hd, w.attn_scratch, w.attn_scratch_floats,
-                                     st, &nl));
+      int arc = launch_attention_decode_cluster(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd,
+                                                w.lens(), w.seq(), 1, c.n_heads, c.n_kv_heads, hd, st, &nl);
+      if (arc == SM_ERR_UNSUPPORTED)
+        arc = launch_attention_decode(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd, w.lens(),
+                                      w.seq(), 1, c.n_heads, c.n_kv_heads, hd, w.attn_scratch, w.attn_scratch_floats,
+                                      st, &nl);
+      SM_TRY(arc);
       GemvArgs o;
       o.K = qd;
       o.x = w.att;
@@ -731,9 +747,13 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
                                       head_stride, w.att, qd, rows, pos0 + rows, c.n_heads, c.n_kv_heads, hd, st,
                                       &nl));
     } else {
-      SM_TRY(launch_attention_decode(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd, w.lens(),
-                                     w.seq(), rows, c.n_heads, c.n_kv_heads, hd, w.attn_scratch,
-                                     w.attn_scratch_floats, st, &nl));
+      int arc = launch_attention_decode_cluster(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd,
+                                                w.lens(), w.seq(), rows, c.n_heads, c.n_kv_heads, hd, st, &nl);
+      if (arc == SM_ERR_UNSUPPORTED)
+        arc = launch_attention_decode(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd, w.lens(),
+                                      w.seq(), rows, c.n_heads, c.n_kv_heads, hd, w.attn_scratch,
+                                      w.attn_scratch_floats, st, &nl);
+      SM_TRY(arc);
     }
     // o-proj with the residual add fused in its epilogue (TransformerBlock.cs:170)
     SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.x, rows, H, 1, st, &nl));

@@ -133,6 +133,10 @@ int launch_attention_decode(const float* q, int q_stride, const float* kc, const
                             const int* lens, const int* seq_map, int B, int nH, int nKv, int hd, float* scratch,
                             size_t scratch_floats, cudaStream_t st, int* n_launch);
 size_t attention_decode_scratch_floats(int B, int nH, int max_ctx);
+int launch_attention_decode_cluster(const float* q, int q_stride, const float* kc, const float* vc,
+                                    int64_t seq_stride, int64_t row_stride, int64_t head_stride, int max_ctx,
+                                    float* out, int out_stride, const int* lens, const int* seq_map, int B, int nH,
+                                    int nKv, int hd, cudaStream_t st, int* n_launch);
 int launch_rope_qk_append(float* qkv, int rows, int qkv_stride, int nH, int nKv, int hd, const int* positions,
                           const int* seq_ids, const float* sin_t, const float* cos_t, float* kc, float* vc,
                           int max_ctx, cudaStream_t st);

@@ -184,27 +184,32 @@ struct Unit<SM_Q4_0> {
   }
 };
 
-// One warp, four weight rows (GLU: two output rows = two gate rows + two up rows).
-template <int FMT>
-__device__ __forceinline__ void group_rows(const GemvArgs& a, const GemvSeg& s, int lg, const float* xs,
-                                           const float* x16, int lane) {
+// Rows of group lg handled by this segment (GLU: R/2 gate rows then the same R/2 up rows).
+template <int R>
+__device__ __forceinline__ int group_row(const GemvSeg& s, int lg, int r) {
+  return s.mode == GEMV_GLU ? lg * (R / 2) + (r % (R / 2)) : lg * R + r;
+}
+
+// Partial dot products of R rows over this warp's share of K (units sub, sub+S, ...).
+template <int FMT, int R>
+__device__ __forceinline__ void group_partial(const GemvArgs& a, const GemvSeg& s, int lg, const float* xs,
+                                              const float* x16, int lane, int sub, float* acc) {
   const int K = a.K, units = K >> 5;
   const int j = lane & 7;
   const bool glu = s.mode == GEMV_GLU;
-  int rows[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) rows[r] = glu ? lg * 2 + (r & 1) : lg * 4 + r;
-  GemvSeg up = s;  // GLU rows 2, 3 read the up-projection weight
+  GemvSeg up = s;  // GLU rows R/2.. read the up-projection weight
   if (glu) {
     up.data = s.data2;
     up.aux = s.aux2;
   }
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int u = lane; u < units; u += 32) {
-    typename Unit<FMT>::Raw raw[4];
+  int rows[R];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      if (rows[r] < s.rows) Unit<FMT>::load(r >= 2 ? up : s, rows[r], u, K, raw[r]);
+  for (int r = 0; r < R; ++r) rows[r] = group_row<R>(s, lg, r);
+  for (int u = sub * 32 + lane; u < units; u += 32 * a.S) {
+    typename Unit<FMT>::Raw raw[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (rows[r] < s.rows) Unit<FMT>::load((glu && r >= R / 2) ? up : s, rows[r], u, K, raw[r]);
     float xr[32];
     const float* xp = xs + 32 * u;
 #pragma unroll
@@ -214,29 +219,64 @@ __device__ __forceinline__ void group_rows(const GemvArgs& a, const GemvSeg& s, 
     }
     const float xa = x16[2 * u], xb = x16[2 * u + 1];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < R; ++r)
       if (rows[r] < s.rows) acc[r] += Unit<FMT>::dot(raw[r], j, xr, xa, xb);
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) acc[r] = warp_sum(acc[r]);
-  if (lane < 4) {
-    if (glu) {
-      if (lane < 2 && rows[lane] < s.rows) {
-        const float g = lane == 0 ? acc[0] : acc[1];
-        const float uu = lane == 0 ? acc[2] : acc[3];
-        const float c = fmaxf(-20.f, fminf(g, 20.f));
-        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));
-        s.y[rows[lane]] = __fmul_rn(__fmul_rn(g, sig), uu);
-      }
-    } else if (rows[lane] < s.rows) {
-      const float v = acc[lane];
-      float* dst = s.y + rows[lane];
-      *dst = s.mode == GEMV_ADD ? *dst + v : v;
-    }
   }
 }
 
-__device__ __forceinline__ void prefetch_rows(const GemvArgs& a, const GemvSeg& s, int lg, int lane) {
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, const GemvArgs& a, int pos, int d) {
+  // RotaryEmbedding.cs:103-116 on the pair (d, d+1), d even
+  const int half = a.head_dim / 2, i = d / 2;
+  const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
+  const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+  x0 = y0;
+  x1 = y1;
+}
+
+// Epilogue of one group, final row values v[0..R-1].
+template <int R>
+__device__ __forceinline__ void group_store(const GemvArgs& a, const GemvSeg& s, int lg, float* v) {
+  if (s.mode == GEMV_GLU) {
+#pragma unroll
+    for (int r = 0; r < R / 2; ++r) {
+      const int row = group_row<R>(s, lg, r);
+      if (row >= s.rows) continue;
+      const float g = v[r], u = v[r + R / 2];
+      const float c = fmaxf(-20.f, fminf(g, 20.f));
+      const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));  // ActivationOps.cs:304-309
+      s.y[row] = __fmul_rn(__fmul_rn(g, sig), u);
+    }
+    return;
+  }
+  const int row0 = group_row<R>(s, lg, 0);
+  if (s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE) {
+    const int pos = *a.pos;
+#pragma unroll
+    for (int r = 0; r < R; r += 2) rope_pair(v[r], v[r + 1], a, pos, (row0 + r) % a.head_dim);
+  }
+  if (s.mode == GEMV_ROPE_K_CACHE || s.mode == GEMV_V_CACHE) {
+    // head-major cache [seq][kv_head][pos][hd] (MultiHeadAttention.cs:262-274)
+    const int64_t seq = *a.seq, pos = *a.pos;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = row0 + r;
+      if (row >= s.rows) continue;
+      const int h = row / a.head_dim, d = row - h * a.head_dim;
+      s.y[((seq * a.n_kv + h) * a.max_ctx + pos) * a.head_dim + d] = v[r];
+    }
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    if (row >= s.rows) continue;
+    s.y[row] = s.mode == GEMV_ADD ? s.y[row] + v[r] : v[r];
+  }
+}
+
+__device__ __forceinline__ void prefetch_rows(const GemvArgs& a, const GemvSeg& s, int lg, int R, int sub,
+                                              int lane) {
   const int K = a.K;
   int64_t row_bytes;
   switch (s.fmt) {
@@ -246,29 +286,41 @@ __device__ __forceinline__ void prefetch_rows(const GemvArgs& a, const GemvSeg& 
     default: row_bytes = K >> 1; break;
   }
   const bool glu = s.mode == GEMV_GLU;
-  const int r0 = glu ? lg * 2 : lg * 4;
-  const int nr = min(glu ? 2 : 4, s.rows - r0);
+  const int rg = glu ? R / 2 : R;
+  const int r0 = lg * rg;
+  const int nr = min(rg, s.rows - r0);
   for (int w = 0; w < (glu ? 2 : 1); ++w) {
     const uint8_t* base = (w == 0 ? s.data : s.data2) + r0 * row_bytes;
     const int64_t bytes = nr * row_bytes;
-    for (int64_t off = (int64_t)lane * 128; off < bytes; off += 32 * 128)
+    for (int64_t off = (int64_t)(sub * 32 + lane) * 128; off < bytes; off += 32 * 128 * a.S)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
   }
 }
 
-template <int FA, int FB>
+__device__ __forceinline__ int seg_of(const GemvArgs& a, int g) {
+  int si = 0;
+  while (si + 1 < a.nseg && g >= a.seg[si + 1].group_begin) ++si;
+  return si;
+}
+
+// A CTA of 8 warps works on 8/S row groups at a time; the S warps of a group
+// split K and combine their partials through shared memory.
+template <int FA, int FB, int R>
 __global__ void __launch_bounds__(THREADS, 2) gemv1_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ float smem[];
   float* xs = smem;             // [K] swizzled
   float* x16 = xs + a.K;        // [K/16] sums of 16 consecutive x
-  float* red = x16 + a.K / 16;  // [WARPS]
+  float* red = x16 + a.K / 16;  // [WARPS][R]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gw = blockIdx.x * WARPS + warp, nw = gridDim.x * WARPS;
+  const int S = a.S, gpc = WARPS / S;
+  const int sub = warp % S;
   // 1. weights do not depend on the previous kernel: start pulling them into L2
-  for (int g = gw; g < a.ngroups; g += nw) {
-    int si = 0;
-    while (si + 1 < a.nseg && g >= a.seg[si + 1].group_begin) ++si;
-    prefetch_rows(a, a.seg[si], g - a.seg[si].group_begin, lane);
+  for (int base = blockIdx.x * gpc; base < a.ngroups; base += gridDim.x * gpc) {
+    const int g = base + warp / S;
+    if (g < a.ngroups) {
+      const int si = seg_of(a, g);
+      prefetch_rows(a, a.seg[si], g - a.seg[si].group_begin, R, sub, lane);
+    }
   }
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -302,15 +354,34 @@ __global__ void __launch_bounds__(THREADS, 2) gemv1_kernel(const __grid_constant
   }
   __syncthreads();
   // 3. row groups
-  for (int g = gw; g < a.ngroups; g += nw) {
+  for (int base = blockIdx.x * gpc; base < a.ngroups; base += gridDim.x * gpc) {
+    const int g = base + warp / S;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
     int si = 0;
-    while (si + 1 < a.nseg && g >= a.seg[si + 1].group_begin) ++si;
-    const GemvSeg& s = a.seg[si];
-    const int lg = g - s.group_begin;
-    if (FA == FB || s.fmt == FA)
-      group_rows<FA>(a, s, lg, xs, x16, lane);
-    else
-      group_rows<FB>(a, s, lg, xs, x16, lane);
+    if (g < a.ngroups) {
+      si = seg_of(a, g);
+      const GemvSeg& s = a.seg[si];
+      if (FA == FB || s.fmt == FA)
+        group_partial<FA, R>(a, s, g - s.group_begin, xs, x16, lane, sub, acc);
+      else
+        group_partial<FB, R>(a, s, g - s.group_begin, xs, x16, lane, sub, acc);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+    if (S > 1) {
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < R; ++r) red[warp * R + r] = acc[r];
+      __syncthreads();
+      if (sub == 0 && lane == 0)
+        for (int w = 1; w < S; ++w)
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[r] += red[(warp + w) * R + r];
+    }
+    if (g < a.ngroups && sub == 0 && lane == 0) group_store<R>(a, a.seg[si], g - a.seg[si].group_begin, acc);
+    if (S > 1) __syncthreads();
   }
 }
 
@@ -329,6 +400,8 @@ int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y
   if (a.nseg >= GEMV_MAX_SEG) return fail(SM_ERR_INVALID_ARG, "gemv1: too many segments");
   if (!gemv1_supports(w, a.K) || (w2 && (!gemv1_supports(*w2, a.K) || w2->scheme != w.scheme || w2->rows != w.rows)))
     return fail(SM_ERR_UNSUPPORTED, "gemv1: unsupported weight for the M=1 path");
+  if ((mode == GEMV_ROPE_Q || mode == GEMV_ROPE_K_CACHE) && (a.head_dim <= 0 || w.rows % a.head_dim))
+    return fail(SM_ERR_INVALID_ARG, "gemv1: RoPE epilogue needs whole heads");
   GemvSeg& s = a.seg[a.nseg];
   s.fmt = w.scheme;
   s.rows = w.rows;
@@ -339,14 +412,41 @@ int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y
   s.data2 = w2 ? (const uint8_t*)w2->data : nullptr;
   s.aux2 = w2 ? w2->aux : nullptr;
   s.y = y;
-  s.group_begin = a.ngroups;
-  a.ngroups += mode == GEMV_GLU ? (w.rows + 1) / 2 : (w.rows + 3) / 4;
   a.nseg++;
   return SM_OK;
 }
 
-int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch) {
-  const size_t smem = sizeof(float) * ((size_t)a.K + a.K / 16 + WARPS);
+namespace {
+int set_groups(GemvArgs& a, int R) {
+  a.ngroups = 0;
+  for (int i = 0; i < a.nseg; ++i) {
+    GemvSeg& s = a.seg[i];
+    s.group_begin = a.ngroups;
+    a.ngroups += s.mode == GEMV_GLU ? ceil_div(s.rows, R / 2) : ceil_div(s.rows, R);
+  }
+  return a.ngroups;
+}
+
+template <int R>
+void* pick_kernel(int fa, int fb) {
+  if (fa == fb) {
+    switch (fa) {
+      case SM_Q4_K: return (void*)gemv1_kernel<SM_Q4_K, SM_Q4_K, R>;
+      case SM_Q6_K: return (void*)gemv1_kernel<SM_Q6_K, SM_Q6_K, R>;
+      case SM_Q8_0: return (void*)gemv1_kernel<SM_Q8_0, SM_Q8_0, R>;
+      case SM_Q4_0: return (void*)gemv1_kernel<SM_Q4_0, SM_Q4_0, R>;
+    }
+  } else if (fa == SM_Q4_K && fb == SM_Q6_K) {
+    return (void*)gemv1_kernel<SM_Q4_K, SM_Q6_K, R>;
+  }
+  return nullptr;
+}
+}  // namespace
+
+int launch_gemv1(const GemvArgs& args, cudaStream_t st, int* n_launch) {
+  GemvArgs a = args;
+  const size_t smem = sizeof(float) * ((size_t)a.K + a.K / 16 + WARPS * 4);
+  if (smem > 200 * 1024) return fail(SM_ERR_UNSUPPORTED, "gemv1: K too large");
   // one or two distinct formats per launch (each pair is its own instantiation)
   int fa = a.seg[0].fmt, fb = fa;
   for (int i = 1; i < a.nseg; ++i) {
@@ -355,27 +455,39 @@ int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch) {
     fb = a.seg[i].fmt;
   }
   if (fb == SM_Q4_K && fa == SM_Q6_K) std::swap(fa, fb);
-  void (*kern)(GemvArgs) = nullptr;
-  if (fa == fb) {
-    switch (fa) {
-      case SM_Q4_K: kern = gemv1_kernel<SM_Q4_K, SM_Q4_K>; break;
-      case SM_Q6_K: kern = gemv1_kernel<SM_Q6_K, SM_Q6_K>; break;
-      case SM_Q8_0: kern = gemv1_kernel<SM_Q8_0, SM_Q8_0>; break;
-      case SM_Q4_0: kern = gemv1_kernel<SM_Q4_0, SM_Q4_0>; break;
+  // rows per group R and warps per group S: fill the SMs (2 CTAs x 8 warps each) while keeping
+  // every lane of a warp busy over K (units of 32 weights strided by 32*S)
+  const int units = a.K / 32;
+  const int target_warps = 148 * 2 * WARPS;
+  int bestR = 4, bestS = 1;
+  double best = -1;
+  for (int R : {4, 2})
+    for (int S : {1, 2, 4, 8}) {
+      const int ng = set_groups(a, R);
+      const int per = 32 * S;
+      const double lane_eff = (double)units / (per * ((units + per - 1) / per));
+      const double par_eff = std::min(1.0, (double)ng * S / target_warps);
+      const double score = lane_eff * par_eff * (R == 4 ? 1.0 : 0.85);
+      if (score > best + 1e-9) {
+        best = score;
+        bestR = R;
+        bestS = S;
+      }
     }
-  } else if (fa == SM_Q4_K && fb == SM_Q6_K) {
-    kern = gemv1_kernel<SM_Q4_K, SM_Q6_K>;
-  }
+  a.S = bestS;
+  set_groups(a, bestR);
+  void* kern = bestR == 4 ? pick_kernel<4>(fa, fb) : pick_kernel<2>(fa, fb);
   if (!kern) return fail(SM_ERR_UNSUPPORTED, "gemv1: unsupported format mix in one launch");
-  if (smem > 200 * 1024) return fail(SM_ERR_UNSUPPORTED, "gemv1: K too large");
-  static bool attr_set[64][8][8] = {};
+  static bool attr_set[64][8][8][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev][fa][fb]) {
+  const int ri = bestR == 4 ? 0 : 1;
+  if (dev < 64 && !attr_set[dev][fa][fb][ri]) {
     SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    attr_set[dev][fa][fb] = true;
+    attr_set[dev][fa][fb][ri] = true;
   }
-  const int grid = std::max(1, std::min(ceil_div(a.ngroups, WARPS), 148 * 2));
+  const int gpc = WARPS / bestS;
+  const int grid = std::max(1, std::min(ceil_div(a.ngroups, gpc), 148 * 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(THREADS);
@@ -386,7 +498,8 @@ int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+  void* params[] = {&a};
+  SM_CUDA_TRY(cudaLaunchKernelExC(&cfg, kern, params));
   if (n_launch) ++*n_launch;
   return SM_OK;
 }

@@ -5,7 +5,10 @@
 namespace sm {
 
 constexpr int GEMV_MAX_SEG = 4;
-enum { GEMV_STORE = 0, GEMV_ADD = 1, GEMV_GLU = 2 };
+// STORE: y[row] = v; ADD: y[row] += v (residual); GLU: y[row] = silu(gate) * up;
+// ROPE_Q: RoPE on pairs, then store; ROPE_K_CACHE / V_CACHE: (RoPE and) store into the
+// head-major KV cache at (*seq, *pos).
+enum { GEMV_STORE = 0, GEMV_ADD = 1, GEMV_GLU = 2, GEMV_ROPE_Q = 3, GEMV_ROPE_K_CACHE = 4, GEMV_V_CACHE = 5 };
 
 struct GemvSeg {
   int fmt = 0, rows = 0, bs = 0, mode = 0;
@@ -23,6 +26,13 @@ struct GemvArgs {
   const float* x = nullptr;
   const float* gamma = nullptr;  // non-null: RMSNorm x first (eps below)
   float eps = 1e-5f;
+  int S = 1;  // warps per row group (set by the launcher)
+  // RoPE / KV-cache epilogues
+  const int* pos = nullptr;
+  const int* seq = nullptr;
+  const float* sin_t = nullptr;
+  const float* cos_t = nullptr;
+  int head_dim = 0, n_kv = 0, max_ctx = 0;
 };
 
 bool gemv1_supports(const DevWeight& w, int K);
