@@ -614,6 +614,16 @@ __global__ void decode_commit_kernel(const int* __restrict__ seq, int* __restric
 // One-row step (bs1 decode): fused launches built on the M = 1 GEMV.  Per layer:
 // [RMSNorm + Q|K|V] -> RoPE + KV append -> attention -> [O-proj + residual]
 // -> [RMSNorm + gate/up + SiLU-gate] -> [down-proj + residual].
+// warp-per-row-group GEMV; SMALLMIND_GEMV_STREAM=1 selects the TMA-ring streaming kernel
+int launch_m1(const GemvArgs& a, sm_model* m, cudaStream_t st, int& nl) {
+  const char* e = std::getenv("SMALLMIND_GEMV_STREAM");
+  if (e && e[0] == '1') {
+    const int rc = launch_gemv_stream(a, m->ctx->dev_status, st, &nl);
+    if (rc != SM_ERR_UNSUPPORTED) return rc;
+  }
+  return launch_gemv1(a, st, &nl);
+}
+
 bool m1_supported(const sm_model* m) {
   const auto& c = m->cfg;
   for (const auto& L : m->layers) {
@@ -656,7 +666,7 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WQ], nullptr, w.qkv, GEMV_ROPE_Q));
       SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WK], nullptr, kc, GEMV_ROPE_K_CACHE));
       SM_TRY(gemv1_segment(qkv, *L.w[SM_ROLE_WV], nullptr, vc, GEMV_V_CACHE));
-      SM_TRY(launch_gemv1(qkv, st, &nl));
+      SM_TRY(launch_m1(qkv, m, st, nl));
       int arc = launch_attention_decode_cluster(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd,
                                                 w.lens(), w.seq(), 1, c.n_heads, c.n_kv_heads, hd, st, &nl);
       if (arc == SM_ERR_UNSUPPORTED)
@@ -668,7 +678,7 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       o.K = qd;
       o.x = w.att;
       SM_TRY(gemv1_segment(o, *L.w[SM_ROLE_WO], nullptr, w.x, GEMV_ADD));
-      SM_TRY(launch_gemv1(o, st, &nl));
+      SM_TRY(launch_m1(o, m, st, nl));
       GemvArgs gu;
       gu.K = H;
       gu.x = w.x;
@@ -676,11 +686,11 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       gu.eps = c.norm_eps;
       if (L.w[SM_ROLE_W_GATE]->scheme == L.w[SM_ROLE_W_UP]->scheme) {
         SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_GATE], L.w[SM_ROLE_W_UP], w.g, GEMV_GLU));
-        SM_TRY(launch_gemv1(gu, st, &nl));
+        SM_TRY(launch_m1(gu, m, st, nl));
       } else {
         SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_GATE], nullptr, w.g, GEMV_STORE));
         SM_TRY(gemv1_segment(gu, *L.w[SM_ROLE_W_UP], nullptr, w.u, GEMV_STORE));
-        SM_TRY(launch_gemv1(gu, st, &nl));
+        SM_TRY(launch_m1(gu, m, st, nl));
         SM_TRY(launch_silu_mul(w.g, w.u, w.g, c.ffn_hidden, st));
         ++nl;
       }
@@ -688,7 +698,7 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       dn.K = c.ffn_hidden;
       dn.x = w.g;
       SM_TRY(gemv1_segment(dn, *L.w[SM_ROLE_W_DOWN], nullptr, w.x, GEMV_ADD));
-      SM_TRY(launch_gemv1(dn, st, &nl));
+      SM_TRY(launch_m1(dn, m, st, nl));
     }
   }
   return SM_OK;
@@ -705,7 +715,7 @@ int head_m1(sm_model* m, const float* x_row, int& nl) {
   hd.gamma = m->out_norm;
   hd.eps = c.norm_eps;
   SM_TRY(gemv1_segment(hd, *m->output, nullptr, w.logits, GEMV_STORE));
-  SM_TRY(launch_gemv1(hd, st, &nl));
+  SM_TRY(launch_m1(hd, m, st, nl));
   SM_TRY(launch_argmax(w.logits, 1, c.vocab_size, w.amax(), st));
   ++nl;
   return SM_OK;

@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "gemv1.cuh"
+#include "gemv_units.cuh"
 
 namespace sm {
 namespace {
@@ -33,162 +34,6 @@ constexpr int THREADS = 256;
 constexpr int WARPS = THREADS / 32;
 
 __device__ __forceinline__ int swz(int k) { return k ^ (((k >> 5) & 7) << 2); }
-
-__device__ __forceinline__ float fbyte(uint32_t t, int b) {
-  // bytes (0, 0, t.byte_b, 0x3F): the float 1.0 with t.byte_b's low 7 bits in the top mantissa bits
-  return __uint_as_float(__byte_perm(t, 0x3F000000u, 0x7044u | (b << 8)));
-}
-
-template <int FMT>
-struct Unit;
-
-// Q4_K block (144 B): d, dmin fp16 | 12 B of 6-bit scales/mins | 128 B nibbles.
-template <>
-struct Unit<SM_Q4_K> {
-  struct Raw {
-    int4 hdr, qs;
-  };
-  __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
-    const uint8_t* blk = s.data + ((int64_t)row * (K >> 8) + (u >> 3)) * Q4K_BLOCK_BYTES;
-    r.hdr = __ldg((const int4*)blk);
-    r.qs = __ldg((const int4*)(blk + 16 + 16 * (u & 7)));
-  }
-  __device__ __forceinline__ static float dot(const Raw& r, int j, const float* x, float x16a, float x16b) {
-    const float d = __half2float(__ushort_as_half((unsigned short)(r.hdr.x & 0xFFFF)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)((uint32_t)r.hdr.x >> 16)));
-    // 8 six-bit scales are bits 6j..6j+5 of bytes 4..9, mins of bytes 10..15 (Q4KTensor.cs:109-126)
-    const uint64_t sb = (uint32_t)r.hdr.y | ((uint64_t)((uint32_t)r.hdr.z & 0xFFFFu) << 32);
-    const uint64_t mb = ((uint32_t)r.hdr.z >> 16) | ((uint64_t)(uint32_t)r.hdr.w << 16);
-    const float sc = d * (float)((sb >> (6 * j)) & 63);
-    const float mn = dmin * (float)((mb >> (6 * j)) & 63);
-    const uint32_t w[4] = {(uint32_t)r.qs.x, (uint32_t)r.qs.y, (uint32_t)r.qs.z, (uint32_t)r.qs.w};
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t tl = ((w[i] << 3) & 0x78787878u) | 0x80808080u;
-      const uint32_t th = ((w[i] >> 1) & 0x78787878u) | 0x80808080u;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        a0 = fmaf(fbyte(tl, b), x[8 * i + 2 * b], a0);
-        a1 = fmaf(fbyte(th, b), x[8 * i + 2 * b + 1], a1);
-      }
-    }
-    const float s16 = 16.f * sc;
-    return s16 * (a0 + a1) - (s16 + mn) * (x16a + x16b);
-  }
-};
-
-// Q6_K device body (208 B): ql 128 | qh' 64 (re-packed) | int8 scales 16; d in aux.
-template <>
-struct Unit<SM_Q6_K> {
-  struct Raw {
-    int4 ql;
-    int2 qh;
-    unsigned short sc;
-    unsigned short d;
-  };
-  __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
-    const int64_t b = (int64_t)row * (K >> 8) + (u >> 3);
-    const uint8_t* blk = s.data + b * Q6K_BODY_BYTES;
-    const int j = u & 7;
-    r.ql = __ldg((const int4*)(blk + 16 * j));
-    r.qh = __ldg((const int2*)(blk + 128 + 8 * j));
-    r.sc = __ldg((const unsigned short*)(blk + 192 + 2 * j));
-    r.d = __ldg((const unsigned short*)s.aux + b);
-  }
-  __device__ __forceinline__ static float half16(uint32_t w0, uint32_t w1, uint32_t W, const float* x) {
-    // elements 0..7 from w0, 8..15 from w1; byte b of W holds highs of 2b, 2b+1, 8+2b, 9+2b
-    const uint32_t t0 = ((w0 << 1) & 0x1E1E1E1Eu) | ((W << 5) & 0x60606060u) | 0x80808080u;
-    const uint32_t t1 = ((w0 >> 3) & 0x1E1E1E1Eu) | ((W << 3) & 0x60606060u) | 0x80808080u;
-    const uint32_t t2 = ((w1 << 1) & 0x1E1E1E1Eu) | ((W << 1) & 0x60606060u) | 0x80808080u;
-    const uint32_t t3 = ((w1 >> 3) & 0x1E1E1E1Eu) | ((W >> 1) & 0x60606060u) | 0x80808080u;
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      a0 = fmaf(fbyte(t0, b), x[2 * b], a0);
-      a1 = fmaf(fbyte(t1, b), x[2 * b + 1], a1);
-      a0 = fmaf(fbyte(t2, b), x[8 + 2 * b], a0);
-      a1 = fmaf(fbyte(t3, b), x[9 + 2 * b], a1);
-    }
-    return a0 + a1;
-  }
-  __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float x16a, float x16b) {
-    const float d = __half2float(__ushort_as_half(r.d));
-    const float sa = d * (float)(int8_t)(r.sc & 0xFF), sb = d * (float)(int8_t)(r.sc >> 8);
-    const float fa = half16((uint32_t)r.ql.x, (uint32_t)r.ql.y, (uint32_t)r.qh.x, x);
-    const float fb = half16((uint32_t)r.ql.z, (uint32_t)r.ql.w, (uint32_t)r.qh.y, x + 16);
-    return sa * (64.f * fa - 96.f * x16a) + sb * (64.f * fb - 96.f * x16b);
-  }
-};
-
-// Q8_0: 32 int8 + fp32 block scale (block size a multiple of 32).
-template <>
-struct Unit<SM_Q8_0> {
-  struct Raw {
-    int4 a, b;
-    float sc;
-  };
-  __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
-    const int64_t e0 = (int64_t)row * K + 32 * u;
-    r.a = __ldg((const int4*)(s.data + e0));
-    r.b = __ldg((const int4*)(s.data + e0) + 1);
-    r.sc = __ldg((const float*)s.aux + e0 / s.bs);
-  }
-  __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float, float) {
-    const uint32_t w[8] = {(uint32_t)r.a.x, (uint32_t)r.a.y, (uint32_t)r.a.z, (uint32_t)r.a.w,
-                           (uint32_t)r.b.x, (uint32_t)r.b.y, (uint32_t)r.b.z, (uint32_t)r.b.w};
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t v = w[i] ^ 0x80808080u;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const float q = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | b)) - 8388736.f;
-        if (b & 1)
-          a1 = fmaf(q, x[4 * i + b], a1);
-        else
-          a0 = fmaf(q, x[4 * i + b], a0);
-      }
-    }
-    return r.sc * (a0 + a1);
-  }
-};
-
-// Q4_0: 32 signed nibbles (global-index order: even low) + fp32 block scale.
-template <>
-struct Unit<SM_Q4_0> {
-  struct Raw {
-    int4 q;
-    float sc;
-  };
-  __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
-    const int64_t e0 = (int64_t)row * K + 32 * u;
-    r.q = __ldg((const int4*)(s.data + (e0 >> 1)));
-    r.sc = __ldg((const float*)s.aux + e0 / s.bs);
-  }
-  __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float x16a, float x16b) {
-    const uint32_t w[4] = {(uint32_t)r.q.x, (uint32_t)r.q.y, (uint32_t)r.q.z, (uint32_t)r.q.w};
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t v = w[i] ^ 0x88888888u;  // two's-complement nibble -> nibble + 8
-      const uint32_t tl = ((v << 3) & 0x78787878u) | 0x80808080u;
-      const uint32_t th = ((v >> 1) & 0x78787878u) | 0x80808080u;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        a0 = fmaf(fbyte(tl, b), x[8 * i + 2 * b], a0);
-        a1 = fmaf(fbyte(th, b), x[8 * i + 2 * b + 1], a1);
-      }
-    }
-    return r.sc * (16.f * (a0 + a1) - 24.f * (x16a + x16b));
-  }
-};
-
-// Rows of group lg handled by this segment (GLU: R/2 gate rows then the same R/2 up rows).
-template <int R>
-__device__ __forceinline__ int group_row(const GemvSeg& s, int lg, int r) {
-  return s.mode == GEMV_GLU ? lg * (R / 2) + (r % (R / 2)) : lg * R + r;
-}
 
 // Partial dot products of R rows over this warp's share of K (units sub, sub+S, ...).
 template <int FMT, int R>
@@ -221,57 +66,6 @@ __device__ __forceinline__ void group_partial(const GemvArgs& a, const GemvSeg& 
 #pragma unroll
     for (int r = 0; r < R; ++r)
       if (rows[r] < s.rows) acc[r] += Unit<FMT>::dot(raw[r], j, xr, xa, xb);
-  }
-}
-
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, const GemvArgs& a, int pos, int d) {
-  // RotaryEmbedding.cs:103-116 on the pair (d, d+1), d even
-  const int half = a.head_dim / 2, i = d / 2;
-  const float c = a.cos_t[pos * half + i], sn = a.sin_t[pos * half + i];
-  const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-  const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
-  x0 = y0;
-  x1 = y1;
-}
-
-// Epilogue of one group, final row values v[0..R-1].
-template <int R>
-__device__ __forceinline__ void group_store(const GemvArgs& a, const GemvSeg& s, int lg, float* v) {
-  if (s.mode == GEMV_GLU) {
-#pragma unroll
-    for (int r = 0; r < R / 2; ++r) {
-      const int row = group_row<R>(s, lg, r);
-      if (row >= s.rows) continue;
-      const float g = v[r], u = v[r + R / 2];
-      const float c = fmaxf(-20.f, fminf(g, 20.f));
-      const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));  // ActivationOps.cs:304-309
-      s.y[row] = __fmul_rn(__fmul_rn(g, sig), u);
-    }
-    return;
-  }
-  const int row0 = group_row<R>(s, lg, 0);
-  if (s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE) {
-    const int pos = *a.pos;
-#pragma unroll
-    for (int r = 0; r < R; r += 2) rope_pair(v[r], v[r + 1], a, pos, (row0 + r) % a.head_dim);
-  }
-  if (s.mode == GEMV_ROPE_K_CACHE || s.mode == GEMV_V_CACHE) {
-    // head-major cache [seq][kv_head][pos][hd] (MultiHeadAttention.cs:262-274)
-    const int64_t seq = *a.seq, pos = *a.pos;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = row0 + r;
-      if (row >= s.rows) continue;
-      const int h = row / a.head_dim, d = row - h * a.head_dim;
-      s.y[((seq * a.n_kv + h) * a.max_ctx + pos) * a.head_dim + d] = v[r];
-    }
-    return;
-  }
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int row = row0 + r;
-    if (row >= s.rows) continue;
-    s.y[row] = s.mode == GEMV_ADD ? s.y[row] + v[r] : v[r];
   }
 }
 
