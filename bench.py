@@ -210,6 +210,60 @@ def cpu_decode_sample(cfg, ctx_len, steps, threads):
     return steps / dt, dt, build_s
 
 
+def make_weights(sm, ctx, torch, scheme, rows, cols, count, seed=7):
+    """`count` distinct INTENDED-layout weights quantized on the device (N(0, 0.02))."""
+    import ctypes as C
+    from smallmind_b200 import _lib as L
+    lib = L.lib()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    sch = int(getattr(sm.QuantScheme, scheme))
+    out = []
+    n = rows * cols
+    for _ in range(count):
+        src = torch.randn(n, generator=gen, device="cuda") * 0.02
+        nbytes = {6: n // 256 * 144, 7: n // 256 * 210, 2: n, 3: n // 2}[sch]
+        data = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        scales = torch.empty(max(1, n // 32), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        L.check(lib.sm_quantize(ctx.handle, sch, src.data_ptr(), n, 32, data.data_ptr(), scales.data_ptr()))
+        h = C.c_void_p()
+        L.check(lib.sm_weight_upload_device(ctx.handle, sch, rows, cols, 32, data.data_ptr(), nbytes,
+                                            scales.data_ptr() if sch in (2, 3) else None,
+                                            n // 32 if sch in (2, 3) else 0, L.LAYOUT_INTENDED, C.byref(h)))
+        w = sm.CudaWeightTensor.__new__(sm.CudaWeightTensor)
+        w.ctx, w.handle, w._rows, w._cols = ctx, h, rows, cols
+        w._scheme, w.layout = sm.QuantScheme(sch), L.LAYOUT_INTENDED
+        out.append(w)
+    return out
+
+
+def run_gemv_sweep(args):
+    """Op-sweep GEMV at M = 1: device time per launch from a CUDA graph over
+    enough distinct weights to exceed L2."""
+    import torch
+
+    import smallmind_b200 as sm
+    ctx = sm.CudaContext(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    torch.cuda.set_stream(stream)
+    hbm, _ = peaks()
+    res = {}
+    for scheme in ("Q4_K", "Q6_K", "Q8_0", "Q4_0"):
+        for (K, N) in ((2048, 2048), (2048, 5632), (5632, 2048), (4096, 11008)):
+            if args.gemv_only and args.gemv_only != f"{scheme} {K}x{N}":
+                continue
+            nb = N * K * BYTES[scheme]
+            count = max(2, int(300e6 // nb) + 1)
+            ws = make_weights(sm, ctx, torch, scheme, N, K, count)
+            ms, alg = time_gemv(sm, ctx, ws, torch, reps=3)
+            res[f"{scheme} {K}x{N}"] = {"us": round(ms * 1000, 2), "GBs": round(alg / (ms * 1e-3) / 1e9, 1),
+                                       "frac": round(alg / (ms * 1e-3) / 1e9 / hbm, 3)}
+            for w in ws:
+                w.close()
+    print(json.dumps({"gemv_sweep_m1": res, "peak_gbs": hbm}), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -401,12 +455,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
+    ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
+    ap.add_argument("--gemv-only", default=None, help="restrict --gemv-sweep to 'SCHEME KxN' (profiling)")
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the device decode loop (profiling runs: no e2e, GEMV, bs64 or CPU legs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.gemv_sweep:
+        run_gemv_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "gemv1.cuh"
+#include "decode_mega.cuh"
 
 // ---------------------------------------------------------------- errors
 namespace sm {
@@ -133,14 +134,22 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
   if (scheme == SM_Q6_K) {
     const int64_t nb = n / 256;
     d.data_bytes = (size_t)nb * Q6K_BODY_BYTES;
-    d.aux_bytes = (size_t)nb * 2;
+    int64_t aux_elems = nb;
+    if (layout == SM_LAYOUT_INTENDED) {  // one 16-byte-padded row of d values per weight row
+      d.aux_bpr = cols / 256;
+      d.aux_stride = (d.aux_bpr * 2 + 15) / 16 * 8;
+      aux_elems = (int64_t)rows * d.aux_stride;
+    }
+    d.aux_bytes = (size_t)aux_elems * 2;
     if (cudaMalloc(&d.data, d.data_bytes) != cudaSuccess || cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
       return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+    cudaMemsetAsync(d.aux, 0, d.aux_bytes, st);
     void* staging = nullptr;
     if (cudaMallocAsync(&staging, nbytes, st) != cudaSuccess)
       return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
     cudaMemcpyAsync(staging, data, nbytes, kind, st);
-    int rc = launch_q6k_relayout((const uint8_t*)staging, (uint8_t*)d.data, (uint16_t*)d.aux, nb, st);
+    int rc = launch_q6k_relayout((const uint8_t*)staging, (uint8_t*)d.data, (uint16_t*)d.aux, nb, d.aux_bpr,
+                                 d.aux_stride, st);
     cudaFreeAsync(staging, st);
     if (rc) return cleanup(rc);
   } else {
@@ -148,10 +157,21 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
     if (cudaMalloc(&d.data, nbytes) != cudaSuccess) return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
     cudaMemcpyAsync(d.data, data, nbytes, kind, st);
     if (has_scales) {
-      d.aux_bytes = nscales * sizeof(float);
-      if (cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
-        return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
-      cudaMemcpyAsync(d.aux, scales, d.aux_bytes, kind, st);
+      if (layout == SM_LAYOUT_INTENDED && cols % bs == 0) {  // 16-byte-padded row of scales per weight row
+        d.aux_bpr = cols / bs;
+        d.aux_stride = (d.aux_bpr * 4 + 15) / 16 * 4;
+        d.aux_bytes = (size_t)rows * d.aux_stride * sizeof(float);
+        if (cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
+          return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+        cudaMemsetAsync(d.aux, 0, d.aux_bytes, st);
+        cudaMemcpy2DAsync(d.aux, (size_t)d.aux_stride * 4, scales, (size_t)d.aux_bpr * 4, (size_t)d.aux_bpr * 4, rows,
+                          kind, st);
+      } else {
+        d.aux_bytes = nscales * sizeof(float);
+        if (cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
+          return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+        cudaMemcpyAsync(d.aux, scales, d.aux_bytes, kind, st);
+      }
     }
   }
   cudaError_t e = cudaStreamSynchronize(st);
@@ -557,6 +577,11 @@ struct sm_kv {
   std::map<int, Graph> graphs;  // decode batch size -> captured step
   int* pinned = nullptr;        // host staging for per-step inputs
   int pinned_cap = 0;
+  // one-launch bs1 decode step (decode_mega.cu)
+  MegaLayer* mega_layers = nullptr;  // device table of per-layer segments
+  unsigned* mega_sync = nullptr;     // grid barrier / combine counters
+  unsigned long long* mega_trace = nullptr;  // SMALLMIND_MEGA_TRACE: per-CTA phase timestamps
+  int mega_generation = -1;
   size_t layer_stride() const { return (size_t)max_seqs * m->cfg.n_kv_heads * max_tokens * m->cfg.head_dim; }
 };
 
@@ -565,7 +590,9 @@ namespace {
 int work_reserve(sm_model* m, int rows, int logit_rows, int attn_rows, int max_tokens) {
   Work& w = m->work;
   const auto& c = m->cfg;
-  const size_t need_scratch = attention_decode_scratch_floats(std::max(1, attn_rows), c.n_heads, max_tokens);
+  const size_t need_scratch =
+      std::max(attention_decode_scratch_floats(std::max(1, attn_rows), c.n_heads, max_tokens),
+               mega_scratch_floats(c.n_heads, c.n_kv_heads, c.head_dim, max_tokens, mega_grid_size()));
   if (rows <= w.cap_rows && logit_rows <= w.cap_logit_rows && need_scratch <= w.attn_scratch_floats) return SM_OK;
   cudaStreamSynchronize(m->ctx->stream);
   const int R = std::max(rows, w.cap_rows);
@@ -787,6 +814,116 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
   return SM_OK;
 }
 
+MegaSeg mega_seg(const DevWeight& w, const DevWeight* w2, int mode, float* y) {
+  MegaSeg s;
+  s.fmt = w.scheme;
+  s.rows = w.rows;
+  s.bs = w.block_size;
+  s.aux_bpr = w.aux_bpr;
+  s.aux_stride = w.aux_stride;
+  s.mode = mode;
+  s.data = (const uint8_t*)w.data;
+  s.aux = w.aux;
+  s.data2 = w2 ? (const uint8_t*)w2->data : nullptr;
+  s.aux2 = w2 ? w2->aux : nullptr;
+  s.y = y;
+  return s;
+}
+
+bool mega_enabled(sm_model* m) {
+  const char* e = std::getenv("SMALLMIND_MEGA");
+  if (e && e[0] == '0') return false;
+  if (!m1_supported(m)) return false;
+  for (const auto& L : m->layers)
+    if (L.w[SM_ROLE_W_GATE]->scheme != L.w[SM_ROLE_W_UP]->scheme) return false;
+  return true;
+}
+
+// Fills the one-launch decode arguments for the current workspace and cache;
+// returns SM_ERR_UNSUPPORTED if the shape does not fit the kernel.
+int mega_args(sm_model* m, sm_kv* kv, MegaArgs& a) {
+  const auto& c = m->cfg;
+  Work& w = m->work;
+  a.n_layers = c.n_layers;
+  a.H = c.hidden;
+  a.qd = m->qd();
+  a.kd = m->kd();
+  a.F = c.ffn_hidden;
+  a.V = c.vocab_size;
+  a.nH = c.n_heads;
+  a.nKv = c.n_kv_heads;
+  a.hd = c.head_dim;
+  a.max_ctx = kv->max_tokens;
+  a.eps = c.norm_eps;
+  if (!mega_supported(a)) return SM_ERR_UNSUPPORTED;
+  const int grid = mega_grid_size();
+  if (mega_scratch_floats(a.nH, a.nKv, a.hd, a.max_ctx, grid) > w.attn_scratch_floats) return SM_ERR_UNSUPPORTED;
+  if (!kv->mega_layers || kv->mega_generation != w.generation) {
+    std::vector<MegaLayer> hl(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+      const auto& L = m->layers[l];
+      float* kc = kv->k + kv->layer_stride() * l;
+      float* vc = kv->v + kv->layer_stride() * l;
+      MegaLayer& t = hl[l];
+      t.qkv[0] = mega_seg(*L.w[SM_ROLE_WQ], nullptr, GEMV_ROPE_Q, w.qkv);
+      t.qkv[1] = mega_seg(*L.w[SM_ROLE_WK], nullptr, GEMV_ROPE_K_CACHE, kc);
+      t.qkv[2] = mega_seg(*L.w[SM_ROLE_WV], nullptr, GEMV_V_CACHE, vc);
+      t.o = mega_seg(*L.w[SM_ROLE_WO], nullptr, GEMV_ADD, w.x);
+      t.gu = mega_seg(*L.w[SM_ROLE_W_GATE], L.w[SM_ROLE_W_UP], GEMV_GLU, w.g);
+      t.down = mega_seg(*L.w[SM_ROLE_W_DOWN], nullptr, GEMV_ADD, w.x);
+      t.attn_norm = L.attn_norm;
+      t.ffn_norm = L.ffn_norm;
+      t.kc = kc;
+      t.vc = vc;
+    }
+    if (!kv->mega_layers) SM_CUDA_TRY(cudaMalloc(&kv->mega_layers, sizeof(MegaLayer) * c.n_layers));
+    if (!kv->mega_sync) SM_CUDA_TRY(cudaMalloc(&kv->mega_sync, 64 * sizeof(unsigned)));
+    SM_CUDA_TRY(cudaMemcpy(kv->mega_layers, hl.data(), sizeof(MegaLayer) * c.n_layers, cudaMemcpyHostToDevice));
+    kv->mega_generation = w.generation;
+  }
+  a.layers = kv->mega_layers;
+  a.head = mega_seg(*m->output, nullptr, GEMV_STORE, w.logits);
+  if (!mega_seg_supported(a.head)) return SM_ERR_UNSUPPORTED;
+  for (const auto& L : m->layers)
+    for (int r : {SM_ROLE_WQ, SM_ROLE_WK, SM_ROLE_WV, SM_ROLE_WO, SM_ROLE_W_GATE, SM_ROLE_W_UP, SM_ROLE_W_DOWN})
+      if (!mega_seg_supported(mega_seg(*L.w[r], nullptr, GEMV_STORE, nullptr))) return SM_ERR_UNSUPPORTED;
+  a.out_norm = m->out_norm;
+  a.embd = m->embd;
+  a.sin_t = m->sin_t;
+  a.cos_t = m->cos_t;
+  a.x = w.x;
+  a.q = w.qkv;
+  a.att = w.att;
+  a.act = w.g;
+  a.logits = w.logits;
+  a.next_token = w.amax();
+  a.token = w.tok();
+  a.seq = w.seq();
+  a.kv_len = kv->len_dev;
+  const int chunks = std::max(1, grid / a.nKv);
+  const int G = a.nH / a.nKv;
+  float* sc = w.attn_scratch;
+  a.scores = sc;
+  sc += (size_t)a.nH * a.max_ctx;
+  a.cmax = sc;
+  sc += (size_t)a.nKv * chunks * G;
+  a.psum = sc;
+  sc += (size_t)a.nKv * chunks * G;
+  a.pacc = sc;
+  sc += (size_t)a.nKv * chunks * G * a.hd;
+  a.amax_val = sc;
+  sc += grid;
+  a.amax_idx = (int*)sc;
+  a.sync = kv->mega_sync;
+  a.status = m->ctx->dev_status;
+  if (std::getenv("SMALLMIND_MEGA_TRACE")) {
+    if (!kv->mega_trace)
+      SM_CUDA_TRY(cudaMalloc(&kv->mega_trace, sizeof(unsigned long long) * MEGA_TRACE_EVENTS * grid));
+    a.trace = kv->mega_trace;
+  }
+  return SM_OK;
+}
+
 bool use_graphs() {
   const char* e = std::getenv("SMALLMIND_CUDA_GRAPHS");
   return !(e && e[0] == '0');
@@ -954,6 +1091,9 @@ SM_API int sm_kv_destroy(sm_kv* kv) {
   cudaStreamSynchronize(kv->m->ctx->stream);
   for (auto& it : kv->graphs)
     if (it.second.exec) cudaGraphExecDestroy(it.second.exec);
+  if (kv->mega_layers) cudaFree(kv->mega_layers);
+  if (kv->mega_sync) cudaFree(kv->mega_sync);
+  if (kv->mega_trace) cudaFree(kv->mega_trace);
   cudaFree(kv->k);
   cudaFree(kv->v);
   cudaFree(kv->len_dev);
@@ -1071,7 +1211,10 @@ SM_API int sm_decode(sm_model* m, sm_kv* kv, const int* seq_ids, const int* toke
     SM_CUDA_TRY(cudaMemcpyAsync(w.tok(), tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
     SM_CUDA_TRY(cudaMemcpyAsync(w.seq(), seq_ids, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
   }
+  MegaArgs mega;
+  const bool use_mega = n == 1 && mega_enabled(m) && mega_args(m, kv, mega) == SM_OK;
   auto body = [&](int& nl) -> int {
+    if (use_mega) return launch_decode_mega(mega, st, &nl);
     decode_prep_kernel<<<ceil_div(n, 128), 128, 0, st>>>(w.seq(), w.pos(), w.lens(), kv->len_dev, n, kv->max_tokens,
                                                           m->ctx->dev_status);
     ++nl;
@@ -1116,6 +1259,17 @@ SM_API int sm_decode(sm_model* m, sm_kv* kv, const int* seq_ids, const int* toke
   if (logits)
     SM_CUDA_TRY(cudaMemcpyAsync(logits, w.logits, sizeof(float) * (size_t)n * m->cfg.vocab_size, out_kind, st));
   if (next_tokens) SM_CUDA_TRY(cudaMemcpyAsync(next_tokens, w.amax(), sizeof(int) * n, out_kind, st));
+  if (use_mega && mega.trace) {
+    // profiling: append this step's per-CTA phase timestamps to the trace file
+    const int grid = mega_grid_size();
+    std::vector<unsigned long long> t((size_t)grid * MEGA_TRACE_EVENTS);
+    SM_CUDA_TRY(cudaMemcpyAsync(t.data(), mega.trace, t.size() * 8, cudaMemcpyDeviceToHost, st));
+    SM_CUDA_TRY(cudaStreamSynchronize(st));
+    if (FILE* f = std::fopen(std::getenv("SMALLMIND_MEGA_TRACE"), "ab")) {
+      std::fwrite(t.data(), 8, t.size(), f);
+      std::fclose(f);
+    }
+  }
   if (host) {
     SM_CUDA_TRY(cudaStreamSynchronize(st));
     for (int i = 0; i < n; ++i) kv->len_host[seq_ids[i]] += 1;

@@ -43,10 +43,21 @@ struct DevWeight {
   void* data = nullptr;
   void* aux = nullptr;     // Q8_0/Q4_0: float scales; Q6_K: half d[]
   size_t data_bytes = 0, aux_bytes = 0;
+  // INTENDED-layout weights keep each row's scales (Q8_0/Q4_0) or d values (Q6_K)
+  // in a row of `aux_stride` elements, padded to 16 bytes, so a row's packed
+  // bytes and its scales can both be moved with 16-byte bulk copies.
+  // aux_stride == 0: scales in plain linear block order.
+  int aux_bpr = 0;     // scale blocks per row
+  int aux_stride = 0;  // elements per padded row
   // matmul orientation view: N outputs, K inputs
   int N() const { return layout == SM_LAYOUT_INTENDED ? rows : cols; }
   int K() const { return layout == SM_LAYOUT_INTENDED ? cols : rows; }
 };
+
+// linear scale-block index -> index in the (possibly row-padded) aux array
+__host__ __device__ __forceinline__ int64_t aux_idx(int64_t b, int bpr, int stride) {
+  return stride ? (b / bpr) * stride + (b % bpr) : b;
+}
 
 constexpr int Q4K_BLOCK_BYTES = 144;
 constexpr int Q6K_BLOCK_BYTES = 210;
@@ -113,7 +124,8 @@ int ctx_view(sm_ctx* ctx, int* device, cudaStream_t* stream, int64_t** launches)
 // quant.cu
 int launch_dequant(const DevWeight& w, float* out, cudaStream_t st);
 int launch_quantize(int scheme, const float* src, int64_t n, int bs, void* data, float* scales, cudaStream_t st);
-int launch_q6k_relayout(const uint8_t* src, uint8_t* body, uint16_t* d, int64_t nblocks, cudaStream_t st);
+int launch_q6k_relayout(const uint8_t* src, uint8_t* body, uint16_t* d, int64_t nblocks, int bpr, int stride,
+                        cudaStream_t st);
 // gemv.cu: y[m][n] (+)= x[m][k] . W^T over a row range; epilogue: 0 store, 1 add into y
 int launch_matmul(const DevWeight& w, const float* x, float* y, int M, int ldy, int accumulate, cudaStream_t st,
                   int* n_launch);

@@ -1,0 +1,826 @@
+// Persistent one-launch decode step for one sequence (bs1).
+//
+// A decode step is ~30 MB of weights per layer read once.  Launching a kernel
+// per GEMV costs ~2 us of ramp-up and drain each on B200, which at these
+// sizes is as long as the transfer itself, so this kernel runs the whole step
+// (22 layers + LM head + argmax) as one launch: one CTA per SM, co-resident.
+//
+//  * Warp 15 of every CTA is a producer.  It walks the fixed schedule of the
+//    step's GEMV rows assigned to this CTA (Q|K|V, O, gate/up, down for every
+//    layer, then the head) and streams them into a ring of shared-memory
+//    stages with cp.async.bulk + mbarrier.  It never waits for other CTAs, so
+//    while the consumers sit in a grid barrier or do attention, the next
+//    phases' weights keep arriving.
+//  * Warps 0..14 consume: per phase they build their 32-element slice of the
+//    input vector in registers (RMSNorm fused), compute per-(row, unit)
+//    partials from the staged bytes (exact byte-permute dequant of
+//    gemv_units.cuh), reduce rows in a fixed order and run the epilogue (RoPE
+//    + KV append, residual add, SiLU gate).
+//  * Phases are separated by a global barrier (atomic counter, bounded spin).
+//    Attention is two phases: scores + slice max per (kv head, chunk), then
+//    Pade exp against the exact row max, partial e.V, and a last-arriving-CTA
+//    combine per kv head (threadfence + counter).
+//  * Every wait is bounded (~2 s of clock64); on timeout the kernel records
+//    SM_ERR_TIMEOUT in the context status word and returns.
+#include <algorithm>
+#include <cfloat>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "decode_mega.cuh"
+#include "gemv_units.cuh"
+#include "mbar.cuh"
+
+namespace sm {
+namespace {
+
+constexpr int MT = 512;              // threads per CTA
+constexpr int MW = MT / 32;          // warps
+constexpr int CWARPS = MW - 1;       // consumer warps
+constexpr int CT = CWARPS * 32;      // consumer threads
+constexpr int MGMAX = 8;             // q heads per kv head
+constexpr long long kSpin = 4000000000LL;
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
+
+__device__ __forceinline__ int64_t row_bytes_fmt(int fmt, int K) {
+  switch (fmt) {
+    case SM_Q4_K: return (int64_t)(K >> 8) * Q4K_BLOCK_BYTES;
+    case SM_Q6_K: return (int64_t)(K >> 8) * Q6K_BODY_BYTES;
+    case SM_Q8_0: return K;
+    default: return K >> 1;
+  }
+}
+
+// bytes of one padded row of scales / d (0: the format has none)
+__device__ __forceinline__ int64_t aux_row_bytes(const MegaSeg& s) {
+  if (s.fmt == SM_Q4_K) return 0;
+  return (int64_t)s.aux_stride * (s.fmt == SM_Q6_K ? 2 : 4);
+}
+
+// output rows per stage: as many as fit one ring slot (weights + scales, gate + up for GLU)
+__device__ __forceinline__ int stage_rows(const MegaSeg& s, int K, int64_t slot_bytes) {
+  const int mult = s.mode == GEMV_GLU ? 2 : 1;
+  const int64_t per = mult * (row_bytes_fmt(s.fmt, K) + aux_row_bytes(s));
+  return (int)max((int64_t)1, min((int64_t)64, slot_bytes / per));
+}
+
+// rows of a segment for CTA i of n: whole row pairs, balanced
+__device__ __forceinline__ void seg_rows(int rows, int i, int n, int& r0, int& r1) {
+  const int pairs = (rows + 1) / 2;
+  r0 = min(rows, 2 * (int)((int64_t)pairs * i / n));
+  r1 = min(rows, 2 * (int)((int64_t)pairs * (i + 1) / n));
+}
+
+struct Shared {
+  uint64_t full[16];
+  uint64_t empty[16];
+  float red[MW * MGMAX];
+  float vec[4 * MGMAX];
+  int flag[4];
+  int consumed;
+  int abort;
+  volatile int phase;  // consumers' current GEMV phase (no-lookahead mode)
+};
+
+// ---------------------------------------------------------------- producer
+struct Producer {
+  const MegaArgs& a;
+  Shared& sh;
+  uint8_t* ring;
+  int64_t slot_bytes;
+  int k = 0;  // stages issued
+  bool ok = true;
+
+  __device__ void seg(const MegaSeg& s, int K, int /*rb*/, int phase) {
+    if (!ok) return;
+    const int rb = stage_rows(s, K, slot_bytes);
+    if (!a.lookahead) {
+      const long long t0 = clock64();
+      while (sh.phase < phase && !sh.abort)
+        if (clock64() - t0 > kSpin) {
+          ok = false;
+          return;
+        }
+    }
+    int r0, r1;
+    seg_rows(s.rows, blockIdx.x, gridDim.x, r0, r1);
+    const int64_t rbytes = row_bytes_fmt(s.fmt, K);
+    const bool glu = s.mode == GEMV_GLU;
+    for (int row = r0; row < r1; row += rb) {
+      const int n = min(rb, r1 - row);
+      const int slot = k % a.nslots;
+      if (k >= a.nslots) {
+        if (!mbar_wait_bounded(&sh.empty[slot], ((k / a.nslots) - 1) & 1, a.status) || sh.abort) {
+          ok = false;
+          return;
+        }
+      }
+      uint8_t* dst = ring + slot * slot_bytes;
+      const uint32_t bytes = (uint32_t)(n * rbytes);
+      const int64_t arb = aux_row_bytes(s);
+      const uint32_t abytes = (uint32_t)(n * arb);
+      const int nw = glu ? 2 : 1;
+      mbar_expect_tx(&sh.full[slot], nw * (bytes + abytes));
+      bulk_g2s(dst, s.data + row * rbytes, bytes, &sh.full[slot]);
+      if (glu) bulk_g2s(dst + rb * rbytes, s.data2 + row * rbytes, bytes, &sh.full[slot]);
+      if (abytes) {
+        uint8_t* adst = dst + nw * rb * rbytes;
+        bulk_g2s(adst, (const uint8_t*)s.aux + row * arb, abytes, &sh.full[slot]);
+        if (glu) bulk_g2s(adst + rb * arb, (const uint8_t*)s.aux2 + row * arb, abytes, &sh.full[slot]);
+      }
+      ++k;
+    }
+  }
+};
+
+// ---------------------------------------------------------------- consumers
+struct Consumer {
+  const MegaArgs& a;
+  Shared& sh;
+  uint8_t* ring;
+  int64_t slot_bytes;
+  float* part;
+  GemvArgs ep;  // epilogue context (RoPE / cache)
+  int tid;
+  int k = 0;  // stages consumed
+  unsigned barrier_gen = 0;
+  int ev = 0;
+  __device__ void stamp() {
+    if (a.trace && tid == 0 && ev < MEGA_TRACE_EVENTS) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.trace[(size_t)blockIdx.x * MEGA_TRACE_EVENTS + ev] = t;
+    }
+    ++ev;
+  }
+  // this thread's slice of the current input vector, as dp4a byte planes
+  XPlanes xp;
+  bool pair = true;  // plane packing (PAIR for K-quants / Q4_0, NATURAL for Q8_0)
+  const float* x_src = nullptr;
+  const float* x_gamma = nullptr;
+  int x_K = 0;
+  int U = 1, u = 0, ph = 0, P = 1, nwpp = 1;
+  bool u_ok = false;
+
+  __device__ bool grid_barrier() {
+    // all consumer stores of this CTA are done before thread 0 arrives
+    cons_sync();
+    stamp();
+    ++barrier_gen;
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(&a.sync[0], 1u);
+      const unsigned target = barrier_gen * gridDim.x;
+      const long long t0 = clock64();
+      int ok = 1;
+      while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
+        if (v >= target) break;
+        if (clock64() - t0 > kSpin) {
+          atomicExch(a.status, SM_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+      sh.flag[0] = ok;
+    }
+    cons_sync();
+    stamp();
+    if (!sh.flag[0]) {
+      if (tid == 0) sh.abort = 1;
+      return false;
+    }
+    return true;
+  }
+
+  // x slice for a phase with K inputs (optionally RMS-normalised with gamma)
+  __device__ void load_x(const float* src, const float* gamma, int K, bool want_pair = true) {
+    x_src = src;
+    x_gamma = gamma;
+    x_K = K;
+    pair = want_pair;
+    float xr[32];
+    // warp w covers units (w % nwpp)*32 + lane of row phase w / nwpp, so a warp's
+    // partials for one row can be reduced with shuffles inside the compute loop
+    U = K >> 5;
+    nwpp = (U + 31) / 32;
+    P = CWARPS / nwpp;
+    ph = (tid >> 5) / nwpp;
+    const int u_raw = ((tid >> 5) % nwpp) * 32 + (tid & 31);
+    u_ok = u_raw < U && ph < P;
+    u = u_ok ? u_raw : 0;
+    // one coalesced pass per CTA (the vector was written by other CTAs: bypass L1).
+    // 16-byte chunk c of unit w is stored at chunk (c + w) % 8 of that unit, so the
+    // 8 lanes of a quarter-warp reading chunk c of 8 consecutive units hit 8
+    // different bank groups.
+    float4* xs = (float4*)part;        // [K/4]
+    float4* gs = (float4*)part + K / 4; // [K/4]
+    for (int t = tid; t < K / 4; t += CT) {
+      const int w = t >> 3, p = (w << 3) + (((t & 7) + w) & 7);
+      xs[p] = __ldcg((const float4*)src + t);
+      if (gamma) gs[p] = __ldg((const float4*)gamma + t);
+    }
+    cons_sync();
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 v = xs[(u << 3) + ((c + u) & 7)];
+      xr[4 * c] = v.x; xr[4 * c + 1] = v.y; xr[4 * c + 2] = v.z; xr[4 * c + 3] = v.w;
+    }
+    if (gamma) {
+      float ss = 0.f;
+      if (ph == 0 && u_ok)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss = fmaf(xr[i], xr[i], ss);
+      ss = warp_sum(ss);
+      if ((tid & 31) == 0) sh.red[tid >> 5] = ss;
+      cons_sync();
+      float tot = 0.f;
+      for (int w = 0; w < CWARPS; ++w) tot += sh.red[w];
+      const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 gv = gs[(u << 3) + ((c + u) & 7)];
+        xr[4 * c] = __fmul_rn(gv.x, __fmul_rn(xr[4 * c], inv));
+        xr[4 * c + 1] = __fmul_rn(gv.y, __fmul_rn(xr[4 * c + 1], inv));
+        xr[4 * c + 2] = __fmul_rn(gv.z, __fmul_rn(xr[4 * c + 2], inv));
+        xr[4 * c + 3] = __fmul_rn(gv.w, __fmul_rn(xr[4 * c + 3], inv));
+      }
+    }
+    cons_sync();  // staging area (part) and sh.red are reused next
+    make_planes(xr, pair, xp);
+  }
+
+  // one unit of a staged row (integer dot path); `auxp` is the row's staged scales / d
+  __device__ float dot(int fmt, int bs, const uint8_t* rowp, const uint8_t* auxp) {
+    switch (fmt) {
+      case SM_Q4_K: {
+        Unit<SM_Q4_K>::Raw r;
+        const uint8_t* blk = rowp + (u >> 3) * Q4K_BLOCK_BYTES;
+        r.hdr = *(const int4*)blk;
+        r.qs = *(const int4*)(blk + 16 + 16 * (u & 7));
+        return dot_i8_q4k(r, u & 7, xp);
+      }
+      case SM_Q6_K: {
+        Unit<SM_Q6_K>::Raw r;
+        const uint8_t* blk = rowp + (u >> 3) * Q6K_BODY_BYTES;
+        const int j = u & 7;
+        r.ql = *(const int4*)(blk + 16 * j);
+        r.qh = *(const int2*)(blk + 128 + 8 * j);
+        r.sc = *(const unsigned short*)(blk + 192 + 2 * j);
+        r.d = ((const unsigned short*)auxp)[u >> 3];
+        return dot_i8_q6k(r, xp);
+      }
+      case SM_Q8_0: {
+        Unit<SM_Q8_0>::Raw r;
+        r.a = *(const int4*)(rowp + 32 * u);
+        r.b = *((const int4*)(rowp + 32 * u) + 1);
+        r.sc = ((const float*)auxp)[(32 * u) / bs];
+        return dot_i8_q8(r, xp);
+      }
+      default: {
+        Unit<SM_Q4_0>::Raw r;
+        r.q = *(const int4*)(rowp + 16 * u);
+        r.sc = ((const float*)auxp)[(32 * u) / bs];
+        return dot_i8_q4_0(r, xp);
+      }
+    }
+  }
+
+  static __device__ GemvSeg to_gemv(const MegaSeg& s) {
+    GemvSeg g;
+    g.fmt = s.fmt;
+    g.rows = s.rows;
+    g.bs = s.bs;
+    g.aux_bpr = s.aux_bpr;
+    g.aux_stride = s.aux_stride;
+    g.mode = s.mode;
+    g.data = s.data;
+    g.aux = s.aux;
+    g.data2 = s.data2;
+    g.aux2 = s.aux2;
+    g.y = s.y;
+    return g;
+  }
+
+  // GEMV rows of this CTA for one segment; `amax` (head only) tracks the local argmax.
+  __device__ bool seg(const MegaSeg& s, int K, int /*rb*/, float* amax_v = nullptr, int* amax_i = nullptr) {
+    const int rb = stage_rows(s, K, slot_bytes);
+    int r0, r1;
+    seg_rows(s.rows, blockIdx.x, gridDim.x, r0, r1);
+    const int nout = r1 - r0;
+    const int64_t rbytes = row_bytes_fmt(s.fmt, K);
+    const bool glu = s.mode == GEMV_GLU;
+    const GemvSeg g = to_gemv(s);
+    if ((s.fmt != SM_Q8_0) != pair) load_x(x_src, x_gamma, x_K, s.fmt != SM_Q8_0);
+    stamp();
+    for (int row = r0; row < r1; row += rb) {
+      const int n = min(rb, r1 - row);
+      const int slot = k % a.nslots;
+      if (!mbar_wait_bounded(&sh.full[slot], (k / a.nslots) & 1, a.status)) {
+        sh.abort = 1;
+        return false;
+      }
+      if (row == r0) stamp();
+      const uint8_t* st = ring + slot * slot_bytes;
+      const uint8_t* sa = st + (glu ? 2 : 1) * rb * rbytes;  // staged scales / d
+      const int64_t arb = aux_row_bytes(s);
+      const int nrows = glu ? 2 * n : n;
+      if (ph < P)  // warp-uniform; four independent rows per pass for instruction-level parallelism
+        for (int sr0 = ph; sr0 < nrows; sr0 += 4 * P) {
+          float v[4];
+          int pidx[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int sr = sr0 + q * P;
+            v[q] = 0.f;
+            pidx[q] = -1;
+            if (sr < nrows) {
+              const bool up = glu && sr >= n;
+              const int lr = up ? sr - n : sr;
+              const int srow = up ? rb + lr : lr;
+              if (u_ok) v[q] = dot(s.fmt, s.bs, st + (int64_t)srow * rbytes, sa + (int64_t)srow * arb);
+              pidx[q] = ((up ? nout : 0) + (row - r0) + lr) * nwpp + ((tid >> 5) % nwpp);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[q] = warp_sum(v[q]);
+          if ((tid & 31) == 0)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (pidx[q] >= 0) part[pidx[q]] = v[q];
+        }
+      __syncwarp();
+      if ((tid & 31) == 0) mbar_arrive(&sh.empty[slot]);
+      ++k;
+    }
+    if (r0 == r1) stamp();
+    stamp();
+    cons_sync();
+    const bool pairs = s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE;
+    const int nitems = pairs ? (nout + 1) / 2 : nout;
+    const int lane = tid & 31, warp = tid >> 5;
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int it = tid; it < nitems; it += CT) {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      int rin[2] = {it, 0};
+      int nr = 1;
+      if (glu) {
+        rin[1] = nout + it;
+        nr = 2;
+      } else if (pairs) {
+        rin[0] = 2 * it;
+        rin[1] = 2 * it + 1;
+        nr = (2 * it + 1 < nout) ? 2 : 1;
+      }
+      for (int q = 0; q < nr; ++q) {
+        float t = 0.f;
+        for (int j = 0; j < nwpp; ++j) t += part[rin[q] * nwpp + j];
+        v[q] = t;
+      }
+      if (glu)
+        group_store<2>(ep, g, r0 + it, v);
+      else if (pairs)
+        group_store<2>(ep, g, (r0 >> 1) + it, v);
+      else
+        group_store<1>(ep, g, r0 + it, v);
+      if (amax_v && (v[0] > bv || (v[0] == bv && r0 + it < bi))) {
+        bv = v[0];
+        bi = r0 + it;
+      }
+    }
+    if (amax_v) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        sh.red[warp] = bv;
+        ((int*)sh.vec)[warp] = bi;
+      }
+    }
+    cons_sync();
+    if (amax_v && tid == 0) {
+      for (int w = 0; w < CWARPS; ++w) {
+        const float ov = sh.red[w];
+        const int oi = ((int*)sh.vec)[w];
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      *amax_v = bv;
+      *amax_i = bi;
+    }
+    return true;
+  }
+
+  // ---- attention, phase A: scores and slice max of item (kv head g, chunk c)
+  __device__ void attn_scores(const MegaLayer& L, int g, int c, int chunks, int len) {
+    const int G = a.nH / a.nKv, HD = 64;
+    const int per = (len + chunks - 1) / chunks;
+    const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
+    float* qs = part;  // [G][64]
+    for (int t = tid; t < G * HD; t += CT) qs[t] = __ldcg(&a.q[g * G * HD + t]);
+    cons_sync();
+    const int64_t seq = *a.seq;
+    const float* kb = L.kc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
+    const int sub = tid & 7, slot = tid >> 3;  // 60 key slots
+    constexpr int SLOTS = CT / 8;
+    float lmax[MGMAX];
+#pragma unroll
+    for (int h = 0; h < MGMAX; ++h) lmax[h] = -FLT_MAX;
+    const float scale = 1.0f / sqrtf((float)HD);
+    for (int p = 0; p < (n + SLOTS - 1) / SLOTS; ++p) {
+      const int jj = p * SLOTS + slot;
+      const bool valid = jj < n;
+      float kv[8];
+      if (valid) {
+        const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * HD + sub * 8);
+        const float4 t0 = __ldcg(kp), t1 = __ldcg(kp + 1);
+        kv[0] = t0.x; kv[1] = t0.y; kv[2] = t0.z; kv[3] = t0.w;
+        kv[4] = t1.x; kv[5] = t1.y; kv[6] = t1.z; kv[7] = t1.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kv[i] = 0.f;
+      }
+#pragma unroll
+      for (int h = 0; h < MGMAX; ++h) {
+        if (h >= G) break;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s = fmaf(qs[h * HD + sub * 8 + i], kv[i], s);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        if (valid) {
+          if (sub == 0) a.scores[(int64_t)(g * G + h) * a.max_ctx + j0 + jj] = s;
+          lmax[h] = fmaxf(lmax[h], __fmul_rn(s, scale));
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < MGMAX; ++h) {
+      const float m = warp_max(lmax[h]);
+      if ((tid & 31) == 0) sh.red[(tid >> 5) * MGMAX + h] = m;
+    }
+    cons_sync();
+    if (tid < G) {
+      float m = -FLT_MAX;
+      for (int w = 0; w < CWARPS; ++w) m = fmaxf(m, sh.red[w * MGMAX + tid]);
+      a.cmax[(g * chunks + c) * G + tid] = m;
+    }
+    cons_sync();
+  }
+
+  // ---- attention, phase B: e = FastExp(s*scale - max), partial sums, last CTA of the head combines
+  __device__ void attn_pv(const MegaLayer& L, int g, int c, int chunks, int len) {
+    const int G = a.nH / a.nKv, HD = 64;
+    const int per = (len + chunks - 1) / chunks;
+    const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
+    const float scale = 1.0f / sqrtf((float)HD);
+    float* es = part;                    // [G][per]
+    float* pp = part + MGMAX * per;      // [CT/64][G][64]
+    {
+      // exact row max of every head of the group: all chunk maxima, gathered in parallel
+      float* cm = part + MGMAX * per + (CT / 64) * MGMAX * 64;  // [chunks][G]
+      for (int t = tid; t < chunks * G; t += CT) cm[t] = __ldcg(&a.cmax[g * chunks * G + t]);
+      cons_sync();
+      if (tid < G) {
+        float m = -FLT_MAX;
+        for (int cc = 0; cc < chunks; ++cc) m = fmaxf(m, cm[cc * G + tid]);
+        sh.vec[tid] = m;
+      }
+      cons_sync();
+    }
+    for (int t = tid; t < G * n; t += CT) {
+      const int h = t / n, jj = t - h * n;
+      const float s = __ldcg(&a.scores[(int64_t)(g * G + h) * a.max_ctx + j0 + jj]);
+      es[h * per + jj] = pade_exp(__fsub_rn(__fmul_rn(s, scale), sh.vec[h]));
+    }
+    cons_sync();
+    const int64_t seq = *a.seq;
+    const float* vb = L.vc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
+    constexpr int PH = CT / 64;  // 7 key phases
+    // the chunk's V rows (contiguous in the head-major cache) into shared memory in one pass
+    float* vs = part + MGMAX * per + PH * MGMAX * 64 + chunks * G;
+    for (int t = tid; t < n * (HD / 4); t += CT)
+      ((float4*)vs)[t] = __ldcg((const float4*)(vb + (int64_t)j0 * HD) + t);
+    cons_sync();
+    const int d = tid % 64, kp = tid / 64;
+    if (kp < PH) {
+      float acc[MGMAX];
+#pragma unroll
+      for (int h = 0; h < MGMAX; ++h) acc[h] = 0.f;
+      for (int jj = kp; jj < n; jj += PH) {
+        const float v = vs[jj * HD + d];
+#pragma unroll
+        for (int h = 0; h < MGMAX; ++h)
+          if (h < G) acc[h] = fmaf(es[h * per + jj], v, acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < MGMAX; ++h)
+        if (h < G) pp[(kp * MGMAX + h) * 64 + d] = acc[h];
+    }
+    cons_sync();
+    const int base = (g * chunks + c) * G;
+    for (int t = tid; t < G * 64; t += CT) {
+      const int h = t / 64, dd = t - h * 64;
+      float s = 0.f;
+      for (int p = 0; p < PH; ++p) s += pp[(p * MGMAX + h) * 64 + dd];
+      a.pacc[(int64_t)(base + h) * 64 + dd] = s;
+    }
+    if (tid < G) {
+      float s = 0.f;
+      for (int jj = 0; jj < n; ++jj) s += es[tid * per + jj];
+      a.psum[base + tid] = s;
+    }
+    cons_sync();
+  }
+
+  // ---- attention, phase C: out[o] = sum_c pacc / sum_c psum for this CTA's slice of the outputs
+  __device__ void attn_combine(int chunks) {
+    const int G = a.nH / a.nKv, NO = a.nH * 64;
+    const int o0 = (int)((int64_t)NO * blockIdx.x / gridDim.x), o1 = (int)((int64_t)NO * (blockIdx.x + 1) / gridDim.x);
+    const int n = o1 - o0;
+    if (n <= 0) return;
+    float* vals = part;                  // [n][chunks]
+    float* tots = part + n * chunks;     // [2][chunks] partial sums of the (at most two) heads spanned
+    const int h0 = o0 / 64;
+    for (int t = tid; t < n * chunks; t += CT) {
+      const int o = o0 + t / chunks, c = t % chunks;
+      const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
+      vals[t] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
+    }
+    const int nh = (o1 - 1) / 64 - h0 + 1;
+    for (int t = tid; t < nh * chunks; t += CT) {
+      const int h = h0 + t / chunks, c = t % chunks, g = h / G, hh = h % G;
+      tots[t] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
+    }
+    cons_sync();
+    for (int t = tid; t < n; t += CT) {
+      const int o = o0 + t, hi = o / 64 - h0;
+      float s = 0.f, tot = 0.f;
+      for (int c = 0; c < chunks; ++c) {
+        s += vals[t * chunks + c];
+        tot += tots[hi * chunks + c];
+      }
+      a.att[o] = s * __fdiv_rn(1.f, tot);
+    }
+    cons_sync();
+  }
+};
+
+__global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constant__ MegaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Shared& sh = *(Shared*)smem_raw;
+  float* part = (float*)(smem_raw + ((sizeof(Shared) + 127) / 128) * 128);
+  uint8_t* ring = smem_raw + a.ring_offset;
+  const int64_t slot_bytes = (int64_t)(((a.smem_bytes - a.ring_offset) / a.nslots) / 128 * 128);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < a.nslots; ++i) {
+      mbar_init(&sh.full[i], 1);
+      mbar_init(&sh.empty[i], CWARPS);
+    }
+    sh.abort = 0;
+    sh.consumed = 0;
+    sh.phase = -1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int len = a.kv_len[*a.seq] + 1;  // context including this token
+  if (len > a.max_ctx) {
+    if (tid == 0 && blockIdx.x == 0) atomicExch(a.status, SM_ERR_SHAPE);
+    return;
+  }
+  if (warp == CWARPS) {
+    // ------------------------------------------------------------ producer
+    if ((tid & 31) == 0) {
+      Producer p{a, sh, ring, slot_bytes};
+      for (int l = 0; l < a.n_layers; ++l) {
+        const MegaLayer& L = a.layers[l];
+        for (int s = 0; s < 3; ++s) p.seg(L.qkv[s], a.H, a.stage_rows_h, 4 * l);
+        p.seg(L.o, a.qd, a.stage_rows_h, 4 * l + 1);
+        p.seg(L.gu, a.H, a.stage_rows_h, 4 * l + 2);
+        p.seg(L.down, a.F, a.stage_rows_f, 4 * l + 3);
+      }
+      p.seg(a.head, a.H, a.stage_rows_v, 4 * a.n_layers);
+      // drain: wait (bounded) until every stage issued has landed before exiting
+      if (!p.ok) {
+        for (int kk = max(0, p.k - a.nslots); kk < p.k; ++kk)
+          mbar_wait_bounded(&sh.full[kk % a.nslots], (kk / a.nslots) & 1, nullptr);
+      }
+    }
+    return;
+  }
+  // -------------------------------------------------------------- consumers
+  Consumer c{a, sh, ring, slot_bytes, part};
+  c.tid = tid;
+  c.ep.pos = nullptr;
+  c.ep.seq = a.seq;
+  c.ep.head_dim = a.hd;
+  c.ep.n_kv = a.nKv;
+  c.ep.max_ctx = a.max_ctx;
+  // the position of this token = the sequence length before it: kv_len[seq]
+  __shared__ int pos_s;
+  __shared__ float rope_s[2][64];  // sin / cos row of this position (head_dim <= 128)
+  if (tid == 0) pos_s = len - 1;
+  const int half = a.hd / 2;
+  for (int t = tid; t < half; t += CT) {
+    rope_s[0][t] = a.sin_t[(int64_t)(len - 1) * half + t];
+    rope_s[1][t] = a.cos_t[(int64_t)(len - 1) * half + t];
+  }
+  cons_sync();
+  c.ep.pos = &pos_s;
+  // epilogue reads table[pos * half + i]: point at the shared row shifted back by pos * half
+  c.ep.sin_t = &rope_s[0][0] - (int64_t)(len - 1) * half;
+  c.ep.cos_t = &rope_s[1][0] - (int64_t)(len - 1) * half;
+  c.stamp();
+  const float* emb = a.embd + (int64_t)(*a.token) * a.H;
+  if (blockIdx.x == 0)
+    for (int t = tid; t < a.H; t += CT) a.x[t] = emb[t];  // residual stream
+  const int G = a.nH / a.nKv;
+  const int chunks = max(1, (int)gridDim.x / a.nKv);
+  (void)G;
+  for (int l = 0; l < a.n_layers; ++l) {
+    const MegaLayer& L = a.layers[l];
+    // Q|K|V with RMSNorm; RoPE and the KV append in the epilogue
+    if (l > 0 && !c.grid_barrier()) return;
+    // this CTA's attention chunks of the layer: K / V rows into L2 ahead of the attention phases
+    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
+      const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
+      const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
+      const int64_t off = ((int64_t)(*a.seq) * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
+      const int lines = (j1 - j0) * 2;  // 256-byte rows
+      for (int t = tid; t < 2 * lines; t += CT) {
+        const float* base = (t < lines ? L.kc : L.vc) + off;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
+      }
+    }
+    c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, L.qkv[0].fmt != SM_Q8_0);
+    if (tid == 0) sh.phase = 4 * l;
+    for (int s = 0; s < 3; ++s)
+      if (!c.seg(L.qkv[s], a.H, a.stage_rows_h)) return;
+    if (!c.grid_barrier()) return;
+    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
+    if (!c.grid_barrier()) return;
+    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_pv(L, it / chunks, it % chunks, chunks, len);
+    if (!c.grid_barrier()) return;
+    c.attn_combine(chunks);
+    if (!c.grid_barrier()) return;
+    c.load_x(a.att, nullptr, a.qd, L.o.fmt != SM_Q8_0);
+    if (tid == 0) sh.phase = 4 * l + 1;
+    if (!c.seg(L.o, a.qd, a.stage_rows_h)) return;
+    if (!c.grid_barrier()) return;
+    c.load_x(a.x, L.ffn_norm, a.H, L.gu.fmt != SM_Q8_0);
+    if (tid == 0) sh.phase = 4 * l + 2;
+    if (!c.seg(L.gu, a.H, a.stage_rows_h)) return;
+    if (!c.grid_barrier()) return;
+    c.load_x(a.act, nullptr, a.F, L.down.fmt != SM_Q8_0);
+    if (tid == 0) sh.phase = 4 * l + 3;
+    if (!c.seg(L.down, a.F, a.stage_rows_f)) return;
+  }
+  if (!c.grid_barrier()) return;
+  c.load_x(a.x, a.out_norm, a.H, a.head.fmt != SM_Q8_0);
+  if (tid == 0) sh.phase = 4 * a.n_layers;
+  if (!c.seg(a.head, a.H, a.stage_rows_v, &a.amax_val[blockIdx.x], &a.amax_idx[blockIdx.x])) return;
+  c.stamp();
+  // greedy argmax over the CTAs' partial maxima (lowest id on ties); the last CTA commits
+  __threadfence();
+  cons_sync();
+  __shared__ int last_s;
+  if (tid == 0) {
+    const unsigned old = atomicAdd(&a.sync[63], 1u);
+    last_s = old == gridDim.x - 1;
+    __threadfence();
+  }
+  cons_sync();
+  if (last_s && tid < 32) {
+    // the CTA that arrives last reduces every CTA's (max, index) in one warp
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int b = tid; b < (int)gridDim.x; b += 32) {
+      const float v = __ldcg(&a.amax_val[b]);
+      const int i = __ldcg(&a.amax_idx[b]);
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (tid == 0) {
+      *a.next_token = bi;
+      a.kv_len[*a.seq] = len;
+    }
+  }
+}
+
+}  // namespace
+
+int mega_grid_size() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+size_t mega_scratch_floats(int nH, int nKv, int hd, int max_ctx, int grid) {
+  const int chunks = std::max(1, grid / nKv);
+  const int G = nH / nKv;
+  return (size_t)nH * max_ctx + (size_t)nKv * chunks * G * (2 + hd) + 2 * (size_t)grid + 64;
+}
+
+bool mega_supported(const MegaArgs& a) {
+  if (a.hd != 64 || a.nH % a.nKv || a.nH / a.nKv > MGMAX) return false;
+  if ((a.H % 256) || (a.qd % 256) || (a.F % 32)) return false;
+  if (a.H / 32 > CT || a.qd / 32 > CT || a.F / 32 > CT) return false;
+  return true;
+}
+
+bool mega_seg_supported(const MegaSeg& s) {
+  if (s.fmt == SM_Q4_K) return true;
+  return (s.fmt == SM_Q6_K || s.fmt == SM_Q8_0 || s.fmt == SM_Q4_0) && s.aux_stride > 0;
+}
+
+int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch) {
+  const int grid = mega_grid_size();
+  int optin = 0, dev0 = 0;
+  cudaGetDevice(&dev0);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev0);
+  const int smem_total = optin - 1024;  // leave room for the kernel's static shared memory
+  a.smem_bytes = smem_total;
+  // stage rows: ~24 KB per stage
+  auto rb_for = [](int64_t row_bytes, int mult) {
+    return (int)std::max<int64_t>(1, (40 * 1024) / (row_bytes * mult));
+  };
+  // largest staged row (weights + padded scales / d) over the formats
+  auto max_row_bytes = [](int K) {
+    return std::max<int64_t>((int64_t)K / 256 * Q6K_BODY_BYTES + ((int64_t)K / 256 * 2 + 15) / 16 * 16,
+                             (int64_t)K + ((int64_t)K / 32 * 4 + 15) / 16 * 16);
+  };
+  const int64_t rb_h = max_row_bytes(a.H), rb_f = max_row_bytes(a.F);
+  a.stage_rows_h = rb_for(rb_h, 2);
+  a.stage_rows_f = rb_for(rb_f, 1);
+  a.stage_rows_v = rb_for(rb_h, 1);
+  const int64_t slot_need = std::max({rb_h * 2 * a.stage_rows_h, rb_f * a.stage_rows_f, rb_h * a.stage_rows_v});
+  // partials: the most rows any CTA holds in one segment (GLU: gate + up) x units
+  auto cta_rows = [&](int rows) { return 2 * (((rows + 1) / 2 + grid - 1) / grid); };
+  auto nwpp = [](int K) { return (int64_t)((K / 32 + 31) / 32); };
+  const int64_t part = std::max({(int64_t)2 * cta_rows(a.F) * nwpp(a.H), (int64_t)cta_rows(a.qd) * nwpp(a.H),
+                                 (int64_t)cta_rows(a.H) * std::max(nwpp(a.qd), nwpp(a.F)),
+                                 (int64_t)cta_rows(a.V) * nwpp(a.H), (int64_t)MGMAX * (a.max_ctx / 2 + 64) + 4096,
+                                 (int64_t)(MGMAX + 64) * (a.max_ctx / std::max(1, grid / a.nKv) + 2) + 4096 +
+                                     (int64_t)std::max(1, grid / a.nKv) * MGMAX,
+                                 (int64_t)2 * std::max({a.H, a.qd, a.F})});
+  a.part_floats = (int)part;
+  const int shared_bytes = (int)((sizeof(Shared) + 127) / 128 * 128);
+  a.ring_offset = (int)((shared_bytes + part * 4 + 127) / 128 * 128);
+  const int64_t ring = smem_total - a.ring_offset;
+  const int64_t slot = (slot_need + 127) / 128 * 128;
+  a.nslots = (int)std::min<int64_t>(16, ring / slot);
+  if (const char* e = std::getenv("SMALLMIND_MEGA_SLOTS")) a.nslots = std::max(2, std::min(a.nslots, atoi(e)));
+  if (const char* e = std::getenv("SMALLMIND_MEGA_LOOKAHEAD")) a.lookahead = atoi(e);
+  if (a.nslots < 2) return fail(SM_ERR_UNSUPPORTED, "decode_mega: shared memory too small for the stage ring");
+  // the kernel recomputes the slot size as (227 KB - ring_offset) / nslots rounded down to 128 B
+  if ((int64_t)(((smem_total - a.ring_offset) / a.nslots) / 128 * 128) < slot_need)
+    return fail(SM_ERR_UNSUPPORTED, "decode_mega: stage slot too small");
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_total));
+    attr_set[dev] = true;
+  }
+  SM_CUDA_TRY(cudaMemsetAsync(a.sync, 0, 64 * sizeof(unsigned), st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(MT);
+  cfg.dynamicSmemBytes = smem_total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barriers rely on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_mega_kernel, a));
+  if (n_launch) *n_launch += 1;
+  return SM_OK;
+}
+
+}  // namespace sm

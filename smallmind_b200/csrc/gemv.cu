@@ -11,6 +11,8 @@
 // REFERENCE layout (C = A . B, B[K][N]): the orientation the reference kernels
 // are written in (MatMulF32Q8.cs:61-79, FusedQ4KMatMul.cs:122,127).  Kept for
 // op-level parity; one thread per output column.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemv1.cuh"
 
@@ -40,7 +42,7 @@ struct Decoder<SM_Q8_0> {
   __device__ __forceinline__ static void decode(const DevWeight& W, int row, int u, int K, bool literal_kq, int N,
                                                 UnitW& o) {
     const int8_t* q = (const int8_t*)W.data + (int64_t)row * K + 32 * u;
-    const float sc = ((const float*)W.aux)[((int64_t)row * K + 32 * u) / W.block_size];
+    const float sc = ((const float*)W.aux)[aux_idx(((int64_t)row * K + 32 * u) / W.block_size, W.aux_bpr, W.aux_stride)];
     int4 a = __ldg((const int4*)q), b = __ldg((const int4*)q + 1);
     const int v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -56,7 +58,7 @@ struct Decoder<SM_Q4_0> {
   __device__ __forceinline__ static void decode(const DevWeight& W, int row, int u, int K, bool, int, UnitW& o) {
     const int64_t e0 = (int64_t)row * K + 32 * u;
     const uint8_t* q = (const uint8_t*)W.data + e0 / 2;
-    const float sc = ((const float*)W.aux)[e0 / W.block_size];
+    const float sc = ((const float*)W.aux)[aux_idx(e0 / W.block_size, W.aux_bpr, W.aux_stride)];
     int4 a = __ldg((const int4*)q);
     const int v[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
@@ -109,7 +111,7 @@ struct Decoder<SM_Q6_K> {
     const int64_t b = kq_block(row, u >> 3, K, N, literal);
     const uint8_t* blk = (const uint8_t*)W.data + b * Q6K_BODY_BYTES;
     const int j = u & 7;
-    const float d = half_bits_to_float(((const uint16_t*)W.aux)[b]);
+    const float d = half_bits_to_float(((const uint16_t*)W.aux)[aux_idx(b, W.aux_bpr, W.aux_stride)]);
     int4 ql = __ldg((const int4*)(blk + 16 * j));
     int2 qh = __ldg((const int2*)(blk + 128 + 8 * j));
     const unsigned short sc2 = __ldg((const unsigned short*)(blk + 192 + 2 * j));
@@ -202,11 +204,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_rows_kernel(DevWeight W, co
 __device__ __forceinline__ float elem_weight(const DevWeight& W, int64_t li) {
   switch (W.scheme) {
     case SM_Q8_0:
-      return __fmul_rn((float)((const int8_t*)W.data)[li], ((const float*)W.aux)[li / W.block_size]);
+      return __fmul_rn((float)((const int8_t*)W.data)[li], ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)]);
     case SM_Q4_0: {
       const uint8_t p = ((const uint8_t*)W.data)[li >> 1];
       const int nib = (li & 1) ? (p >> 4) : (p & 0xF);
-      return __fmul_rn((float)(nib < 8 ? nib : nib - 16), ((const float*)W.aux)[li / W.block_size]);
+      return __fmul_rn((float)(nib < 8 ? nib : nib - 16), ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)]);
     }
     default:
       return ((const float*)W.data)[li];
@@ -228,12 +230,12 @@ __global__ void matmul_literal_linear_kernel(DevWeight W, const float* __restric
     float q, sc;
     if (W.scheme == SM_Q8_0) {
       q = (float)((const int8_t*)W.data)[li];
-      sc = ((const float*)W.aux)[li / W.block_size];
+      sc = ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)];
     } else if (W.scheme == SM_Q4_0) {
       const uint8_t p = ((const uint8_t*)W.data)[li >> 1];
       const int nib = (li & 1) ? (p >> 4) : (p & 0xF);
       q = (float)(nib < 8 ? nib : nib - 16);
-      sc = ((const float*)W.aux)[li / W.block_size];
+      sc = ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)];
     } else {
       q = ((const float*)W.data)[li];
       sc = 1.f;
@@ -311,6 +313,11 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     a.K = K;
     a.x = x;
     SM_TRY(gemv1_segment(a, W, nullptr, y, accumulate ? GEMV_ADD : GEMV_STORE));
+    const char* e = std::getenv("SMALLMIND_GEMV_STREAM");
+    if (e && e[0] == '1') {
+      const int rc = launch_gemv_stream(a, nullptr, st, n_launch);
+      if (rc != SM_ERR_UNSUPPORTED) return rc;
+    }
     return launch_gemv1(a, st, n_launch);
   }
   const bool fast = kq || (K % 32 == 0 && (W.scheme == SM_F32 || W.block_size % 32 == 0));

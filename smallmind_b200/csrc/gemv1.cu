@@ -200,6 +200,8 @@ int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y
   s.fmt = w.scheme;
   s.rows = w.rows;
   s.bs = w.block_size;
+  s.aux_bpr = w.aux_bpr;
+  s.aux_stride = w.aux_stride;
   s.mode = mode;
   s.data = (const uint8_t*)w.data;
   s.aux = w.aux;

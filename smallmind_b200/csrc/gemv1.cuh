@@ -12,6 +12,7 @@ enum { GEMV_STORE = 0, GEMV_ADD = 1, GEMV_GLU = 2, GEMV_ROPE_Q = 3, GEMV_ROPE_K_
 
 struct GemvSeg {
   int fmt = 0, rows = 0, bs = 0, mode = 0;
+  int aux_bpr = 0, aux_stride = 0;  // DevWeight::aux_bpr / aux_stride
   const uint8_t* data = nullptr;
   const void* aux = nullptr;
   const uint8_t* data2 = nullptr;  // GLU: the up-projection weight (same scheme and shape)

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "gemv1.cuh"
 #include "gemv_units.cuh"
+#include "mbar.cuh"
 
 namespace sm {
 namespace {
@@ -25,48 +26,6 @@ namespace {
 constexpr int ST_THREADS = 512;
 constexpr int ST_WARPS = ST_THREADS / 32;
 constexpr int MAX_STAGE_ROWS = 16;  // rows in one stage (GLU: gate + up rows)
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: gives up after ~2 s of clock64 time and reports SM_ERR_TIMEOUT.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > 4000000000LL) {
-      if (status) atomicExch(status, SM_ERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
-}
 
 __device__ __forceinline__ int64_t row_bytes_of(int fmt, int K) {
   switch (fmt) {
@@ -120,10 +79,6 @@ __device__ __forceinline__ float unit_dot_smem(const GemvSeg& s, const uint8_t* 
   typename Unit<FMT>::Raw raw;
   Unit<FMT>::load_row(s, rowp, grow, u, K, up, raw);
   return Unit<FMT>::dot(raw, u & 7, xr, xa, xb);
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Warp 15 produces (bulk copies into the ring), warps 0..14 consume.  full[s]

@@ -73,7 +73,7 @@ struct Unit<SM_Q6_K> {
     r.ql = __ldg((const int4*)(blk + 16 * j));
     r.qh = __ldg((const int2*)(blk + 128 + 8 * j));
     r.sc = __ldg((const unsigned short*)(blk + 192 + 2 * j));
-    r.d = __ldg((const unsigned short*)s.aux + b);
+    r.d = __ldg((const unsigned short*)s.aux + aux_idx(b, s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static void load_row(const GemvSeg& s, const uint8_t* rowp, int row, int u, int K,
                                                   bool up, Raw& r) {
@@ -82,7 +82,8 @@ struct Unit<SM_Q6_K> {
     r.ql = *(const int4*)(blk + 16 * j);
     r.qh = *(const int2*)(blk + 128 + 8 * j);
     r.sc = *(const unsigned short*)(blk + 192 + 2 * j);
-    r.d = __ldg((const unsigned short*)(up ? s.aux2 : s.aux) + (int64_t)row * (K >> 8) + (u >> 3));
+    r.d = __ldg((const unsigned short*)(up ? s.aux2 : s.aux) +
+                aux_idx((int64_t)row * (K >> 8) + (u >> 3), s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static float half16(uint32_t w0, uint32_t w1, uint32_t W, const float* x) {
     // elements 0..7 from w0, 8..15 from w1; byte b of W holds highs of 2b, 2b+1, 8+2b, 9+2b
@@ -120,13 +121,13 @@ struct Unit<SM_Q8_0> {
     const int64_t e0 = (int64_t)row * K + 32 * u;
     r.a = __ldg((const int4*)(s.data + e0));
     r.b = __ldg((const int4*)(s.data + e0) + 1);
-    r.sc = __ldg((const float*)s.aux + e0 / s.bs);
+    r.sc = __ldg((const float*)s.aux + aux_idx(e0 / s.bs, s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static void load_row(const GemvSeg& s, const uint8_t* rowp, int row, int u, int K,
                                                   bool up, Raw& r) {
     r.a = *(const int4*)(rowp + 32 * u);
     r.b = *((const int4*)(rowp + 32 * u) + 1);
-    r.sc = __ldg((const float*)(up ? s.aux2 : s.aux) + ((int64_t)row * K + 32 * u) / s.bs);
+    r.sc = __ldg((const float*)(up ? s.aux2 : s.aux) + aux_idx(((int64_t)row * K + 32 * u) / s.bs, s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float, float) {
     const uint32_t w[8] = {(uint32_t)r.a.x, (uint32_t)r.a.y, (uint32_t)r.a.z, (uint32_t)r.a.w,
@@ -158,12 +159,12 @@ struct Unit<SM_Q4_0> {
   __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
     const int64_t e0 = (int64_t)row * K + 32 * u;
     r.q = __ldg((const int4*)(s.data + (e0 >> 1)));
-    r.sc = __ldg((const float*)s.aux + e0 / s.bs);
+    r.sc = __ldg((const float*)s.aux + aux_idx(e0 / s.bs, s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static void load_row(const GemvSeg& s, const uint8_t* rowp, int row, int u, int K,
                                                   bool up, Raw& r) {
     r.q = *(const int4*)(rowp + 16 * u);
-    r.sc = __ldg((const float*)(up ? s.aux2 : s.aux) + ((int64_t)row * K + 32 * u) / s.bs);
+    r.sc = __ldg((const float*)(up ? s.aux2 : s.aux) + aux_idx(((int64_t)row * K + 32 * u) / s.bs, s.aux_bpr, s.aux_stride));
   }
   __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float x16a, float x16b) {
     const uint32_t w[4] = {(uint32_t)r.q.x, (uint32_t)r.q.y, (uint32_t)r.q.z, (uint32_t)r.q.w};
@@ -239,9 +240,146 @@ __device__ __forceinline__ void group_store(const GemvArgs& a, const GemvSeg& s,
   for (int r = 0; r < R; ++r) {
     const int row = row0 + r;
     if (row >= s.rows) continue;
-    s.y[row] = s.mode == GEMV_ADD ? s.y[row] + v[r] : v[r];
+    s.y[row] = s.mode == GEMV_ADD ? __ldcg(&s.y[row]) + v[r] : v[r];
   }
 }
 
+
+}  // namespace sm
+
+namespace sm {
+
+// ---------------------------------------------------------------------------
+// Integer dot path.  The 32 activations of a unit become 24-bit fixed point
+// with one power-of-two exponent per unit, X_i = round(x_i * 2^(23-e)), split
+// into three byte planes X = a*2^16 + b*2^8 + c (a signed, b and c unsigned).
+// The packed weights' integer codes then meet the planes in dp4a (exact int32
+// sums), and sum(q x) = 2^(e-23) * (A*65536 + B*256 + C).  Rounding x to 24
+// bits relative to the unit's largest |x| keeps the result well inside the
+// 1e-4 GEMV tolerance.
+//
+// PAIR packing (Q4_K, Q4_0, Q6_K code words): plane words 0..3 hold elements
+// 8i, 8i+2, 8i+4, 8i+6 (low nibbles of code word i), words 4..7 elements
+// 8i+1, ... (high nibbles).  NATURAL packing (Q8_0): word i = elements 4i..4i+3.
+struct XPlanes {
+  uint32_t a[8], b[8], c[8];
+  float inv;        // 2^(e-23)
+  float x16a, x16b; // sums of x over elements 0..15 and 16..31 (exact-order fp32)
+};
+
+__device__ __forceinline__ void make_planes(const float* x, bool pair, XPlanes& p) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+  int ex = 0;
+  frexpf(amax, &ex);  // amax < 2^ex
+  const float up = ldexpf(1.f, 23 - ex);
+  p.inv = ldexpf(1.f, ex - 23);
+  int X[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) X[i] = amax > 0.f ? __float2int_rn(x[i] * up) : 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    int e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = pair ? (8 * (w & 3) + 2 * j + (w >> 2)) : (4 * w + j);
+    // byte 2 / 1 / 0 of four 32-bit values -> one word per plane
+    const uint32_t x0 = X[e[0]], x1 = X[e[1]], x2 = X[e[2]], x3 = X[e[3]];
+    p.a[w] = __byte_perm(__byte_perm(x0, x1, 0x0062), __byte_perm(x2, x3, 0x0062), 0x5410);
+    p.b[w] = __byte_perm(__byte_perm(x0, x1, 0x0051), __byte_perm(x2, x3, 0x0051), 0x5410);
+    p.c[w] = __byte_perm(__byte_perm(x0, x1, 0x0040), __byte_perm(x2, x3, 0x0040), 0x5410);
+  }
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    s0 += x[i];
+    s1 += x[16 + i];
+  }
+  p.x16a = s0;
+  p.x16b = s1;
+}
+
+// dp4a with a signed first operand (weight codes) and a signed / unsigned plane
+__device__ __forceinline__ int dp_ss(uint32_t q, uint32_t a, int acc) {
+  int r;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(a), "r"(acc));
+  return r;
+}
+__device__ __forceinline__ int dp_su(uint32_t q, uint32_t b, int acc) {
+  int r;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(b), "r"(acc));
+  return r;
+}
+
+struct IAcc {
+  int A = 0, B = 0, C = 0;
+  __device__ __forceinline__ void add(uint32_t q, const XPlanes& p, int w) {
+    A = dp_ss(q, p.a[w], A);
+    B = dp_su(q, p.b[w], B);
+    C = dp_su(q, p.c[w], C);
+  }
+  __device__ __forceinline__ float value(float inv) const {
+    return inv * fmaf((float)A, 65536.f, fmaf((float)B, 256.f, (float)C));
+  }
+};
+
+// sum over the unit of (code * x) for each format; codes as in the reference:
+// Q4_K q in [0,15]; Q6_K q in [0,63] per 16-element half; Q8_0 q in [-127,127];
+// Q4_0 nibble + 8 in [0,15].
+__device__ __forceinline__ float dot_i8_q4k(const Unit<SM_Q4_K>::Raw& r, int j, const XPlanes& p) {
+  const float d = __half2float(__ushort_as_half((unsigned short)(r.hdr.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)((uint32_t)r.hdr.x >> 16)));
+  const uint64_t sb = (uint32_t)r.hdr.y | ((uint64_t)((uint32_t)r.hdr.z & 0xFFFFu) << 32);
+  const uint64_t mb = ((uint32_t)r.hdr.z >> 16) | ((uint64_t)(uint32_t)r.hdr.w << 16);
+  const float sc = d * (float)((sb >> (6 * j)) & 63);
+  const float mn = dmin * (float)((mb >> (6 * j)) & 63);
+  const uint32_t w[4] = {(uint32_t)r.qs.x, (uint32_t)r.qs.y, (uint32_t)r.qs.z, (uint32_t)r.qs.w};
+  IAcc acc;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc.add(w[i] & 0x0F0F0F0Fu, p, i);
+    acc.add((w[i] >> 4) & 0x0F0F0F0Fu, p, 4 + i);
+  }
+  return sc * acc.value(p.inv) - mn * (p.x16a + p.x16b);
+}
+
+__device__ __forceinline__ float dot_i8_q6k(const Unit<SM_Q6_K>::Raw& r, const XPlanes& p) {
+  const float d = __half2float(__ushort_as_half(r.d));
+  const float sa = d * (float)(int8_t)(r.sc & 0xFF), sb = d * (float)(int8_t)(r.sc >> 8);
+  const uint32_t w0 = r.ql.x, w1 = r.ql.y, w2 = r.ql.z, w3 = r.ql.w;
+  const uint32_t W0 = r.qh.x, W1 = r.qh.y;
+  // byte b of W holds the highs of elements 2b, 2b+1, 8+2b, 9+2b of its 16-element half
+  IAcc h0, h1;
+  h0.add((w0 & 0x0F0F0F0Fu) | ((W0 << 4) & 0x30303030u), p, 0);
+  h0.add(((w0 >> 4) & 0x0F0F0F0Fu) | ((W0 << 2) & 0x30303030u), p, 4);
+  h0.add((w1 & 0x0F0F0F0Fu) | (W0 & 0x30303030u), p, 1);
+  h0.add(((w1 >> 4) & 0x0F0F0F0Fu) | ((W0 >> 2) & 0x30303030u), p, 5);
+  h1.add((w2 & 0x0F0F0F0Fu) | ((W1 << 4) & 0x30303030u), p, 2);
+  h1.add(((w2 >> 4) & 0x0F0F0F0Fu) | ((W1 << 2) & 0x30303030u), p, 6);
+  h1.add((w3 & 0x0F0F0F0Fu) | (W1 & 0x30303030u), p, 3);
+  h1.add(((w3 >> 4) & 0x0F0F0F0Fu) | ((W1 >> 2) & 0x30303030u), p, 7);
+  return sa * (h0.value(p.inv) - 32.f * p.x16a) + sb * (h1.value(p.inv) - 32.f * p.x16b);
+}
+
+__device__ __forceinline__ float dot_i8_q8(const Unit<SM_Q8_0>::Raw& r, const XPlanes& p) {
+  const uint32_t w[8] = {(uint32_t)r.a.x, (uint32_t)r.a.y, (uint32_t)r.a.z, (uint32_t)r.a.w,
+                         (uint32_t)r.b.x, (uint32_t)r.b.y, (uint32_t)r.b.z, (uint32_t)r.b.w};
+  IAcc acc;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc.add(w[i], p, i);
+  return r.sc * acc.value(p.inv);
+}
+
+__device__ __forceinline__ float dot_i8_q4_0(const Unit<SM_Q4_0>::Raw& r, const XPlanes& p) {
+  const uint32_t w[4] = {(uint32_t)r.q.x, (uint32_t)r.q.y, (uint32_t)r.q.z, (uint32_t)r.q.w};
+  IAcc acc;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t v = w[i] ^ 0x88888888u;  // nibble + 8
+    acc.add(v & 0x0F0F0F0Fu, p, i);
+    acc.add((v >> 4) & 0x0F0F0F0Fu, p, 4 + i);
+  }
+  return r.sc * (acc.value(p.inv) - 8.f * (p.x16a + p.x16b));
+}
 
 }  // namespace sm

@@ -7,19 +7,19 @@ namespace {
 // ---------------------------------------------------------------- dequant
 // Q8Tensor.cs:131-158: w = (float)q * scale.
 __global__ void dequant_q8_kernel(const int8_t* __restrict__ q, const float* __restrict__ scales, int64_t n, int bs,
-                                  float* __restrict__ out) {
+                                  int bpr, int stride, float* __restrict__ out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = __fmul_rn((float)q[i], scales[i / bs]);
+    out[i] = __fmul_rn((float)q[i], scales[aux_idx(i / bs, bpr, stride)]);
 }
 
 // Q4Tensor.cs:150-179: nibble by global index (even low), two's complement, * scale.
 __global__ void dequant_q4_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scales, int64_t n, int bs,
-                                  float* __restrict__ out) {
+                                  int bpr, int stride, float* __restrict__ out) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     uint8_t p = q[i >> 1];
     int nib = (i & 1) ? (p >> 4) : (p & 0xF);
     int v = nib < 8 ? nib : nib - 16;
-    out[i] = __fmul_rn((float)v, scales[i / bs]);
+    out[i] = __fmul_rn((float)v, scales[aux_idx(i / bs, bpr, stride)]);
   }
 }
 
@@ -54,11 +54,11 @@ __device__ __forceinline__ int q6k_high2(const uint8_t* qhp, int v) {
 }
 
 __global__ void dequant_q6k_kernel(const uint8_t* __restrict__ body, const uint16_t* __restrict__ dv, int64_t nblocks,
-                                   float* __restrict__ out) {
+                                   int bpr, int stride, float* __restrict__ out) {
   const int v = threadIdx.x;  // 256 threads, one per element
   for (int64_t b = blockIdx.x; b < nblocks; b += gridDim.x) {
     const uint8_t* blk = body + b * Q6K_BODY_BYTES;
-    const float d = half_bits_to_float(dv[b]);
+    const float d = half_bits_to_float(dv[aux_idx(b, bpr, stride)]);
     const int8_t scale = (int8_t)blk[192 + v / 16];
     const float s = __fmul_rn(d, (float)scale);
     const uint8_t qlb = blk[v >> 1];
@@ -81,7 +81,7 @@ __global__ void dequant_f32_kernel(const float* __restrict__ w, int64_t n, float
 // byte b of the matching ql words, so the GEMV builds four 6-bit values with a
 // few shifts and masks per 32-bit word.
 __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ body,
-                                    uint16_t* __restrict__ dv, int64_t nblocks) {
+                                    uint16_t* __restrict__ dv, int64_t nblocks, int bpr, int stride) {
   for (int64_t b = blockIdx.x; b < nblocks; b += gridDim.x) {
     const uint8_t* s = src + b * Q6K_BLOCK_BYTES;
     uint8_t* o = body + b * Q6K_BODY_BYTES;
@@ -95,7 +95,7 @@ __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ src, uint8_t* __
         o[i] = (uint8_t)(h(v0) | (h(v0 + 1) << 2) | (h(v0 + 8) << 4) | (h(v0 + 9) << 6));
       }
     }
-    if (threadIdx.x == 0) dv[b] = (uint16_t)s[208] | ((uint16_t)s[209] << 8);
+    if (threadIdx.x == 0) dv[aux_idx(b, bpr, stride)] = (uint16_t)s[208] | ((uint16_t)s[209] << 8);
   }
 }
 
@@ -282,18 +282,18 @@ int launch_dequant(const DevWeight& w, float* out, cudaStream_t st) {
   switch (w.scheme) {
     case SM_Q8_0:
       dequant_q8_kernel<<<grid_for(w.n, 256), 256, 0, st>>>((const int8_t*)w.data, (const float*)w.aux, w.n,
-                                                             w.block_size, out);
+                                                             w.block_size, w.aux_bpr, w.aux_stride, out);
       break;
     case SM_Q4_0:
       dequant_q4_kernel<<<grid_for(w.n, 256), 256, 0, st>>>((const uint8_t*)w.data, (const float*)w.aux, w.n,
-                                                             w.block_size, out);
+                                                             w.block_size, w.aux_bpr, w.aux_stride, out);
       break;
     case SM_Q4_K:
       dequant_q4k_kernel<<<grid_for(w.n / 256, 1), 128, 0, st>>>((const uint8_t*)w.data, w.n / 256, out);
       break;
     case SM_Q6_K:
       dequant_q6k_kernel<<<grid_for(w.n / 256, 1), 256, 0, st>>>((const uint8_t*)w.data, (const uint16_t*)w.aux,
-                                                                  w.n / 256, out);
+                                                                  w.n / 256, w.aux_bpr, w.aux_stride, out);
       break;
     case SM_F32:
       dequant_f32_kernel<<<grid_for(w.n, 256), 256, 0, st>>>((const float*)w.data, w.n, out);
@@ -305,8 +305,9 @@ int launch_dequant(const DevWeight& w, float* out, cudaStream_t st) {
   return SM_OK;
 }
 
-int launch_q6k_relayout(const uint8_t* src, uint8_t* body, uint16_t* d, int64_t nblocks, cudaStream_t st) {
-  q6k_relayout_kernel<<<grid_for(nblocks, 1), 64, 0, st>>>(src, body, d, nblocks);
+int launch_q6k_relayout(const uint8_t* src, uint8_t* body, uint16_t* d, int64_t nblocks, int bpr, int stride,
+                        cudaStream_t st) {
+  q6k_relayout_kernel<<<grid_for(nblocks, 1), 64, 0, st>>>(src, body, d, nblocks, bpr, stride);
   SM_CUDA_TRY(cudaGetLastError());
   return SM_OK;
 }
