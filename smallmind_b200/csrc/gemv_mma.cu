@@ -1,0 +1,334 @@
+// Decode GEMV (M = 1) for Q4_K on the integer tensor-core path.
+//
+// One mma.sync.m16n8k32 (u8 x s8 -> s32) covers one 32-weight unit (one Q4_K
+// sub-block) of 16 rows.  Lane (g, tig) owns code word tig of the unit for rows
+// g and g + 8: byte i of the word holds the codes of elements 8 tig + 2i (low
+// nibble, lo) and 8 tig + 2i + 1 (high nibble, hi).  The A fragment takes the
+// word twice: masked to its low nibbles at k = 4 tig + i, and unchanged
+// (lo + 16 hi) at k = 16 + 4 tig + i, so no unpacking beyond one AND.  The
+// matching B values are, with x in fixed point relative to the largest |x| of
+// its 256-element block (one power-of-two exponent e per block),
+//   at k = 16 + 4 tig + i:  H = round(x_hi * 2^(17-e))
+//   at k =      4 tig + i:  L - H,  L = round(x_lo * 2^(21-e))
+// so that lo (L - H) + (lo + 16 hi) H = lo L + hi (16 H): the exact integer
+// dot of the codes with x at 21 bits (low elements) and 17 bits (high).  The
+// B values are split into three signed 8-bit digits v = a*2^16 + b*2^8 + c
+// held in B columns 0..2, giving integer sums A_j, B_j, C_j per row and unit j.
+// The reference element formula (Q4KTensor.cs:129-147), w = d s_j q - dmin m_j,
+// then gives per row and block
+//   sum_k w_k x_k ~= d 2^(e-21) sum_j s_j (A_j 65536 + B_j 256 + C_j)
+//                    - dmin sum_j m_j (sum of x over unit j),
+// with the six-bit s_j multiplying the digit sums in integer arithmetic.
+// The x rounding stays far inside the 1e-4 GEMV tolerance.  (The 4-bit
+// m16n8k64 form would take the code words as they are, but runs at half this
+// speed on sm_100a.)
+//
+// One persistent CTA per SM owns a contiguous range of 16-row tiles: warp 15
+// brings each tile (one bulk copy per row, rows padded apart so the fragment
+// loads are free of bank conflicts) into a shared-memory ring, issued before
+// the PDL wait.  The other warps take the (tile, 256-weight block) items in turn
+// with no CTA-wide barrier; each writes its block partials and arrives on the
+// slot's empty barrier, and the producer warp, once all have arrived, sums the
+// partials in block order (deterministic), stores y and refills the slot.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv1.cuh"
+#include "mbar.cuh"
+
+namespace sm {
+namespace {
+
+constexpr int MM_THREADS = 768;
+constexpr int MM_CWARPS = MM_THREADS / 32 - 1;
+constexpr int MM_CT = MM_CWARPS * 32;
+constexpr int ROWS = 16;  // rows per stage (one MMA tile)
+
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(MM_CT) : "memory"); }
+
+// D = A B (zero accumulator input)
+__device__ __forceinline__ void mma_u8s8(int& d0, int& d1, int& d2, int& d3, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  const int z = 0;
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+}
+
+struct MmaArgs {
+  const uint8_t* w = nullptr;  // Q4_K rows (INTENDED layout)
+  const float* x = nullptr;
+  float* y = nullptr;
+  int N = 0, K = 0, accumulate = 0;
+  int nslots = 2;
+  int row_stride = 0;  // bytes between rows in a ring slot (row bytes + 16 or 32: no bank conflicts)
+  int64_t slot_bytes = 0;
+  int plane_offset = 0, red_offset = 0, scw_offset = 0, ring_offset = 0;
+  int* status = nullptr;
+};
+
+constexpr int SCW = 9;  // per-warp scale scratch row stride (floats): rows g = 0..7 on distinct banks
+
+__global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __grid_constant__ MmaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = (uint64_t*)smem;  // [8]
+  uint64_t* empty = full + 8;        // [8]
+  uint32_t* planes = (uint32_t*)(smem + a.plane_offset);  // [U][3][4][2] words, then usum, bexp
+  float* red = (float*)(smem + a.red_offset);             // [nslots][NB][ROWS] block partials
+  float* scw_all = (float*)(smem + a.scw_offset);         // [MM_CWARPS][ROWS * SCW + 2 * ROWS]
+  uint8_t* ring = smem + a.ring_offset;
+  const int K = a.K, U = K >> 5, NB = K >> 8;
+  const uint32_t rbytes = (uint32_t)NB * Q4K_BLOCK_BYTES;
+  const int rs = a.row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ngroups = (a.N + ROWS - 1) / ROWS;
+  const int g0 = (int)((int64_t)ngroups * blockIdx.x / gridDim.x);
+  const int g1 = (int)((int64_t)ngroups * (blockIdx.x + 1) / gridDim.x);
+  const int nst = g1 - g0;
+  float* usum = (float*)(planes + U * 24);  // [U] sum of x over the unit
+  float* bexp = usum + U;                   // [NB] 2^(e-21) of the block
+  if (tid == 0) {
+    for (int i = 0; i < a.nslots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NB);  // one arrival per (tile, block) item
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == MM_CWARPS) {
+    // producer: one bulk copy per row into the padded slot (the weights do not
+    // depend on the previous kernel, so this starts before the PDL wait); once
+    // every block item of a tile has arrived on the slot's empty barrier, sum
+    // the block partials in block order (deterministic), store y, refill.
+    auto issue = [&](int k) {
+      const int slot = k % a.nslots;
+      const int row = (g0 + k) * ROWS;
+      const int n = min(ROWS, a.N - row);
+      if (lane == 0) mbar_expect_tx(&full[slot], (uint32_t)n * rbytes);
+      __syncwarp();
+      if (lane < n)
+        bulk_g2s(ring + slot * a.slot_bytes + lane * rs, a.w + (int64_t)(row + lane) * rbytes, rbytes, &full[slot]);
+    };
+    int next = 0;
+    for (; next < min(nst, a.nslots); ++next) issue(next);
+    if (lane == 0) asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // y may be the previous kernel's output
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int k = 0; k < nst; ++k) {
+      if (!mbar_wait_bounded(&empty[slot], phase, a.status)) return;
+      const int row0 = (g0 + k) * ROWS;
+      const int n = min(ROWS, a.N - row0);
+      if (lane < n) {
+        const float* rd = red + (slot * NB) * ROWS + lane;
+        float s = 0.f;
+        for (int b = 0; b < NB; ++b) s += rd[b * ROWS];
+        float* dst = a.y + row0 + lane;
+        *dst = a.accumulate ? *dst + s : s;
+      }
+      __syncwarp();
+      if (next < nst) issue(next++);
+      if (++slot == a.nslots) slot = 0, phase ^= 1;
+    }
+    return;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // ---- digit planes of x: one warp per 256-element block, four lanes per
+  // unit, eight elements per lane; one exponent per block
+  for (int blk = warp; blk < NB; blk += MM_CWARPS) {
+    const int u = blk * 8 + (lane >> 2), p = lane & 3;
+    const float4* xp = (const float4*)(a.x + 32 * u + 8 * p);
+    const float4 v0 = __ldcg(xp), v1 = __ldcg(xp + 1);
+    const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float amax = 0.f, sx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      amax = fmaxf(amax, fabsf(xv[i]));
+      sx += xv[i];
+    }
+    sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+    sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+    amax = warp_max(amax);
+    int ex = 0;
+    frexpf(amax, &ex);  // amax < 2^ex
+    const float up = ldexpf(1.f, 21 - ex), uph = ldexpf(1.f, 17 - ex);
+    // B fragment of lane (column q, tig): word 0 = values at k = 4 tig + i,
+    // word 1 = values at k = 16 + 4 tig + i; stored together at [u][q][tig][2]
+    uint32_t pw[2][3] = {};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int L = amax > 0.f ? __float2int_rn(xv[2 * i] * up) : 0;       // |L| <= 2^21
+      const int H = amax > 0.f ? __float2int_rn(xv[2 * i + 1] * uph) : 0;  // |H| <= 2^17
+      const int v2[2] = {L - H, H};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int X = v2[h];
+        const int c = ((X + 128) & 255) - 128;
+        const int X1 = (X - c) >> 8;
+        const int b = ((X1 + 128) & 255) - 128;
+        const int hi = (X1 - b) >> 8;
+        pw[h][0] |= (uint32_t)(hi & 255) << (8 * i);
+        pw[h][1] |= (uint32_t)(b & 255) << (8 * i);
+        pw[h][2] |= (uint32_t)(c & 255) << (8 * i);
+      }
+    }
+    uint2* d = (uint2*)(planes + u * 24) + p;
+#pragma unroll
+    for (int q = 0; q < 3; ++q) d[4 * q] = make_uint2(pw[0][q], pw[1][q]);
+    if (p == 0) usum[u] = sx;
+    if (lane == 0) bexp[blk] = ldexpf(1.f, ex - 21);
+  }
+  csync();
+  const int g = lane >> 2, tig = lane & 3;
+  // C columns: 0 = A (x 65536), 1 = B (x 256), 2 = C (x 1); lane tig holds columns 2 tig, 2 tig + 1
+  const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : 0.f);
+  const float fB = tig == 0 ? 256.f : 0.f;
+  // lanes of columns 3..7 load column g % 3 as well: their sums meet zero multipliers
+  const uint2* pl = (const uint2*)(planes + (g % 3) * 8) + tig;
+  float* scw = scw_all + warp * (ROWS * SCW + 2 * ROWS);
+  float* msum = scw + ROWS * SCW;
+  float* fdv = msum + ROWS;
+  const int sr = lane >> 1, sh = lane & 1;  // scale decode: row, half of the sub-blocks
+  // item (tile k, block kb) = warp, warp + MM_CWARPS, ... of nst * NB, walked without divisions
+  int k = 0, kb = warp, slot = 0;
+  uint32_t phase = 0;
+  while (kb >= NB) {
+    kb -= NB;
+    ++k;
+    if (++slot == a.nslots) slot = 0, phase ^= 1;
+  }
+  for (; k < nst;) {
+    if (!mbar_wait_bounded(&full[slot], phase, a.status)) return;
+    const uint8_t* st = ring + slot * a.slot_bytes + kb * Q4K_BLOCK_BYTES;
+    const int row0 = (g0 + k) * ROWS;
+    const int n = min(ROWS, a.N - row0);
+    {
+      // sub-block scales and mins of row sr, sub-blocks 4 sh .. 4 sh + 3
+      // (Q4KTensor.cs:109-132): six-bit scales kept as integers, the mins
+      // folded with the unit sums of x, d with the block's x exponent
+      const int4 hdr = *(const int4*)(st + min(sr, n - 1) * rs);
+      const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((unsigned short)((uint32_t)hdr.x >> 16)));
+      const uint64_t sb = (uint32_t)hdr.y | ((uint64_t)((uint32_t)hdr.z & 0xFFFFu) << 32);
+      const uint64_t mb = ((uint32_t)hdr.z >> 16) | ((uint64_t)(uint32_t)hdr.w << 16);
+      const uint32_t s24 = (uint32_t)(sb >> (24 * sh)), m24 = (uint32_t)(mb >> (24 * sh));
+      const float4 q = *(const float4*)(usum + kb * 8 + 4 * sh);
+      int* si = (int*)scw + sr * SCW + 4 * sh;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) si[j] = (s24 >> (6 * j)) & 63;
+      float mpart = (float)(m24 & 63) * q.x;
+      mpart = fmaf((float)((m24 >> 6) & 63), q.y, mpart);
+      mpart = fmaf((float)((m24 >> 12) & 63), q.z, mpart);
+      mpart = fmaf((float)((m24 >> 18) & 63), q.w, mpart);
+      mpart = dmin * (mpart + __shfl_xor_sync(0xffffffffu, mpart, 1));
+      if (sh == 0) {
+        msum[sr] = mpart;
+        fdv[sr] = d * bexp[kb];
+      }
+    }
+    __syncwarp();
+    const uint8_t* rg = st + min(g, n - 1) * rs + 16 + 4 * tig;
+    const uint8_t* rg8 = st + min(g + 8, n - 1) * rs + 16 + 4 * tig;
+    const uint2* plu = pl + kb * 8 * 12;
+    const int* si = (const int*)scw;
+    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;  // C columns (2 tig, 2 tig + 1) of rows g and g + 8, scaled
+    // four independent MMAs in flight, then their epilogues
+#pragma unroll
+    for (int j0 = 0; j0 < 8; j0 += 4) {
+      int dd[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w0 = *(const uint32_t*)(rg + 16 * (j0 + j));
+        const uint32_t w1 = *(const uint32_t*)(rg8 + 16 * (j0 + j));
+        const uint2 b = plu[12 * (j0 + j)];
+        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, w0, w1, b.x, b.y);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int s0 = si[g * SCW + j0 + j], s1 = si[(g + 8) * SCW + j0 + j];
+        t0 += s0 * dd[j][0];
+        t1 += s0 * dd[j][1];
+        t2 += s1 * dd[j][2];
+        t3 += s1 * dd[j][3];
+      }
+    }
+    // |t| < 2^29: columns 0 (x 65536), 1 (x 256) on lane tig 0, column 2 on tig 1
+    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
+    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    float* rd = red + (slot * NB) * ROWS;
+    if (tig == 0) {
+      rd[kb * ROWS + g] = fmaf(fdv[g], acc0, -msum[g]);
+      rd[kb * ROWS + g + 8] = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    __syncwarp();
+    kb += MM_CWARPS;
+    while (kb >= NB) {
+      kb -= NB;
+      ++k;
+      if (++slot == a.nslots) slot = 0, phase ^= 1;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
+                        int* n_launch) {
+  if (W.scheme != SM_Q4_K || W.layout != SM_LAYOUT_INTENDED) return SM_ERR_UNSUPPORTED;
+  const int K = W.K(), N = W.N(), U = K / 32;
+  if (K % 256 || U > 1024) return SM_ERR_UNSUPPORTED;
+  MmaArgs a;
+  a.w = (const uint8_t*)W.data;
+  a.x = x;
+  a.y = y;
+  a.N = N;
+  a.K = K;
+  a.accumulate = accumulate;
+  a.status = status;
+  const int NB = K / 256;
+  const int64_t rbytes = (int64_t)NB * Q4K_BLOCK_BYTES;
+  // row stride in 16-byte units odd modulo 8 words-per-row quads: rows g = 0..7
+  // land on distinct bank quads
+  a.row_stride = (int)rbytes + ((NB % 2 == 0) ? 16 : 32);
+  a.slot_bytes = (int64_t)ROWS * a.row_stride;
+  a.plane_offset = 256;
+  a.red_offset = a.plane_offset + U * (24 * 4 + 8);
+  a.scw_offset = a.red_offset + 8 * NB * ROWS * 4;
+  a.ring_offset = a.scw_offset + MM_CWARPS * (ROWS * SCW + 2 * ROWS) * 4;
+  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
+  int optin = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const int64_t budget = optin - 1024 - a.ring_offset;
+  a.nslots = (int)std::min<int64_t>(8, budget / a.slot_bytes);
+  if (a.nslots < 2) return SM_ERR_UNSUPPORTED;
+  const size_t smem = (size_t)a.ring_offset + (size_t)a.nslots * a.slot_bytes;
+  static bool attr_set[64] = {};
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemv_mma_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
+    attr_set[dev] = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ngroups = (N + ROWS - 1) / ROWS;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(sms, ngroups));
+  cfg.blockDim = dim3(MM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel, a));
+  if (n_launch) ++*n_launch;
+  return SM_OK;
+}
+
+}  // namespace sm
