@@ -11,7 +11,8 @@ flush is needed between steps.
 Printed JSON (rank 0): value = decode tokens/s summed over GPUs, device-timed
 (CUDA events on the library's stream, max over ranks); e2e = the same loop
 through the host-pointer C-ABI (token H2D + next token D2H every step);
-roofline = the Q4_K GEMV (the dominant kernel) against measured HBM bandwidth;
+roofline = the decode step kernel (one launch per step) against measured HBM bandwidth,
+with its algorithmic bytes (weights + K/V cache rows read at the mean context);
 cpu_baseline = the CPU oracle (C++ restatement of the reference algorithm) on a
 bounded sample of the same workload.
 
@@ -53,6 +54,13 @@ def weight_bytes_per_token(c):
         mult = 1 if n == "output" else c["n_layers"]
         tot += mult * r * k * BYTES[SCHEMES[n]]
     return tot
+
+
+def step_bytes(c, ctx):
+    """Algorithmic HBM bytes of one bs1 decode step at context ctx: every weight once, the
+    fp32 K/V cache rows of all layers read once, the new K/V rows and the embedding row."""
+    kv_row = c["n_kv_heads"] * c["head_dim"] * 4
+    return (weight_bytes_per_token(c) + c["n_layers"] * 2 * kv_row * (ctx + 1) + 4 * c["hidden"])
 
 
 def peaks():
@@ -333,11 +341,15 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     with clocks:
+        if args.profile_region:
+            torch.cuda.profiler.start()
         e0.record(stream)
         for _ in range(args.steps):
             kv.decode_device(seq.data_ptr(), tok.data_ptr(), 1, None, tok.data_ptr())
         e1.record(stream)
         e1.synchronize()
+        if args.profile_region:
+            torch.cuda.profiler.stop()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -381,10 +393,13 @@ def run_ours(args):
     hbm, peak_kind = peaks()
     g_ms, g_bytes = time_gemv(sm, ctx, weights["w_gate"], torch)
     d_ms, d_bytes = time_gemv(sm, ctx, weights["w_down"], torch)
+    mega = os.environ.get("SMALLMIND_MEGA", "1") != "0"
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "gemv_q4k_traffic.json")) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+        with open(os.path.join(ROOT, "profiles", "decode_mega_traffic.json")) as f:
+            tj = json.load(f)
+        if mega and tj.get("prompt") == args.prompt:
+            traffic = tj.get("dram_bytes_per_launch")
     except Exception:
         pass
 
@@ -418,6 +433,9 @@ def run_ours(args):
     if rank == 0:
         clk = clocks.summary(local)
         wbytes = weight_bytes_per_token(cfg)
+        ctx_mid = args.prompt + args.warmup + args.steps / 2.0
+        sbytes = step_bytes(cfg, ctx_mid)
+        ach = sbytes / (ms_per_step * 1e-3) / 1e9
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -429,11 +447,14 @@ def run_ours(args):
                        "l2": "no flush: 667 MB of weights per step > 126 MB L2"},
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
-            "roofline": {"bound": "hbm", "achieved": round(g_bytes / (g_ms * 1e-3) / 1e9, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(g_bytes / (g_ms * 1e-3) / 1e9 / hbm, 4),
-                         "traffic": traffic, "kernel": "gemv1_kernel<Q4_K> 2048->5632 (M=1)",
-                         "peak_kind": peak_kind},
-            "gemv": {"q4k_2048x5632_us": round(g_ms * 1000, 2), "q6k_5632x2048_us": round(d_ms * 1000, 2),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "traffic": traffic,
+                         "kernel": ("decode_mega_kernel (one launch per step)" if mega
+                                    else "per-kernel decode step"),
+                         "algorithmic_bytes_per_launch": int(sbytes), "peak_kind": peak_kind},
+            "gemv": {"q4k_2048x5632_us": round(g_ms * 1000, 2),
+                     "q4k_gbs": round(g_bytes / (g_ms * 1e-3) / 1e9, 1),
+                     "q6k_5632x2048_us": round(d_ms * 1000, 2),
                      "q6k_gbs": round(d_bytes / (d_ms * 1e-3) / 1e9, 1)},
             "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
             "bs64_decode_tok_s": round(bs64_tps, 1),
@@ -457,6 +478,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
     ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
     ap.add_argument("--gemv-only", default=None, help="restrict --gemv-sweep to 'SCHEME KxN' (profiling)")
+    ap.add_argument("--profile-region", action="store_true",
+                    help="bracket the timed decode loop with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the device decode loop (profiling runs: no e2e, GEMV, bs64 or CPU legs)")
     args = ap.parse_args()
