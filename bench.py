@@ -272,6 +272,67 @@ def run_gemv_sweep(args):
     print(json.dumps({"gemv_sweep_m1": res, "peak_gbs": hbm}), flush=True)
 
 
+def run_gemm_sweep(args):
+    """Op-sweep at M = 8, 64 (decode batches, HBM-bound: GB/s of packed weights +
+    activations) and M = 512, 2048 (prefill, tensor-bound: algorithmic 2*M*K*N FLOP/s against the
+    measured dense bf16 peak).  Device time per call (fp16 split of x + tcgen05 GEMM for M >= 16) from
+    a CUDA graph over rotating weights."""
+    import torch
+
+    import smallmind_b200 as sm
+    ctx = sm.CudaContext(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    torch.cuda.set_stream(stream)
+    hbm, _ = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tflops = 1590.0
+    res = {}
+    for scheme in ("Q4_K", "Q6_K", "Q8_0", "Q4_0"):
+        for (K, N) in ((2048, 2048), (2048, 5632), (5632, 2048), (4096, 11008)):
+            if args.gemv_only and not args.gemv_only.startswith(f"{scheme} {K}x{N}"):
+                continue
+            nb = N * K * BYTES[scheme]
+            ws = make_weights(sm, ctx, torch, scheme, N, K, max(2, int(300e6 // nb) + 1))
+            for M in (8, 64, 512, 2048):
+                if args.gemv_only and args.gemv_only.count(" ") == 2 and args.gemv_only.split()[2] != f"M{M}":
+                    continue
+                x = torch.randn(M, K, device="cuda")
+                y = torch.empty(M, N, device="cuda")
+                reps = 3 if M <= 64 else 1
+                for w in ws:
+                    w.matmul_device(x.data_ptr(), y.data_ptr(), M)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for _ in range(reps):
+                        for w in ws:
+                            w.matmul_device(x.data_ptr(), y.data_ptr(), M)
+                g.replay()
+                stream.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                e1.synchronize()
+                ms = e0.elapsed_time(e1) / (reps * len(ws))
+                key = f"{scheme} {K}x{N} M{M}"
+                if M <= 64:
+                    alg = nb + 4 * M * (K + N)
+                    res[key] = {"us": round(ms * 1000, 2), "GBs": round(alg / (ms * 1e-3) / 1e9, 1),
+                                "frac_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm, 3)}
+                else:
+                    fl = 2.0 * M * K * N / (ms * 1e-3) / 1e12
+                    res[key] = {"us": round(ms * 1000, 1), "TFLOPs": round(fl, 1), "frac_tensor": round(fl / tflops, 3)}
+                del g, x, y
+            for w in ws:
+                w.close()
+    print(json.dumps({"gemm_sweep": res, "peak_gbs": hbm, "peak_tflops": tflops}), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -477,6 +538,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
     ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="time M = 8, 64, 512, 2048 on the op-sweep shapes and exit")
     ap.add_argument("--gemv-only", default=None, help="restrict --gemv-sweep to 'SCHEME KxN' (profiling)")
     ap.add_argument("--profile-region", action="store_true",
                     help="bracket the timed decode loop with cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -485,6 +548,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gemm_sweep:
+        run_gemm_sweep(args)
+        return
     if args.gemv_sweep:
         run_gemv_sweep(args)
     elif args.impl == "reference":

@@ -1,0 +1,436 @@
+// Prefill / batched GEMM y[M][N] (+)= x[M][K] W[N][K]^T on the tcgen05 tensor
+// cores, for every quantized weight format (INTENDED layout).
+//
+// Precision.  The weight of element (n, k) is the exact fp32 value of the
+// reference element formula (Q8Tensor.cs:151, Q4Tensor.cs:150-179,
+// Q4KTensor.cs:129-147, Q6KTensor.cs:105-124).  Both operands are split into
+// fp16 pairs, v = hi + lo with hi = fp16(v), lo = fp16(v - hi) (22 significant
+// bits), and each 16-wide k step issues three kind::f16 MMAs into one fp32 TMEM
+// accumulator: x_hi w_hi + x_hi w_lo + x_lo w_hi.  The dropped x_lo w_lo term
+// and the residuals are ~2^-22 relative, far inside the 1e-4 tolerance.
+// (|x| must stay below the fp16 range, 65504.)
+//
+// Structure (one 128 x 128 output tile per CTA, 320 threads):
+//   * x is split once into fp16 hi / lo planes (gemm_split_kernel) and each
+//     128 x 64 tile of both planes is brought in by TMA with the 128-byte
+//     swizzle (warp 8, one elected lane; no multicast);
+//   * warps 0..7 dequantize the 128 x 64 weight tile (thread = row, 32 k) to
+//     the same swizzled K-major layout, hi and lo planes;
+//   * warp 9, one lane, issues 4 k-steps x 3 tcgen05.mma per stage and
+//     commits each stage back to its producers through an mbarrier;
+//   * warps 0..3 read the accumulator from TMEM (tcgen05.ld 32x32b) and store y.
+// Every mbarrier wait is bounded (SM_ERR_TIMEOUT in *status), and the TMEM
+// columns are always released before the CTA exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "mbar.cuh"
+
+namespace sm {
+namespace {
+
+constexpr int BM = 128;  // x rows per tile (MMA M)
+constexpr int BN = 128;  // weight rows per tile (MMA N)
+constexpr int BK = 64;   // k per stage: one 128-byte swizzle atom of fp16
+constexpr int STAGES = 3;
+constexpr int LOADER_WARPS = 8;
+constexpr int TMA_WARP = LOADER_WARPS;
+constexpr int THREADS = (LOADER_WARPS + 2) * 32;
+constexpr int TILE_A = BM * BK * 2;  // bytes of one fp16 plane of the x tile
+constexpr int TILE_W = BN * BK * 2;
+constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
+constexpr int TMEM_COLS = BN;  // fp32 accumulator: 128 lanes x BN columns
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+
+struct TcArgs {
+  DevWeight W;
+  int M, N, K;
+  float* y;
+  int ldy;
+  int accumulate;
+  int* status;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand in the canonical 128-byte-swizzle layout: rows of 128 B,
+// 8-row atoms of 1024 B (stride byte offset), version 1, layout type 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both
+// K-major, N = BN, M = BM.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(IDESC), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- weight unit -> 32 fp32 values
+// Elements k0 .. k0 + 31 (k0 % 32 == 0) of weight row n, exactly as the
+// reference element formulas produce them.
+__device__ __forceinline__ void weight_unit(const DevWeight& W, int n, int k0, int K, float (&w)[32]) {
+  switch (W.scheme) {
+    case SM_Q4_K: {
+      const int kb = k0 >> 8, j = (k0 >> 5) & 7;
+      const uint8_t* blk = (const uint8_t*)W.data + ((int64_t)n * (K >> 8) + kb) * Q4K_BLOCK_BYTES;
+      const uint32_t h0 = *(const uint32_t*)blk;
+      const float d = half_bits_to_float((uint16_t)(h0 & 0xFFFF)), dmin = half_bits_to_float((uint16_t)(h0 >> 16));
+      int sc, mn;
+      unpack_q4k_scales(blk + 4, j, sc, mn);
+      const float s = __fmul_rn(d, (float)sc), m = __fmul_rn(dmin, (float)mn);
+      const uint4 q = *(const uint4*)(blk + 16 + 16 * j);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t b = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        w[2 * i] = __fsub_rn(__fmul_rn(s, (float)(b & 0xF)), m);
+        w[2 * i + 1] = __fsub_rn(__fmul_rn(s, (float)(b >> 4)), m);
+      }
+      break;
+    }
+    case SM_Q6_K: {
+      const int kb = k0 >> 8, j = (k0 >> 5) & 7;
+      const int64_t b = (int64_t)n * (K >> 8) + kb;
+      const uint8_t* blk = (const uint8_t*)W.data + b * Q6K_BODY_BYTES;
+      const float d = half_bits_to_float(((const uint16_t*)W.aux)[aux_idx(b, W.aux_bpr, W.aux_stride)]);
+      const float s0 = __fmul_rn(d, (float)(int8_t)blk[192 + 2 * j]);
+      const float s1 = __fmul_rn(d, (float)(int8_t)blk[192 + 2 * j + 1]);
+      const uint4 ql = *(const uint4*)(blk + 16 * j);
+      const uint32_t qlw[4] = {ql.x, ql.y, ql.z, ql.w};
+      // re-packed high plane: word t covers elements 16t .. 16t+15; byte bb holds
+      // the highs of 16t+2bb, 16t+2bb+1 (bits 0-3) and 16t+8+2bb, 16t+9+2bb (bits 4-7)
+      const uint2 qh = *(const uint2*)(blk + 128 + 8 * j);
+      const uint32_t qhw[2] = {qh.x, qh.y};
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const uint32_t lb = (qlw[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const int low4 = (e & 1) ? (int)(lb >> 4) : (int)(lb & 0xF);
+        const int t = e >> 4, ee = e & 15;
+        const int bb = (ee & 7) >> 1, sh = ((ee >> 3) << 2) + ((ee & 1) << 1);
+        const int high2 = (int)((qhw[t] >> (8 * bb + sh)) & 3);
+        w[e] = __fmul_rn(e < 16 ? s0 : s1, (float)((low4 | (high2 << 4)) - 32));
+      }
+      break;
+    }
+    case SM_Q8_0: {
+      const int64_t i0 = (int64_t)n * K + k0;
+      const int4* src = (const int4*)((const int8_t*)W.data + i0);
+      const int4 v0 = src[0], v1 = src[1];
+      const int vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const float* sc = (const float*)W.aux;
+      const bool one = W.block_size % 32 == 0;  // one scale block covers the unit
+      const float s1 = sc[aux_idx(i0 / W.block_size, W.aux_bpr, W.aux_stride)];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float s = one ? s1 : sc[aux_idx((i0 + e) / W.block_size, W.aux_bpr, W.aux_stride)];
+        w[e] = __fmul_rn((float)(int8_t)((vw[e >> 2] >> (8 * (e & 3))) & 0xFF), s);
+      }
+      break;
+    }
+    case SM_Q4_0: {
+      const int64_t i0 = (int64_t)n * K + k0;  // even
+      const uint4 q = *(const uint4*)((const uint8_t*)W.data + (i0 >> 1));
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      const float* sc = (const float*)W.aux;
+      const bool one = W.block_size % 32 == 0;
+      const float s1 = sc[aux_idx(i0 / W.block_size, W.aux_bpr, W.aux_stride)];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const uint32_t b = (qw[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const int nib = (e & 1) ? (int)(b >> 4) : (int)(b & 0xF);
+        const float s = one ? s1 : sc[aux_idx((i0 + e) / W.block_size, W.aux_bpr, W.aux_stride)];
+        w[e] = __fmul_rn((float)(nib < 8 ? nib : nib - 16), s);
+      }
+      break;
+    }
+    default: {  // F32
+      const float4* src = (const float4*)((const float*)W.data + (int64_t)n * K + k0);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 v = src[c];
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+    }
+  }
+}
+
+// byte offset of 16-byte chunk c (8 fp16 along k) of row r in a 128B-swizzled tile
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                   const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full_a = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  uint64_t* full_w = full_a + STAGES;
+  uint64_t* empty = full_w + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int K = a.K, nk = K / BK;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_w[s], LOADER_WARPS * 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < LOADER_WARPS) {
+    // ---- weight tiles: thread = (row r, k half h)
+    const int r = tid & (BN - 1), h = tid >> 7;
+    const int n = n0 + r;
+    for (int kt = 0; kt < nk; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
+      float w[32];
+      if (n < a.N) {
+        weight_unit(a.W, n, kt * BK + 32 * h, K, w);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) w[e] = 0.f;
+      }
+      uint8_t* whi = smem + s * STAGE_BYTES + 2 * TILE_A;
+      uint8_t* wlo = whi + TILE_W;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hp[4], lp[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float v0 = w[8 * c + 2 * e], v1 = w[8 * c + 2 * e + 1];
+          const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+          const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+          const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+          hp[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          lp[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        const uint32_t off = sw_off(r, 4 * h + c);
+        *(uint4*)(whi + off) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+        *(uint4*)(wlo + off) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+      }
+      // generic-proxy stores -> visible to the tensor core (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&full_w[s]);
+    }
+  } else if (warp == TMA_WARP) {
+    if (lane == 0) {
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
+        uint8_t* st = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full_a[s], 2 * TILE_A);
+        tma_load_2d(st, &tm_hi, kt * BK, m0, &full_a[s]);
+        tma_load_2d(st + TILE_A, &tm_lo, kt * BK, m0, &full_a[s]);
+      }
+    }
+  } else {  // warp LOADER_WARPS + 1: the MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int kt = 0; kt < nk && ok; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t par = (kt / STAGES) & 1;
+        ok = mbar_wait_bounded(&full_a[s], par, a.status) && mbar_wait_bounded(&full_w[s], par, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint64_t dah = sw128_desc(base), dal = sw128_desc(base + TILE_A);
+        const uint64_t dwh = sw128_desc(base + 2 * TILE_A), dwl = sw128_desc(base + 2 * TILE_A + TILE_W);
+#pragma unroll
+        for (int ks = 0; ks < BK / 16; ++ks) {
+          const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // 16 fp16 = 32 bytes along k
+          mma_f16(tmem, dah + adv, dwh + adv, (kt | ks) != 0);
+          mma_f16(tmem, dah + adv, dwl + adv, 1);
+          mma_f16(tmem, dal + adv, dwh + adv, 1);
+        }
+        mma_commit(&empty[s]);  // stage s may be refilled once these MMAs have read it
+      }
+      mma_commit(done);
+    }
+  }
+
+  if (warp < 4) {
+    // ---- epilogue: TMEM lanes 32 warp .. 32 warp + 31 = x rows, columns = weight rows
+    const bool ok = mbar_wait_bounded(done, 0, a.status);
+    tc_fence_after();
+    if (ok) {
+      const int m = m0 + warp * 32 + lane;
+      float* yr = a.y + (int64_t)m * a.ldy;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        if (m < a.M) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int n = n0 + c0 + e;
+            if (n < a.N) {
+              const float r = __uint_as_float(v[e]);
+              yr[n] = a.accumulate ? yr[n] + r : r;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// x (fp32, rows of K) -> fp16 hi and lo planes
+__global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint2* __restrict__ hi,
+                                  uint2* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i];
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    uint32_t hp[2] = {0, 0}, lp[2] = {0, 0};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __half h = __float2half_rn(f[e]);
+      const __half l = __float2half_rn(__fsub_rn(f[e], __half2float(h)));
+      hp[e >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (e & 1));
+      lp[e >> 1] |= (uint32_t)__half_as_ushort(l) << (16 * (e & 1));
+    }
+    hi[i] = make_uint2(hp[0], hp[1]);
+    lo[i] = make_uint2(lp[0], lp[1]);
+  }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int make_plane_map(CUtensorMap* map, void* base, int M, int K) {
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
+                                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SM_OK : fail(SM_ERR_CUDA, "gemm: tensor map encoding failed");
+}
+
+}  // namespace
+
+bool gemm_tc_supports(const DevWeight& W, int M) {
+  if (W.layout != SM_LAYOUT_INTENDED || M < 16) return false;
+  const int K = W.K();
+  if (K % BK) return false;
+  switch (W.scheme) {
+    case SM_Q4_K:
+    case SM_Q6_K:
+      return K % 256 == 0;
+    case SM_Q8_0:
+    case SM_Q4_0:
+      return W.block_size > 0;
+    case SM_F32:
+      return true;
+  }
+  return false;
+}
+
+int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
+                   cudaStream_t st, int* n_launch) {
+  const int K = W.K(), N = W.N();
+  if (!gemm_tc_supports(W, M)) return SM_ERR_UNSUPPORTED;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  // fp16 hi / lo planes of x in stream-ordered scratch
+  const int64_t n = (int64_t)M * K;
+  void* planes = nullptr;
+  SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)n * 4, st));
+  __half* hi = (__half*)planes;
+  __half* lo = hi + n;
+  int rc = SM_OK;
+  {
+    const int64_t n4 = n / 4;
+    const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
+    gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
+    if (n_launch) ++*n_launch;
+    CUtensorMap mh, ml;
+    rc = make_plane_map(&mh, hi, M, K);
+    if (rc == SM_OK) rc = make_plane_map(&ml, lo, M, K);
+    if (rc == SM_OK) {
+      TcArgs a;
+      a.W = W;
+      a.M = M;
+      a.N = N;
+      a.K = K;
+      a.y = y;
+      a.ldy = ldy;
+      a.accumulate = accumulate;
+      a.status = status;
+      dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+      gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(mh, ml, a);
+      if (cudaGetLastError() != cudaSuccess) rc = fail(SM_ERR_CUDA, "gemm: launch failed");
+      if (n_launch) ++*n_launch;
+    }
+  }
+  cudaFreeAsync(planes, st);
+  return rc;
+}
+
+}  // namespace sm

@@ -326,6 +326,14 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     }
     return launch_gemv1(a, st, n_launch);
   }
+  {
+    // M >= 16: tcgen05 GEMM (SMALLMIND_GEMM_TC=0 selects the CUDA-core row kernel)
+    const char* et = std::getenv("SMALLMIND_GEMM_TC");
+    if (!(et && et[0] == '0') && gemm_tc_supports(W, M)) {
+      const int rc = launch_gemm_tc(W, x, y, M, ldy, accumulate, nullptr, st, n_launch);
+      if (rc != SM_ERR_UNSUPPORTED) return rc;
+    }
+  }
   const bool fast = kq || (K % 32 == 0 && (W.scheme == SM_F32 || W.block_size % 32 == 0));
   if (!fast) {
     dim3 grid(ceil_div(N, 128), M);

@@ -50,6 +50,10 @@ int launch_gemv_stream(const GemvArgs& g, int* status, cudaStream_t st, int* n_l
 bool gemv1_supports(const DevWeight& w, int K);
 int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y, int mode);
 int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch);
+// y[M][N] (+)= x[M][K] W^T on tcgen05 (INTENDED layout, M >= 16, K % 64 == 0)
+bool gemm_tc_supports(const DevWeight& W, int M);
+int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
+                   cudaStream_t st, int* n_launch);
 // Q4_K (INTENDED) y = W x on the int8 tensor-core path (mma.sync m16n8k32)
 int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
                         int* n_launch);
