@@ -36,9 +36,15 @@ constexpr int BM = 128;  // x rows per tile (MMA M)
 constexpr int BN = 128;  // weight rows per tile (MMA N)
 constexpr int BK = 64;   // k per stage: one 128-byte swizzle atom of fp16
 constexpr int STAGES = 3;
-constexpr int LOADER_WARPS = 8;
-constexpr int TMA_WARP = LOADER_WARPS;
-constexpr int THREADS = (LOADER_WARPS + 2) * 32;
+// warp roles: WT = false (weights dequantized in the kernel): warps 0..7 load
+// weight tiles, 8 = TMA, 9 = MMA; WT = true (weights pre-split into fp16
+// planes and loaded by TMA): 4 = TMA, 5 = MMA.  Warps 0..3 run the epilogue.
+template <bool WT>
+struct Roles {
+  static constexpr int LOADER_WARPS = WT ? 0 : 8;
+  static constexpr int TMA_WARP = WT ? 4 : 8;
+  static constexpr int THREADS = (TMA_WARP + 2) * 32;
+};
 constexpr int TILE_A = BM * BK * 2;  // bytes of one fp16 plane of the x tile
 constexpr int TILE_W = BN * BK * 2;
 constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
@@ -52,6 +58,8 @@ struct TcArgs {
   int ldy;
   int accumulate;
   int* status;
+  int kslices;      // split-K: blockIdx.z takes stages [z nk / kslices, (z+1) nk / kslices)
+  float* partial;   // kslices > 1: [kslices][M][N] partial sums (reduced by gemm_reduce_kernel)
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -191,14 +199,124 @@ __device__ __forceinline__ void weight_unit(const DevWeight& W, int n, int k0, i
   }
 }
 
+// Packed bytes of one unit, loaded ahead of their decode (register prefetch).
+// Q4_K: a = block header, b = the unit's 16 code bytes.  Q6_K: a = ql, b.xy =
+// high plane words, b.z = the two int8 scales, b.w = d bits.  Q8_0: a, b = 32
+// codes, s = scale.  Q4_0: a = 16 code bytes, s = scale.
+struct RawUnit {
+  uint4 a, b;
+  float s;
+};
+
+__device__ __forceinline__ bool raw_prefetchable(const DevWeight& W) {
+  return W.scheme == SM_Q4_K || W.scheme == SM_Q6_K ||
+         ((W.scheme == SM_Q8_0 || W.scheme == SM_Q4_0) && W.block_size % 32 == 0);
+}
+
+__device__ __forceinline__ void load_raw(const DevWeight& W, int n, int k0, int K, RawUnit& r) {
+  switch (W.scheme) {
+    case SM_Q4_K: {
+      const uint8_t* blk = (const uint8_t*)W.data + ((int64_t)n * (K >> 8) + (k0 >> 8)) * Q4K_BLOCK_BYTES;
+      r.a = __ldg((const uint4*)blk);
+      r.b = __ldg((const uint4*)(blk + 16 + 16 * ((k0 >> 5) & 7)));
+      break;
+    }
+    case SM_Q6_K: {
+      const int j = (k0 >> 5) & 7;
+      const int64_t b = (int64_t)n * (K >> 8) + (k0 >> 8);
+      const uint8_t* blk = (const uint8_t*)W.data + b * Q6K_BODY_BYTES;
+      r.a = __ldg((const uint4*)(blk + 16 * j));
+      const uint2 qh = __ldg((const uint2*)(blk + 128 + 8 * j));
+      r.b.x = qh.x;
+      r.b.y = qh.y;
+      r.b.z = __ldg((const unsigned short*)(blk + 192 + 2 * j));
+      r.b.w = __ldg(((const unsigned short*)W.aux) + aux_idx(b, W.aux_bpr, W.aux_stride));
+      break;
+    }
+    case SM_Q8_0: {
+      const int64_t i0 = (int64_t)n * K + k0;
+      const uint4* src = (const uint4*)((const int8_t*)W.data + i0);
+      r.a = __ldg(src);
+      r.b = __ldg(src + 1);
+      r.s = __ldg((const float*)W.aux + aux_idx(i0 / W.block_size, W.aux_bpr, W.aux_stride));
+      break;
+    }
+    default: {  // Q4_0
+      const int64_t i0 = (int64_t)n * K + k0;
+      r.a = __ldg((const uint4*)((const uint8_t*)W.data + (i0 >> 1)));
+      r.s = __ldg((const float*)W.aux + aux_idx(i0 / W.block_size, W.aux_bpr, W.aux_stride));
+    }
+  }
+}
+
+// The same element formulas as weight_unit, from prefetched bytes.
+__device__ __forceinline__ void decode_raw(int scheme, int k0, const RawUnit& r, float (&w)[32]) {
+  switch (scheme) {
+    case SM_Q4_K: {
+      const float d = half_bits_to_float((uint16_t)(r.a.x & 0xFFFF));
+      const float dmin = half_bits_to_float((uint16_t)(r.a.x >> 16));
+      // six-bit scale / min j at bits 6j of header bytes 4..9 / 10..15 (Q4KTensor.cs:109-126)
+      const int j = (k0 >> 5) & 7;
+      const uint64_t sb = (uint64_t)r.a.y | ((uint64_t)(r.a.z & 0xFFFFu) << 32);
+      const uint64_t mb = (uint64_t)(r.a.z >> 16) | ((uint64_t)r.a.w << 16);
+      const float s = __fmul_rn(d, (float)(int)((sb >> (6 * j)) & 63));
+      const float m = __fmul_rn(dmin, (float)(int)((mb >> (6 * j)) & 63));
+      const uint32_t qw[4] = {r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t b = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        w[2 * i] = __fsub_rn(__fmul_rn(s, (float)(b & 0xF)), m);
+        w[2 * i + 1] = __fsub_rn(__fmul_rn(s, (float)(b >> 4)), m);
+      }
+      break;
+    }
+    case SM_Q6_K: {
+      const float d = half_bits_to_float((uint16_t)r.b.w);
+      const float s0 = __fmul_rn(d, (float)(int8_t)(r.b.z & 0xFF));
+      const float s1 = __fmul_rn(d, (float)(int8_t)((r.b.z >> 8) & 0xFF));
+      const uint32_t qlw[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+      const uint32_t qhw[2] = {r.b.x, r.b.y};
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const uint32_t lb = (qlw[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const int low4 = (e & 1) ? (int)(lb >> 4) : (int)(lb & 0xF);
+        const int t = e >> 4, ee = e & 15;
+        const int bb = (ee & 7) >> 1, sh = ((ee >> 3) << 2) + ((ee & 1) << 1);
+        const int high2 = (int)((qhw[t] >> (8 * bb + sh)) & 3);
+        w[e] = __fmul_rn(e < 16 ? s0 : s1, (float)((low4 | (high2 << 4)) - 32));
+      }
+      break;
+    }
+    case SM_Q8_0: {
+      const uint32_t vw[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+      for (int e = 0; e < 32; ++e) w[e] = __fmul_rn((float)(int8_t)((vw[e >> 2] >> (8 * (e & 3))) & 0xFF), r.s);
+      break;
+    }
+    default: {  // Q4_0
+      const uint32_t qw[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const uint32_t b = (qw[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const int nib = (e & 1) ? (int)(b >> 4) : (int)(b & 0xF);
+        w[e] = __fmul_rn((float)(nib < 8 ? nib : nib - 16), r.s);
+      }
+    }
+  }
+}
+
 // byte offset of 16-byte chunk c (8 fp16 along k) of row r in a 128B-swizzled tile
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+template <bool WT>
+__global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                   const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo,
                    const __grid_constant__ TcArgs a) {
+  constexpr int LOADER_WARPS = Roles<WT>::LOADER_WARPS;
+  constexpr int TMA_WARP = Roles<WT>::TMA_WARP;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full_a = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -208,12 +326,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  const int K = a.K, nk = K / BK;
+  const int K = a.K;
+  const int nk_all = K / BK;
+  const int kt0 = (int)((int64_t)nk_all * blockIdx.z / a.kslices);
+  const int nk = (int)((int64_t)nk_all * (blockIdx.z + 1) / a.kslices) - kt0;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&full_w[s], LOADER_WARPS * 32);
+      mbar_init(&full_w[s], WT ? 1 : LOADER_WARPS * 32);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
@@ -230,20 +351,34 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < LOADER_WARPS) {
-    // ---- weight tiles: thread = (row r, k half h)
+  if (!WT && warp < LOADER_WARPS) {
+    // ---- weight tiles: thread = (row r, k half h); the packed bytes of the
+    // next two stages are in flight while this one is decoded
     const int r = tid & (BN - 1), h = tid >> 7;
     const int n = n0 + r;
+    const bool live = n < a.N;
+    const bool pf = raw_prefetchable(a.W);
+    RawUnit r0, r1;
+    if (pf && live) {
+      if (nk > 0) load_raw(a.W, n, (kt0 + 0) * BK + 32 * h, K, r0);
+      if (nk > 1) load_raw(a.W, n, (kt0 + 1) * BK + 32 * h, K, r1);
+    }
     for (int kt = 0; kt < nk; ++kt) {
       const int s = kt % STAGES;
-      if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
+      const int k0 = (kt0 + kt) * BK + 32 * h;
       float w[32];
-      if (n < a.N) {
-        weight_unit(a.W, n, kt * BK + 32 * h, K, w);
-      } else {
+      if (!live) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) w[e] = 0.f;
+      } else if (pf) {
+        const RawUnit cur = r0;
+        r0 = r1;
+        if (kt + 2 < nk) load_raw(a.W, n, k0 + 2 * BK, K, r1);
+        decode_raw(a.W.scheme, k0, cur, w);
+      } else {
+        weight_unit(a.W, n, k0, K, w);
       }
+      if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
       uint8_t* whi = smem + s * STAGE_BYTES + 2 * TILE_A;
       uint8_t* wlo = whi + TILE_W;
 #pragma unroll
@@ -252,11 +387,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float v0 = w[8 * c + 2 * e], v1 = w[8 * c + 2 * e + 1];
-          const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-          const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
-          const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
-          hp[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-          lp[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          const __half2 hh = __floats2half2_rn(v0, v1);
+          const float2 hf = __half22float2(hh);
+          const __half2 ll = __floats2half2_rn(__fsub_rn(v0, hf.x), __fsub_rn(v1, hf.y));
+          hp[e] = *(const uint32_t*)&hh;
+          lp[e] = *(const uint32_t*)&ll;
         }
         const uint32_t off = sw_off(r, 4 * h + c);
         *(uint4*)(whi + off) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
@@ -272,18 +407,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = kt % STAGES;
         if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
         uint8_t* st = smem + s * STAGE_BYTES;
-        mbar_expect_tx(&full_a[s], 2 * TILE_A);
-        tma_load_2d(st, &tm_hi, kt * BK, m0, &full_a[s]);
-        tma_load_2d(st + TILE_A, &tm_lo, kt * BK, m0, &full_a[s]);
+        mbar_expect_tx(&full_a[s], WT ? 2 * TILE_A + 2 * TILE_W : 2 * TILE_A);
+        tma_load_2d(st, &tm_hi, (kt0 + kt) * BK, m0, &full_a[s]);
+        tma_load_2d(st + TILE_A, &tm_lo, (kt0 + kt) * BK, m0, &full_a[s]);
+        if (WT) {
+          tma_load_2d(st + 2 * TILE_A, &tm_whi, (kt0 + kt) * BK, n0, &full_a[s]);
+          tma_load_2d(st + 2 * TILE_A + TILE_W, &tm_wlo, (kt0 + kt) * BK, n0, &full_a[s]);
+        }
       }
     }
-  } else {  // warp LOADER_WARPS + 1: the MMA issuer
+  } else if (warp == TMA_WARP + 1) {  // the MMA issuer
     if (lane == 0) {
       bool ok = true;
       for (int kt = 0; kt < nk && ok; ++kt) {
         const int s = kt % STAGES;
         const uint32_t par = (kt / STAGES) & 1;
-        ok = mbar_wait_bounded(&full_a[s], par, a.status) && mbar_wait_bounded(&full_w[s], par, a.status);
+        ok = mbar_wait_bounded(&full_a[s], par, a.status) && (WT || mbar_wait_bounded(&full_w[s], par, a.status));
         if (!ok) break;
         tc_fence_after();
         const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
@@ -308,7 +447,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     if (ok) {
       const int m = m0 + warp * 32 + lane;
-      float* yr = a.y + (int64_t)m * a.ldy;
+      const bool part = a.kslices > 1;
+      float* yr = part ? a.partial + ((int64_t)blockIdx.z * a.M + m) * a.N : a.y + (int64_t)m * a.ldy;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t v[16];
@@ -319,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int n = n0 + c0 + e;
             if (n < a.N) {
               const float r = __uint_as_float(v[e]);
-              yr[n] = a.accumulate ? yr[n] + r : r;
+              yr[n] = (a.accumulate && !part) ? yr[n] + r : r;
             }
           }
         }
@@ -350,6 +490,53 @@ __global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint
     }
     hi[i] = make_uint2(hp[0], hp[1]);
     lo[i] = make_uint2(lp[0], lp[1]);
+  }
+}
+
+// W -> fp16 hi / lo planes [N][K] (one thread per 32-weight unit), for GEMMs
+// with enough x rows that dequantizing each weight once up front is cheaper than
+// once per 128-row tile of x.
+__global__ void weight_split_kernel(const DevWeight W, int N, int K, uint4* __restrict__ hi, uint4* __restrict__ lo) {
+  const int upr = K >> 5;
+  const int64_t units = (int64_t)N * upr;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(u / upr), k0 = (int)(u - (int64_t)n * upr) * 32;
+    float w[32];
+    if (raw_prefetchable(W)) {
+      RawUnit r;
+      load_raw(W, n, k0, K, r);
+      decode_raw(W.scheme, k0, r, w);
+    } else {
+      weight_unit(W, n, k0, K, w);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t hp[4], lp[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v0 = w[8 * c + 2 * e], v1 = w[8 * c + 2 * e + 1];
+        const __half2 hh = __floats2half2_rn(v0, v1);
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn(__fsub_rn(v0, hf.x), __fsub_rn(v1, hf.y));
+        hp[e] = *(const uint32_t*)&hh;
+        lp[e] = *(const uint32_t*)&ll;
+      }
+      hi[u * 4 + c] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+      lo[u * 4 + c] = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+    }
+  }
+}
+
+// y (+)= sum over the k slices of the partial tiles, in slice order
+__global__ void gemm_reduce_kernel(const float* __restrict__ part, int S, int M, int N, float* __restrict__ y,
+                                   int ldy, int accumulate) {
+  const int64_t MN = (int64_t)M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < MN; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int z = 0; z < S; ++z) s += part[z * MN + i];
+    const int64_t m = i / N, n = i - m * N;
+    float* d = y + m * ldy + n;
+    *d = accumulate ? *d + s : s;
   }
 }
 
@@ -395,24 +582,39 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    SM_CUDA_TRY(
+        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    SM_CUDA_TRY(
+        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     attr_set[dev] = true;
   }
-  // fp16 hi / lo planes of x in stream-ordered scratch
-  const int64_t n = (int64_t)M * K;
+  // more than one 128-row tile of x: dequantize W once into fp16 planes and feed
+  // both operands by TMA; otherwise dequantize each weight tile in the kernel
+  const bool wt = M > BM;
+  const int64_t n = (int64_t)M * K, nw = wt ? (int64_t)N * K : 0;
   void* planes = nullptr;
-  SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)n * 4, st));
+  SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)(n + nw) * 4, st));
   __half* hi = (__half*)planes;
   __half* lo = hi + n;
+  __half* whi = lo + n;
+  __half* wlo = whi + nw;
   int rc = SM_OK;
   {
     const int64_t n4 = n / 4;
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
     gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
     if (n_launch) ++*n_launch;
-    CUtensorMap mh, ml;
+    if (wt) {
+      const int64_t units = nw / 32;
+      weight_split_kernel<<<(int)std::min<int64_t>((units + 255) / 256, 148 * 16), 256, 0, st>>>(
+          W, N, K, (uint4*)whi, (uint4*)wlo);
+      if (n_launch) ++*n_launch;
+    }
+    CUtensorMap mh, ml, mwh, mwl;
     rc = make_plane_map(&mh, hi, M, K);
     if (rc == SM_OK) rc = make_plane_map(&ml, lo, M, K);
+    if (rc == SM_OK) rc = make_plane_map(&mwh, wt ? (void*)whi : (void*)hi, wt ? N : M, K);
+    if (rc == SM_OK) rc = make_plane_map(&mwl, wt ? (void*)wlo : (void*)lo, wt ? N : M, K);
     if (rc == SM_OK) {
       TcArgs a;
       a.W = W;
@@ -423,10 +625,40 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
       a.ldy = ldy;
       a.accumulate = accumulate;
       a.status = status;
-      dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-      gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(mh, ml, a);
+      const int gn = (N + BN - 1) / BN, gm = (M + BM - 1) / BM;
+      // split K when the output tiles alone cannot fill the SMs
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int nk = K / BK;
+      int S = 1;
+      if (gn * gm < sms) S = std::max(1, std::min((sms + gn * gm - 1) / (gn * gm), nk / 2));
+      a.kslices = S;
+      a.partial = nullptr;
+      void* pbuf = nullptr;
+      if (S > 1) {
+        if (cudaMallocAsync(&pbuf, (size_t)S * M * N * 4, st) != cudaSuccess) {
+          S = 1;
+          a.kslices = 1;
+          pbuf = nullptr;
+        }
+        a.partial = (float*)pbuf;
+      }
+      dim3 grid(gn, gm, S);
+      if (wt)
+        gemm_tc_kernel<true><<<grid, Roles<true>::THREADS, SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
+      else
+        gemm_tc_kernel<false><<<grid, Roles<false>::THREADS, SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
       if (cudaGetLastError() != cudaSuccess) rc = fail(SM_ERR_CUDA, "gemm: launch failed");
       if (n_launch) ++*n_launch;
+      if (S > 1) {
+        if (rc == SM_OK) {
+          const int64_t MN = (int64_t)M * N;
+          const int blocks = (int)std::min<int64_t>((MN + 255) / 256, 148 * 8);
+          gemm_reduce_kernel<<<blocks, 256, 0, st>>>(a.partial, S, M, N, y, ldy, accumulate);
+          if (n_launch) ++*n_launch;
+        }
+        cudaFreeAsync(pbuf, st);
+      }
     }
   }
   cudaFreeAsync(planes, st);

@@ -52,3 +52,17 @@ def test_gemm_tc_small_activations(ctx, O):
     # activations far below 1 exercise the fp16 low planes in their subnormal range
     out, ref = _run(ctx, O, "Q4_K", 64, 512, 128, seed=7, xscale=1e-3)
     assert rel_err(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("scheme", ["Q4_K", "Q8_0"])
+def test_gemm_tc_full_grid_no_split(ctx, O, scheme):
+    # 2 x 74 output tiles fill the SMs, so K is not split
+    out, ref = _run(ctx, O, scheme, 256, 256, 128 * 74, seed=9)
+    assert rel_err(out, ref) <= TOL
+
+
+def test_gemm_tc_long_k_many_slices(ctx, O):
+    # one output tile and 32 k stages: K is split 16 ways and reduced in slice order
+    # (the accumulating form, y += x W^T, runs in the model prefill tests)
+    out, ref = _run(ctx, O, "Q6_K", 32, 2048, 256, seed=11)
+    assert rel_err(out, ref) <= TOL
