@@ -360,6 +360,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import smallmind_b200 as sm
+    from smallmind_b200 import sharding
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -416,10 +417,7 @@ def run_ours(args):
         dist.barrier()
     ms = e0.elapsed_time(e1)
     launches_timed = ctx.launch_count() - launches_w
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = sharding.max_over_ranks(ms, device="cuda")
     ms_per_step = ms / args.steps
     value = world * args.steps / (ms / 1000.0)
     if args.decode_only:
@@ -444,10 +442,7 @@ def run_ours(args):
         t, _ = kv2.decode([0], [nxt], want_logits=False)
         nxt = int(t[0])
     e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = sharding.max_over_ranks(e2e_s, device="cuda")
     kv2.close()
 
     # roofline: the Q4_K GEMV (gate, 2048 -> 5632) and Q6_K (down) over rotating layer weights
