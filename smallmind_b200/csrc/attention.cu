@@ -10,6 +10,8 @@
 
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace sm {
@@ -553,6 +555,15 @@ int launch_attention_prefill(const float* q, int q_stride, const float* k, const
   if (hd != 64) return fail(SM_ERR_UNSUPPORTED, "attention: head_dim must be 64");
   if (nH % nKv) return fail(SM_ERR_UNSUPPORTED, "attention: n_heads must be a multiple of n_kv_heads");
   if (T <= 0 || S < T) return fail(SM_ERR_SHAPE, "attention: need 0 < T <= S");
+  {
+    // tensor-core kernel (SMALLMIND_ATTN_TC=0 selects the CUDA-core one below)
+    const char* e = std::getenv("SMALLMIND_ATTN_TC");
+    if (!(e && e[0] == '0')) {
+      const int rc = launch_attention_prefill_tc(q, q_stride, k, v, row_stride, head_stride, out, out_stride, T, S, nH,
+                                                 nKv, hd, nullptr, st, n_launch);
+      if (rc != SM_ERR_UNSUPPORTED) return rc;
+    }
+  }
   const size_t smem = sizeof(float) * (2 * 64 * (PT + 1) + PT * 64 + PT * (PT + 1));
   auto kern = prefill_attention_kernel<64>;
   SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

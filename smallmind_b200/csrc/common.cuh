@@ -137,6 +137,10 @@ int launch_silu_mul(const float* g, const float* u, float* out, int64_t n, cudaS
 int launch_embed(const float* table, const int* tokens, float* x, int n, int H, cudaStream_t st);
 int launch_argmax(const float* logits, int rows, int V, int* out, cudaStream_t st);
 // attention.cu  (K/V element d of key j, kv head g: base + j*row_stride + g*head_stride + d)
+// causal GQA prefill attention on tcgen05 (hd 64); SM_ERR_UNSUPPORTED when the shape is not handled
+int launch_attention_prefill_tc(const float* q, int q_stride, const float* k, const float* v, int64_t row_stride,
+                                int64_t head_stride, float* out, int out_stride, int T, int S, int nH, int nKv, int hd,
+                                int* status, cudaStream_t st, int* n_launch);
 int launch_attention_prefill(const float* q, int q_stride, const float* k, const float* v, int64_t row_stride,
                              int64_t head_stride, float* out, int out_stride, int T, int S, int nH, int nKv, int hd,
                              cudaStream_t st, int* n_launch);

@@ -41,7 +41,8 @@ def test_silu_mul(ctx, O):
 
 
 @pytest.mark.parametrize("T,S,nH,nKv", [(1, 1, 4, 2), (1, 300, 32, 4), (5, 5, 9, 3), (70, 70, 4, 4),
-                                          (33, 130, 8, 2), (128, 128, 32, 4)])
+                                          (33, 130, 8, 2), (128, 128, 32, 4), (129, 129, 4, 1), (300, 300, 32, 4),
+                                          (200, 700, 8, 2), (640, 640, 32, 4)])
 def test_attention_prefill(ctx, O, T, S, nH, nKv):
     import smallmind_b200 as sm
     hd = 64
