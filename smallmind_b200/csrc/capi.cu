@@ -751,6 +751,17 @@ int head_m1(sm_model* m, const float* x_row, int& nl) {
 // The transformer stack over `rows` token rows whose tok/seq/pos/lens are in
 // work.ints.  prefill: all rows belong to one sequence (prefill_seq) at
 // positions pos0..pos0+rows-1; otherwise one row per sequence (decode).
+// Projections that share their input (Q|K|V, gate|up): one tensor-core GEMM over
+// the stacked weights when it applies, else one launch per weight.
+int matmul_multi(const DevWeight* const* ws, float* const* ys, const int* ld, int nw, const float* x, int rows,
+                 cudaStream_t st, int& nl) {
+  const char* et = std::getenv("SMALLMIND_GEMM_TC");
+  if (!(et && et[0] == '0') && gemm_tc_supports_multi(ws, nw, rows))
+    return launch_gemm_tc_multi(ws, ys, ld, nw, x, rows, 0, nullptr, st, &nl);
+  for (int i = 0; i < nw; ++i) SM_TRY(launch_matmul(*ws[i], x, ys[i], rows, ld[i], 0, st, &nl));
+  return SM_OK;
+}
+
 int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int pos0, int& nl) {
   const auto& c = m->cfg;
   Work& w = m->work;
@@ -773,9 +784,12 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
     SM_TRY(launch_rmsnorm(w.x, L.attn_norm, w.h, rows, H, c.norm_eps, st));
     ++nl;
     // merged [Q | K | V] rows (MultiHeadAttention.cs:213, layout :395-462)
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_WQ], w.h, w.qkv, rows, QS, 0, st, &nl));
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_WK], w.h, w.qkv + qd, rows, QS, 0, st, &nl));
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_WV], w.h, w.qkv + qd + kd, rows, QS, 0, st, &nl));
+    {
+      const DevWeight* ws[3] = {L.w[SM_ROLE_WQ], L.w[SM_ROLE_WK], L.w[SM_ROLE_WV]};
+      float* ys[3] = {w.qkv, w.qkv + qd, w.qkv + qd + kd};
+      const int ld[3] = {QS, QS, QS};
+      SM_TRY(matmul_multi(ws, ys, ld, 3, w.h, rows, st, nl));
+    }
     SM_TRY(launch_rope_qk_append(w.qkv, rows, QS, c.n_heads, c.n_kv_heads, hd, w.pos(), w.seq(), m->sin_t, m->cos_t,
                                  kc, vc, mt, st));
     ++nl;
@@ -796,8 +810,12 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
     SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.x, rows, H, 1, st, &nl));
     SM_TRY(launch_rmsnorm(w.x, L.ffn_norm, w.h, rows, H, c.norm_eps, st));
     ++nl;
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_W_GATE], w.h, w.g, rows, F, 0, st, &nl));
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_W_UP], w.h, w.u, rows, F, 0, st, &nl));
+    {
+      const DevWeight* ws[2] = {L.w[SM_ROLE_W_GATE], L.w[SM_ROLE_W_UP]};
+      float* ys[2] = {w.g, w.u};
+      const int ld[2] = {F, F};
+      SM_TRY(matmul_multi(ws, ys, ld, 2, w.h, rows, st, nl));
+    }
     SM_TRY(launch_silu_mul(w.g, w.u, w.g, (int64_t)rows * F, st));
     ++nl;
     SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.x, rows, H, 1, st, &nl));  // + residual (:184)

@@ -51,11 +51,17 @@ constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
 constexpr int TMEM_COLS = BN;  // fp32 accumulator: 128 lanes x BN columns
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 
+constexpr int MAX_SEG = 3;
+
+// Up to three weights with the same K, stacked along N (Q|K|V, gate|up); each
+// segment but the last spans whole 128-row tiles and has its own output.
 struct TcArgs {
-  DevWeight W;
-  int M, N, K;
-  float* y;
-  int ldy;
+  DevWeight W[MAX_SEG];
+  int nseg;
+  int seg_n0[MAX_SEG + 1];  // prefix sums of the segments' N
+  float* seg_y[MAX_SEG];
+  int seg_ldy[MAX_SEG];
+  int M, N, K;              // N = total over the segments
   int accumulate;
   int* status;
   int kslices;      // split-K: blockIdx.z takes stages [z nk / kslices, (z+1) nk / kslices)
@@ -355,13 +361,16 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
     // ---- weight tiles: thread = (row r, k half h); the packed bytes of the
     // next two stages are in flight while this one is decoded
     const int r = tid & (BN - 1), h = tid >> 7;
-    const int n = n0 + r;
-    const bool live = n < a.N;
-    const bool pf = raw_prefetchable(a.W);
+    int sg = 0;
+    while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
+    const DevWeight& W = a.W[sg];
+    const int n = n0 + r - a.seg_n0[sg];  // row inside the segment's weight
+    const bool live = n0 + r < a.seg_n0[sg + 1];
+    const bool pf = raw_prefetchable(W);
     RawUnit r0, r1;
     if (pf && live) {
-      if (nk > 0) load_raw(a.W, n, (kt0 + 0) * BK + 32 * h, K, r0);
-      if (nk > 1) load_raw(a.W, n, (kt0 + 1) * BK + 32 * h, K, r1);
+      if (nk > 0) load_raw(W, n, (kt0 + 0) * BK + 32 * h, K, r0);
+      if (nk > 1) load_raw(W, n, (kt0 + 1) * BK + 32 * h, K, r1);
     }
     for (int kt = 0; kt < nk; ++kt) {
       const int s = kt % STAGES;
@@ -373,10 +382,10 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
       } else if (pf) {
         const RawUnit cur = r0;
         r0 = r1;
-        if (kt + 2 < nk) load_raw(a.W, n, k0 + 2 * BK, K, r1);
-        decode_raw(a.W.scheme, k0, cur, w);
+        if (kt + 2 < nk) load_raw(W, n, k0 + 2 * BK, K, r1);
+        decode_raw(W.scheme, k0, cur, w);
       } else {
-        weight_unit(a.W, n, k0, K, w);
+        weight_unit(W, n, k0, K, w);
       }
       if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
       uint8_t* whi = smem + s * STAGE_BYTES + 2 * TILE_A;
@@ -448,7 +457,12 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
     if (ok) {
       const int m = m0 + warp * 32 + lane;
       const bool part = a.kslices > 1;
-      float* yr = part ? a.partial + ((int64_t)blockIdx.z * a.M + m) * a.N : a.y + (int64_t)m * a.ldy;
+      int sg = 0;
+      while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
+      const int nb = a.seg_n0[sg], ne = a.seg_n0[sg + 1];
+      // partial sums: [slice][M][N total]; final: the segment's own output, column n - nb
+      float* yr = part ? a.partial + ((int64_t)blockIdx.z * a.M + m) * a.N
+                       : a.seg_y[sg] + (int64_t)m * a.seg_ldy[sg] - nb;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t v[16];
@@ -457,7 +471,7 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int n = n0 + c0 + e;
-            if (n < a.N) {
+            if (n < ne) {
               const float r = __uint_as_float(v[e]);
               yr[n] = (a.accumulate && !part) ? yr[n] + r : r;
             }
@@ -528,15 +542,17 @@ __global__ void weight_split_kernel(const DevWeight W, int N, int K, uint4* __re
 }
 
 // y (+)= sum over the k slices of the partial tiles, in slice order
-__global__ void gemm_reduce_kernel(const float* __restrict__ part, int S, int M, int N, float* __restrict__ y,
-                                   int ldy, int accumulate) {
-  const int64_t MN = (int64_t)M * N;
+__global__ void gemm_reduce_kernel(const float* __restrict__ part, int S, const __grid_constant__ TcArgs a) {
+  const int64_t MN = (int64_t)a.M * a.N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < MN; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int z = 0; z < S; ++z) s += part[z * MN + i];
-    const int64_t m = i / N, n = i - m * N;
-    float* d = y + m * ldy + n;
-    *d = accumulate ? *d + s : s;
+    const int64_t m = i / a.N;
+    const int n = (int)(i - m * a.N);
+    int sg = 0;
+    while (sg + 1 < a.nseg && n >= a.seg_n0[sg + 1]) ++sg;
+    float* d = a.seg_y[sg] + m * a.seg_ldy[sg] + (n - a.seg_n0[sg]);
+    *d = a.accumulate ? *d + s : s;
   }
 }
 
@@ -585,10 +601,21 @@ bool gemm_tc_supports(const DevWeight& W, int M) {
   return false;
 }
 
-int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
-                   cudaStream_t st, int* n_launch) {
-  const int K = W.K(), N = W.N();
-  if (!gemm_tc_supports(W, M)) return SM_ERR_UNSUPPORTED;
+bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M) {
+  if (nw < 1 || nw > MAX_SEG) return false;
+  for (int i = 0; i < nw; ++i) {
+    if (!gemm_tc_supports(*W[i], M) || W[i]->K() != W[0]->K()) return false;
+    if (i + 1 < nw && W[i]->N() % BN) return false;  // segments meet on tile boundaries
+  }
+  return true;
+}
+
+int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
+                         int accumulate, int* status, cudaStream_t st, int* n_launch) {
+  if (!gemm_tc_supports_multi(Ws, nw, M)) return SM_ERR_UNSUPPORTED;
+  const int K = Ws[0]->K();
+  int N = 0;
+  for (int i = 0; i < nw; ++i) N += Ws[i]->N();
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -602,13 +629,13 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
   // more than one 128-row tile of x: dequantize W once into fp16 planes and feed
   // both operands by TMA; otherwise dequantize each weight tile in the kernel
   const bool wt = M > BM;
-  const int64_t n = (int64_t)M * K, nw = wt ? (int64_t)N * K : 0;
+  const int64_t n = (int64_t)M * K, nw_el = wt ? (int64_t)N * K : 0;
   void* planes = nullptr;
-  SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)(n + nw) * 4, st));
+  SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)(n + nw_el) * 4, st));
   __half* hi = (__half*)planes;
   __half* lo = hi + n;
   __half* whi = lo + n;
-  __half* wlo = whi + nw;
+  __half* wlo = whi + nw_el;
   int rc = SM_OK;
   {
     const int64_t n4 = n / 4;
@@ -616,10 +643,15 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
     gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
     if (n_launch) ++*n_launch;
     if (wt) {
-      const int64_t units = nw / 32;
-      weight_split_kernel<<<(int)std::min<int64_t>((units + 255) / 256, 148 * 16), 256, 0, st>>>(
-          W, N, K, (uint4*)whi, (uint4*)wlo);
-      if (n_launch) ++*n_launch;
+      int64_t row0 = 0;
+      for (int i = 0; i < nw; ++i) {
+        const int Ni = Ws[i]->N();
+        const int64_t units = (int64_t)Ni * K / 32;
+        weight_split_kernel<<<(int)std::min<int64_t>((units + 255) / 256, 148 * 16), 256, 0, st>>>(
+            *Ws[i], Ni, K, (uint4*)(whi + row0 * K), (uint4*)(wlo + row0 * K));
+        if (n_launch) ++*n_launch;
+        row0 += Ni;
+      }
     }
     CUtensorMap mh, ml, mwh, mwl;
     rc = make_plane_map(&mh, hi, M, K);
@@ -628,12 +660,17 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
     if (rc == SM_OK) rc = make_plane_map(&mwl, wt ? (void*)wlo : (void*)lo, wt ? N : M, K);
     if (rc == SM_OK) {
       TcArgs a;
-      a.W = W;
+      a.nseg = nw;
+      a.seg_n0[0] = 0;
+      for (int i = 0; i < nw; ++i) {
+        a.W[i] = *Ws[i];
+        a.seg_y[i] = ys[i];
+        a.seg_ldy[i] = ldys[i];
+        a.seg_n0[i + 1] = a.seg_n0[i] + Ws[i]->N();
+      }
       a.M = M;
       a.N = N;
       a.K = K;
-      a.y = y;
-      a.ldy = ldy;
       a.accumulate = accumulate;
       a.status = status;
       const int gn = (N + BN - 1) / BN, gm = (M + BM - 1) / BM;
@@ -665,7 +702,7 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
         if (rc == SM_OK) {
           const int64_t MN = (int64_t)M * N;
           const int blocks = (int)std::min<int64_t>((MN + 255) / 256, 148 * 8);
-          gemm_reduce_kernel<<<blocks, 256, 0, st>>>(a.partial, S, M, N, y, ldy, accumulate);
+          gemm_reduce_kernel<<<blocks, 256, 0, st>>>(a.partial, S, a);
           if (n_launch) ++*n_launch;
         }
         cudaFreeAsync(pbuf, st);
@@ -674,6 +711,14 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
   }
   cudaFreeAsync(planes, st);
   return rc;
+}
+
+int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
+                   cudaStream_t st, int* n_launch) {
+  const DevWeight* ws[1] = {&W};
+  float* ys[1] = {y};
+  const int ld[1] = {ldy};
+  return launch_gemm_tc_multi(ws, ys, ld, 1, x, M, accumulate, status, st, n_launch);
 }
 
 }  // namespace sm

@@ -54,6 +54,11 @@ int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch);
 bool gemm_tc_supports(const DevWeight& W, int M);
 int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
                    cudaStream_t st, int* n_launch);
+// up to 3 weights with the same K stacked along N, each with its own output (ys[i], row stride ldys[i]);
+// every weight but the last must have N % 128 == 0
+bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M);
+int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
+                         int accumulate, int* status, cudaStream_t st, int* n_launch);
 // Q4_K (INTENDED) y = W x on the int8 tensor-core path (mma.sync m16n8k32)
 int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
                         int* n_launch);

@@ -118,3 +118,44 @@ def test_device_mode_decode_loop(ctx, O):
         torch.cuda.synchronize()
     assert got == ref
     assert kv.length(0) == len(prompt) + 7
+
+
+@pytest.mark.parametrize("n_prompt", [40, 160])
+def test_long_prefill_tensor_core_path(ctx, O, n_prompt):
+    # prompts of >= 16 rows run the tcgen05 GEMMs (Q|K|V and gate|up as one stacked-weight
+    # GEMM each; > 128 rows through the fp16 weight planes) and the tcgen05 prefill attention
+    import smallmind_b200 as sm
+    cfg = dict(TINY, max_context=200)
+    host = O.make_model(cfg, _kq_schemes(O), seed=5)
+    model = sm.CudaModel.from_host(ctx, host)
+    kv = sm.KVCache(model, 1, 200)
+    prompt = np.random.RandomState(n_prompt).randint(0, cfg["vocab_size"], n_prompt).astype(np.int32)
+    t, lg = kv.prefill(0, prompt)
+    ref = O.model_forward(host, prompt, 1)[0]
+    assert cosine(lg, ref) >= 0.9999 and t == int(np.argmax(ref))
+    # one decode step on top of the long prefix
+    toks, lg2 = kv.decode([0], [t])
+    ref2 = O.model_forward(host, np.append(prompt, t).astype(np.int32), 1)[0]
+    assert cosine(lg2[0], ref2) >= 0.9999 and int(toks[0]) == int(np.argmax(ref2))
+
+
+def test_batched_decode_20_sequences(ctx, O):
+    # 20 rows per decode step: the batched forward runs the tcgen05 GEMM with split K
+    import smallmind_b200 as sm
+    cfg = dict(TINY, max_context=24)
+    host = O.make_model(cfg, _kq_schemes(O), seed=8)
+    model = sm.CudaModel.from_host(ctx, host)
+    n = 20
+    kv = sm.KVCache(model, n, 24)
+    rs = np.random.RandomState(4)
+    hist, nxt = [], []
+    for s in range(n):
+        p = rs.randint(0, cfg["vocab_size"], 3 + s % 5).astype(np.int32)
+        t, _ = kv.prefill(s, p, want_logits=False)
+        hist.append(list(p) + [t])
+        nxt.append(t)
+    toks, lg = kv.decode(list(range(n)), nxt)
+    for s in range(n):
+        ref = O.model_forward(host, np.array(hist[s], np.int32), 1)[0]
+        assert cosine(lg[s], ref) >= 0.9999
+        assert int(toks[s]) == int(np.argmax(ref))
