@@ -72,6 +72,29 @@ __device__ __forceinline__ void seg_rows(int rows, int i, int n, int& r0, int& r
   r1 = min(rows, 2 * (int)((int64_t)pairs * (i + 1) / n));
 }
 
+// Q|K|V: CTAs [cb[s], cb[s+1]) take segment s, in proportion to its bytes, so
+// every CTA runs one segment (one stage stream, one epilogue) per phase.
+__device__ __forceinline__ void qkv_split(const MegaLayer& L, int K, int grid, int (&cb)[4]) {
+  int64_t b[3], tot = 0;
+  for (int i = 0; i < 3; ++i) {
+    b[i] = (int64_t)L.qkv[i].rows * (row_bytes_fmt(L.qkv[i].fmt, K) + aux_row_bytes(L.qkv[i]));
+    tot += b[i];
+  }
+  cb[0] = 0;
+  cb[1] = (int)min((int64_t)grid - 2, max((int64_t)1, (grid * b[0] + tot / 2) / tot));
+  cb[2] = (int)min((int64_t)grid - 1, max((int64_t)cb[1] + 1, cb[1] + (grid * b[1] + tot / 2) / tot));
+  cb[3] = grid;
+}
+
+// segment rows of CTA `i` when CTAs [c0, c1) share the segment (none outside)
+__device__ __forceinline__ void seg_rows_in(int rows, int i, int c0, int c1, int& r0, int& r1) {
+  if (i < c0 || i >= c1) {
+    r0 = r1 = 0;
+    return;
+  }
+  seg_rows(rows, i - c0, c1 - c0, r0, r1);
+}
+
 struct Shared {
   uint64_t full[16];
   uint64_t empty[16];
@@ -92,7 +115,7 @@ struct Producer {
   int k = 0;  // stages issued
   bool ok = true;
 
-  __device__ void seg(const MegaSeg& s, int K, int /*rb*/, int phase) {
+  __device__ void seg(const MegaSeg& s, int K, int /*rb*/, int phase, int c0 = 0, int c1 = -1) {
     if (!ok) return;
     const int rb = stage_rows(s, K, slot_bytes);
     if (!a.lookahead) {
@@ -104,7 +127,7 @@ struct Producer {
         }
     }
     int r0, r1;
-    seg_rows(s.rows, blockIdx.x, gridDim.x, r0, r1);
+    seg_rows_in(s.rows, blockIdx.x, c0, c1 < 0 ? (int)gridDim.x : c1, r0, r1);
     const int64_t rbytes = row_bytes_fmt(s.fmt, K);
     const bool glu = s.mode == GEMV_GLU;
     for (int row = r0; row < r1; row += rb) {
@@ -305,10 +328,11 @@ struct Consumer {
   }
 
   // GEMV rows of this CTA for one segment; `amax` (head only) tracks the local argmax.
-  __device__ bool seg(const MegaSeg& s, int K, int /*rb*/, float* amax_v = nullptr, int* amax_i = nullptr) {
+  __device__ bool seg(const MegaSeg& s, int K, int /*rb*/, float* amax_v = nullptr, int* amax_i = nullptr,
+                      int c0 = 0, int c1 = -1) {
     const int rb = stage_rows(s, K, slot_bytes);
     int r0, r1;
-    seg_rows(s.rows, blockIdx.x, gridDim.x, r0, r1);
+    seg_rows_in(s.rows, blockIdx.x, c0, c1 < 0 ? (int)gridDim.x : c1, r0, r1);
     const int nout = r1 - r0;
     const int64_t rbytes = row_bytes_fmt(s.fmt, K);
     const bool glu = s.mode == GEMV_GLU;
@@ -607,7 +631,9 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
       Producer p{a, sh, ring, slot_bytes};
       for (int l = 0; l < a.n_layers; ++l) {
         const MegaLayer& L = a.layers[l];
-        for (int s = 0; s < 3; ++s) p.seg(L.qkv[s], a.H, a.stage_rows_h, 4 * l);
+        int cb[4];
+        qkv_split(L, a.H, gridDim.x, cb);
+        for (int s = 0; s < 3; ++s) p.seg(L.qkv[s], a.H, a.stage_rows_h, 4 * l, cb[s], cb[s + 1]);
         p.seg(L.o, a.qd, a.stage_rows_h, 4 * l + 1);
         p.seg(L.gu, a.H, a.stage_rows_h, 4 * l + 2);
         p.seg(L.down, a.F, a.stage_rows_f, 4 * l + 3);
@@ -667,8 +693,12 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     }
     c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, L.qkv[0].fmt != SM_Q8_0);
     if (tid == 0) sh.phase = 4 * l;
-    for (int s = 0; s < 3; ++s)
-      if (!c.seg(L.qkv[s], a.H, a.stage_rows_h)) return;
+    {
+      int cb[4];
+      qkv_split(L, a.H, gridDim.x, cb);
+      const int s = blockIdx.x < cb[1] ? 0 : (blockIdx.x < cb[2] ? 1 : 2);
+      if (!c.seg(L.qkv[s], a.H, a.stage_rows_h, nullptr, nullptr, cb[s], cb[s + 1])) return;
+    }
     if (!c.grid_barrier()) return;
     for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
     if (!c.grid_barrier()) return;
