@@ -446,12 +446,29 @@ struct Consumer {
     return true;
   }
 
+  // Shared-memory layout of the two attention phases (floats): the same CTA
+  // runs item (kv head g, chunk c) in both, so the scores and the chunk's V rows
+  // stay on chip across the barrier between them.
+  //   es [MGMAX][per]        scores of the chunk (phase A), exponentials (B)
+  //   pp [PH][MGMAX][64]     P.V partials (B); the q rows in phase A
+  //   cm [chunks][G]         chunk maxima (B)
+  //   vs [per][64]           V rows of the chunk (cp.async in A, read in B)
+  static constexpr int PH = CT / 64;
+  __device__ float* att_es() { return part; }
+  __device__ float* att_pp(int per) { return part + MGMAX * per; }
+  __device__ float* att_cm(int per) { return att_pp(per) + PH * MGMAX * 64; }
+  __device__ float* att_vs(int per, int chunks) {
+    float* v = att_cm(per) + chunks * MGMAX;
+    return (float*)(((uintptr_t)v + 15) & ~(uintptr_t)15);
+  }
+
   // ---- attention, phase A: scores and slice max of item (kv head g, chunk c)
   __device__ void attn_scores(const MegaLayer& L, int g, int c, int chunks, int len) {
     const int G = a.nH / a.nKv, HD = 64;
     const int per = (len + chunks - 1) / chunks;
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
-    float* qs = part;  // [G][64]
+    float* qs = att_pp(per);  // [G][64]
+    float* es = att_es();
     for (int t = tid; t < G * HD; t += CT) qs[t] = __ldcg(&a.q[g * G * HD + t]);
     cons_sync();
     const int64_t seq = *a.seq;
@@ -485,7 +502,7 @@ struct Consumer {
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         s += __shfl_xor_sync(0xffffffffu, s, 4);
         if (valid) {
-          if (sub == 0) a.scores[(int64_t)(g * G + h) * a.max_ctx + j0 + jj] = s;
+          if (sub == 0) es[h * per + jj] = s;
           lmax[h] = fmaxf(lmax[h], __fmul_rn(s, scale));
         }
       }
@@ -501,6 +518,14 @@ struct Consumer {
       for (int w = 0; w < CWARPS; ++w) m = fmaxf(m, sh.red[w * MGMAX + tid]);
       a.cmax[(g * chunks + c) * G + tid] = m;
     }
+    // the chunk's V rows (contiguous in the head-major cache) into shared memory
+    // with asynchronous copies that land while this CTA waits at the barrier
+    const float* vb = L.vc + ((seq * a.nKv + g) * (int64_t)a.max_ctx + j0) * HD;
+    float* vs = att_vs(per, chunks);
+    for (int t = tid; t < n * (HD / 4); t += CT)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(vs + 4 * t)), "l"(vb + 4 * t)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
     cons_sync();
   }
 
@@ -510,11 +535,11 @@ struct Consumer {
     const int per = (len + chunks - 1) / chunks;
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
     const float scale = 1.0f / sqrtf((float)HD);
-    float* es = part;                    // [G][per]
-    float* pp = part + MGMAX * per;      // [CT/64][G][64]
+    float* es = att_es();         // [G][per] scores from phase A
+    float* pp = att_pp(per);      // [PH][G][64]
     {
       // exact row max of every head of the group: all chunk maxima, gathered in parallel
-      float* cm = part + MGMAX * per + (CT / 64) * MGMAX * 64;  // [chunks][G]
+      float* cm = att_cm(per);  // [chunks][G]
       for (int t = tid; t < chunks * G; t += CT) cm[t] = __ldcg(&a.cmax[g * chunks * G + t]);
       cons_sync();
       if (tid < G) {
@@ -526,18 +551,13 @@ struct Consumer {
     }
     for (int t = tid; t < G * n; t += CT) {
       const int h = t / n, jj = t - h * n;
-      const float s = __ldcg(&a.scores[(int64_t)(g * G + h) * a.max_ctx + j0 + jj]);
-      es[h * per + jj] = pade_exp(__fsub_rn(__fmul_rn(s, scale), sh.vec[h]));
+      es[h * per + jj] = pade_exp(__fsub_rn(__fmul_rn(es[h * per + jj], scale), sh.vec[h]));
     }
+    // the V rows copied in phase A
+    asm volatile("cp.async.wait_all;" ::: "memory");
     cons_sync();
-    const int64_t seq = *a.seq;
-    const float* vb = L.vc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
-    constexpr int PH = CT / 64;  // 7 key phases
-    // the chunk's V rows (contiguous in the head-major cache) into shared memory in one pass
-    float* vs = part + MGMAX * per + PH * MGMAX * 64 + chunks * G;
-    for (int t = tid; t < n * (HD / 4); t += CT)
-      ((float4*)vs)[t] = __ldcg((const float4*)(vb + (int64_t)j0 * HD) + t);
-    cons_sync();
+    (void)L;
+    const float* vs = att_vs(per, chunks);
     const int d = tid % 64, kp = tid / 64;
     if (kp < PH) {
       float acc[MGMAX];
