@@ -313,10 +313,14 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     a.K = K;
     a.x = x;
     SM_TRY(gemv1_segment(a, W, nullptr, y, accumulate ? GEMV_ADD : GEMV_STORE));
-    // Q4_K: integer tensor-core GEMV (SMALLMIND_GEMV_MMA=0 selects the CUDA-core kernel)
+    // Q4_K / Q6_K: integer tensor-core GEMV (SMALLMIND_GEMV_MMA=0 selects the CUDA-core kernel)
     const char* em = std::getenv("SMALLMIND_GEMV_MMA");
     if (!(em && em[0] == '0') && W.scheme == SM_Q4_K) {
       const int rc = launch_gemv_mma_q4k(W, x, y, accumulate, nullptr, st, n_launch);
+      if (rc != SM_ERR_UNSUPPORTED) return rc;
+    }
+    if (!(em && em[0] == '0') && W.scheme == SM_Q6_K) {
+      const int rc = launch_gemv_mma_q6k(W, x, y, accumulate, nullptr, st, n_launch);
       if (rc != SM_ERR_UNSUPPORTED) return rc;
     }
     const char* e = std::getenv("SMALLMIND_GEMV_STREAM");

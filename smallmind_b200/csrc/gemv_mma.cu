@@ -66,6 +66,10 @@ struct MmaArgs {
   int64_t slot_bytes = 0;
   int plane_offset = 0, red_offset = 0, scw_offset = 0, ring_offset = 0;
   int* status = nullptr;
+  // Q6_K: fp16 d values in rows of aux_stride elements (16-byte padded), copied
+  // behind each staged row (abytes per row)
+  const uint16_t* aux = nullptr;
+  int aux_stride = 0, abytes = 0;
 };
 
 constexpr int SCW = 9;  // per-warp scale scratch row stride (floats): rows g = 0..7 on distinct banks
@@ -275,6 +279,226 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
   }
 }
 
+// ---------------------------------------------------------------- Q6_K
+// Q6_K on the same integer tensor-core path.  The 6-bit codes of a 32-weight
+// unit (Q6KTensor.cs:105-124: low nibble from ql, 2 high bits from qh) are
+// rebuilt per A fragment from the ql word and the re-packed high-bit plane of
+// the device layout: lane tig owns ql word tig (elements 8 tig .. 8 tig + 7),
+// even elements at k = 4 tig + i, odd at k = 16 + 4 tig + i.  A unit carries two
+// int8 scales (elements 0..15 and 16..31, lanes tig 0-1 and 2-3), so the B
+// operand holds six digit columns: columns 0..2 the digits of x for the first
+// half (zero at the second half's k positions), 3..5 for the second half.  One
+// MMA gives both halves' integer sums, each multiplied by its integer scale:
+//   sum_k w_k x_k = d 2^(e-22) sum_h sc_h (A_h 65536 + B_h 256 + C_h)
+//                   - 32 d sum_h sc_h (sum of x over half h).
+// x is 22-bit fixed point relative to its 256-element block's largest |x|.
+constexpr int SCW2 = 9;  // int2 per scale row (8 units + 1): rows g = 0..7 on distinct banks
+
+__global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __grid_constant__ MmaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = (uint64_t*)smem;  // [8]
+  uint64_t* empty = full + 8;        // [8]
+  uint2* planes = (uint2*)(smem + a.plane_offset);  // [U][6 columns][4 tig] (even, odd) digit words, then hsum, bexp
+  float* red = (float*)(smem + a.red_offset);       // [nslots][NB][ROWS] block partials
+  uint8_t* scw_all = smem + a.scw_offset;           // per warp: int2 [ROWS][SCW2], float msum[ROWS], fdv[ROWS]
+  uint8_t* ring = smem + a.ring_offset;
+  const int K = a.K, U = K >> 5, NB = K >> 8;
+  const uint32_t rbytes = (uint32_t)NB * Q6K_BODY_BYTES;
+  const int rs = a.row_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ngroups = (a.N + ROWS - 1) / ROWS;
+  const int g0 = (int)((int64_t)ngroups * blockIdx.x / gridDim.x);
+  const int g1 = (int)((int64_t)ngroups * (blockIdx.x + 1) / gridDim.x);
+  const int nst = g1 - g0;
+  float* hsum = (float*)(planes + U * 24);  // [U][2] sum of x over each 16-element half
+  float* bexp = hsum + 2 * U;               // [NB] 2^(e-22) of the block
+  if (tid == 0) {
+    for (int i = 0; i < a.nslots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NB);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == MM_CWARPS) {
+    auto issue = [&](int k) {
+      const int slot = k % a.nslots;
+      const int row = (g0 + k) * ROWS;
+      const int n = min(ROWS, a.N - row);
+      if (lane == 0) mbar_expect_tx(&full[slot], (uint32_t)n * (rbytes + a.abytes));
+      __syncwarp();
+      if (lane < n) {
+        uint8_t* dst = ring + slot * a.slot_bytes + lane * rs;
+        bulk_g2s(dst, a.w + (int64_t)(row + lane) * rbytes, rbytes, &full[slot]);
+        bulk_g2s(dst + rbytes, a.aux + (int64_t)(row + lane) * a.aux_stride, a.abytes, &full[slot]);
+      }
+    };
+    int next = 0;
+    for (; next < min(nst, a.nslots); ++next) issue(next);
+    if (lane == 0) asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // y may be the previous kernel's output
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int k = 0; k < nst; ++k) {
+      if (!mbar_wait_bounded(&empty[slot], phase, a.status)) return;
+      const int row0 = (g0 + k) * ROWS;
+      const int n = min(ROWS, a.N - row0);
+      if (lane < n) {
+        const float* rd = red + (slot * NB) * ROWS + lane;
+        float s = 0.f;
+        for (int b = 0; b < NB; ++b) s += rd[b * ROWS];
+        float* dst = a.y + row0 + lane;
+        *dst = a.accumulate ? *dst + s : s;
+      }
+      __syncwarp();
+      if (next < nst) issue(next++);
+      if (++slot == a.nslots) slot = 0, phase ^= 1;
+    }
+    return;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // ---- digit columns of x: one warp per 256-element block, four lanes per unit
+  for (int blk = warp; blk < NB; blk += MM_CWARPS) {
+    const int u = blk * 8 + (lane >> 2), p = lane & 3;
+    const float4* xp = (const float4*)(a.x + 32 * u + 8 * p);
+    const float4 v0 = __ldcg(xp), v1 = __ldcg(xp + 1);
+    const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float amax = 0.f, sx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      amax = fmaxf(amax, fabsf(xv[i]));
+      sx += xv[i];
+    }
+    sx += __shfl_xor_sync(0xffffffffu, sx, 1);  // the lane pair of one 16-element half
+    amax = warp_max(amax);
+    int ex = 0;
+    frexpf(amax, &ex);  // amax < 2^ex
+    const float up = ldexpf(1.f, 22 - ex);
+    uint32_t pw[2][3] = {};  // [even / odd][digit]
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int X = amax > 0.f ? __float2int_rn(xv[i] * up) : 0;  // |X| <= 2^22
+      const int c = ((X + 128) & 255) - 128;
+      const int X1 = (X - c) >> 8;
+      const int b = ((X1 + 128) & 255) - 128;
+      const int hi = (X1 - b) >> 8;
+      const int eo = i & 1, sh = 8 * (i >> 1);
+      pw[eo][0] |= (uint32_t)(hi & 255) << sh;
+      pw[eo][1] |= (uint32_t)(b & 255) << sh;
+      pw[eo][2] |= (uint32_t)(c & 255) << sh;
+    }
+    uint2* d = planes + u * 24 + p;
+    const int half = p >> 1;
+#pragma unroll
+    for (int col = 0; col < 6; ++col) {
+      const bool mine = (col / 3) == half;
+      d[4 * col] = mine ? make_uint2(pw[0][col % 3], pw[1][col % 3]) : make_uint2(0u, 0u);
+    }
+    if ((p & 1) == 0) hsum[2 * u + half] = sx;
+    if (lane == 0) bexp[blk] = ldexpf(1.f, ex - 22);
+  }
+  csync();
+  const int g = lane >> 2, tig = lane & 3;
+  // C columns of lane tig: 2 tig, 2 tig + 1 -> (half, digit) weights
+  const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : (tig == 2 ? 256.f : 0.f));
+  const float fB = tig == 0 ? 256.f : (tig == 1 ? 65536.f : (tig == 2 ? 1.f : 0.f));
+  const bool s0_first = tig < 2, s1_first = tig == 0;  // which half's scale meets d0 / d1
+  const int hshift = 4 * (tig & 1);                    // high-bit byte fields of this lane's elements
+  const uint2* pl = planes + (g < 6 ? g : 0) * 4 + tig;
+  int2* scw = (int2*)(scw_all + warp * (ROWS * SCW2 * 8 + 2 * ROWS * 4));
+  float* msum = (float*)(scw + ROWS * SCW2);
+  float* fdv = msum + ROWS;
+  const int sr = lane >> 1, shh = lane & 1;  // scale decode: row, half of the units
+  int k = 0, kb = warp, slot = 0;
+  uint32_t phase = 0;
+  while (kb >= NB) {
+    kb -= NB;
+    ++k;
+    if (++slot == a.nslots) slot = 0, phase ^= 1;
+  }
+  for (; k < nst;) {
+    if (!mbar_wait_bounded(&full[slot], phase, a.status)) return;
+    const uint8_t* st = ring + slot * a.slot_bytes;
+    const uint8_t* blk0 = st + kb * Q6K_BODY_BYTES;
+    const int row0 = (g0 + k) * ROWS;
+    const int n = min(ROWS, a.N - row0);
+    {
+      // int8 scales of units 4 shh .. 4 shh + 3 of row sr, the x-sum correction and d
+      const uint8_t* rp = st + min(sr, n - 1) * rs;
+      const int2 sc8 = *(const int2*)(rp + kb * Q6K_BODY_BYTES + 192 + 8 * shh);
+      const float d = __half2float(__ushort_as_half(*(const unsigned short*)(rp + rbytes + 2 * kb)));
+      const uint32_t sw[2] = {(uint32_t)sc8.x, (uint32_t)sc8.y};
+      const float* hs = hsum + 2 * (kb * 8 + 4 * shh);
+      float mpart = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int sa = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1))) & 0xFF);
+        const int sb = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1) + 8)) & 0xFF);
+        scw[sr * SCW2 + 4 * shh + jj] = make_int2(sa, sb);
+        mpart = fmaf((float)sa, hs[2 * jj], mpart);
+        mpart = fmaf((float)sb, hs[2 * jj + 1], mpart);
+      }
+      mpart += __shfl_xor_sync(0xffffffffu, mpart, 1);
+      if (shh == 0) {
+        msum[sr] = 32.f * d * mpart;
+        fdv[sr] = d * bexp[kb];
+      }
+    }
+    __syncwarp();
+    const uint8_t* rg = blk0 + min(g, n - 1) * rs;
+    const uint8_t* rg8 = blk0 + min(g + 8, n - 1) * rs;
+    const uint2* plu = pl + kb * 8 * 24;
+    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+#pragma unroll
+    for (int j0 = 0; j0 < 8; j0 += 4) {
+      int dd[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int jj = j0 + j;
+        const uint32_t w0 = *(const uint32_t*)(rg + 16 * jj + 4 * tig);
+        const uint32_t w1 = *(const uint32_t*)(rg8 + 16 * jj + 4 * tig);
+        const uint32_t W0 = *(const uint32_t*)(rg + 128 + 8 * jj + 4 * (tig >> 1)) >> hshift;
+        const uint32_t W1 = *(const uint32_t*)(rg8 + 128 + 8 * jj + 4 * (tig >> 1)) >> hshift;
+        // even elements: low nibbles + high bits at byte bits 4-5; odd: high nibbles + bits 6-7 of the field
+        const uint32_t e0 = (w0 & 0x0F0F0F0Fu) | ((W0 << 4) & 0x30303030u);
+        const uint32_t e1 = (w1 & 0x0F0F0F0Fu) | ((W1 << 4) & 0x30303030u);
+        const uint32_t o0 = ((w0 >> 4) & 0x0F0F0F0Fu) | ((W0 << 2) & 0x30303030u);
+        const uint32_t o1 = ((w1 >> 4) & 0x0F0F0F0Fu) | ((W1 << 2) & 0x30303030u);
+        const uint2 b = plu[24 * jj];
+        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], e0, e1, o0, o1, b.x, b.y);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int2 s0 = scw[g * SCW2 + j0 + j], s1 = scw[(g + 8) * SCW2 + j0 + j];
+        t0 += (s0_first ? s0.x : s0.y) * dd[j][0];
+        t1 += (s1_first ? s0.x : s0.y) * dd[j][1];
+        t2 += (s0_first ? s1.x : s1.y) * dd[j][2];
+        t3 += (s1_first ? s1.x : s1.y) * dd[j][3];
+      }
+    }
+    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
+    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    float* rd = red + (slot * NB) * ROWS;
+    if (tig == 0) {
+      rd[kb * ROWS + g] = fmaf(fdv[g], acc0, -msum[g]);
+      rd[kb * ROWS + g + 8] = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    __syncwarp();
+    kb += MM_CWARPS;
+    while (kb >= NB) {
+      kb -= NB;
+      ++k;
+      if (++slot == a.nslots) slot = 0, phase ^= 1;
+    }
+  }
+}
+
 }  // namespace
 
 int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
@@ -327,6 +551,67 @@ int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumu
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel, a));
+  if (n_launch) ++*n_launch;
+  return SM_OK;
+}
+
+int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
+                        int* n_launch) {
+  if (W.scheme != SM_Q6_K || W.layout != SM_LAYOUT_INTENDED || W.aux_stride <= 0) return SM_ERR_UNSUPPORTED;
+  const int K = W.K(), N = W.N(), U = K / 32;
+  if (K % 256 || U > 1024) return SM_ERR_UNSUPPORTED;
+  MmaArgs a;
+  a.w = (const uint8_t*)W.data;
+  a.aux = (const uint16_t*)W.aux;
+  a.aux_stride = W.aux_stride;
+  a.abytes = W.aux_stride * 2;
+  if (a.abytes % 16) return SM_ERR_UNSUPPORTED;
+  a.x = x;
+  a.y = y;
+  a.N = N;
+  a.K = K;
+  a.accumulate = accumulate;
+  a.status = status;
+  const int NB = K / 256;
+  const int64_t rbytes = (int64_t)NB * Q6K_BODY_BYTES;
+  // staged row = body + d row; stride an odd number of 16-byte units so rows
+  // g = 0..7 of a fragment load fall on distinct bank quads
+  int rs = (int)(rbytes + a.abytes);
+  if ((rs / 16) % 2 == 0) rs += 16;
+  a.row_stride = rs;
+  a.slot_bytes = (int64_t)ROWS * a.row_stride;
+  a.plane_offset = 256;
+  a.red_offset = a.plane_offset + U * (24 * 8 + 8) + NB * 4;
+  a.red_offset = (a.red_offset + 15) / 16 * 16;
+  a.scw_offset = a.red_offset + 8 * NB * ROWS * 4;
+  a.ring_offset = a.scw_offset + MM_CWARPS * (ROWS * SCW2 * 8 + 2 * ROWS * 4);
+  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
+  int optin = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const int64_t budget = optin - 1024 - a.ring_offset;
+  a.nslots = (int)std::min<int64_t>(8, budget / a.slot_bytes);
+  if (a.nslots < 2) return SM_ERR_UNSUPPORTED;
+  const size_t smem = (size_t)a.ring_offset + (size_t)a.nslots * a.slot_bytes;
+  static bool attr_set[64] = {};
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemv_mma_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
+    attr_set[dev] = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ngroups = (N + ROWS - 1) / ROWS;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(sms, ngroups));
+  cfg.blockDim = dim3(MM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q6k_kernel, a));
   if (n_launch) ++*n_launch;
   return SM_OK;
 }
