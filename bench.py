@@ -385,11 +385,22 @@ def run_ours(args):
     kv.reset(0)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.prefill_only and args.profile_region:
+        torch.cuda.profiler.start()
     e0.record(stream)
     t0_tok, _ = kv.prefill(0, prompt, want_logits=False)
     e1.record(stream)
     e1.synchronize()
+    if args.prefill_only and args.profile_region:
+        torch.cuda.profiler.stop()
     prefill_ms = e0.elapsed_time(e1)
+    if args.prefill_only:
+        if rank == 0:
+            print(json.dumps({"prefill_only": True, "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
+                              "prefill_ms": round(prefill_ms, 3), "prompt": args.prompt}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     seq = torch.zeros(1, dtype=torch.int32, device="cuda")
     tok = torch.tensor([t0_tok], dtype=torch.int32, device="cuda")
@@ -540,7 +551,10 @@ def main():
                     help="time M = 8, 64, 512, 2048 on the op-sweep shapes and exit")
     ap.add_argument("--gemv-only", default=None, help="restrict --gemv-sweep to 'SCHEME KxN' (profiling)")
     ap.add_argument("--profile-region", action="store_true",
-                    help="bracket the timed decode loop with cudaProfilerStart/Stop (ncu --profile-from-start off)")
+                    help="bracket the timed decode loop (or, with --prefill-only, the timed prefill) with "
+                         "cudaProfilerStart/Stop (ncu --profile-from-start off)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="time one warm prefill of the prompt and exit (with --profile-region: bracket it)")
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the device decode loop (profiling runs: no e2e, GEMV, bs64 or CPU legs)")
     args = ap.parse_args()

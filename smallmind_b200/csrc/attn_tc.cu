@@ -14,13 +14,14 @@
 // MMAs into an fp32 TMEM accumulator), ~2^-22 relative.  The Padé quotient uses
 // the hardware reciprocal (a few ulp), far inside the 1e-4 attention tolerance.
 //
-// Structure: one CTA per (q head, 128-query block), 320 threads.
-//   warps 0..7  softmax: TMEM lane = query row (warp % 4 selects the lane
-//               quarter), warps 0..3 take key columns 0..63 of each 128-key
-//               block, warps 4..7 columns 64..127; they also run the epilogue;
-//   warp 8      TMA: the q tile once, then per key block the k tile (pass 1)
+// Structure: one CTA per (q head, 128-query block), 576 threads.
+//   warps 0..15 softmax: TMEM lane = query row (warp % 4 selects the lane
+//               quarter), warp / 4 selects 32 of the 128 key columns of each
+//               block; key blocks wholly below the diagonal skip the mask; they
+//               also run the epilogue (16 of the 64 output dims each);
+//   warp 16     TMA: the q tile once, then per key block the k tile (pass 1)
 //               or the k and v^T tiles (pass 2), 128-byte swizzle, no multicast;
-//   warp 9      one lane issues the MMAs: S = Q K^T (M 128, N 128, K 64) and
+//   warp 17     one lane issues the MMAs: S = Q K^T (M 128, N 128, K 64) and
 //               O += P V (M 128, N 64, K 128).
 // TMEM: S in columns 0..127, O in 128..191.  All waits are bounded.
 #include <cuda.h>
@@ -38,10 +39,12 @@ namespace {
 constexpr int QB = 128;  // queries per CTA
 constexpr int KB = 128;  // keys per block
 constexpr int HD = 64;
-constexpr int THREADS = 320;
-constexpr int SOFT_WARPS = 8;
-constexpr int TMA_WARP = 8;
-constexpr int MMA_WARP = 9;
+constexpr int SOFT_WARPS = 16;
+constexpr int NQ = SOFT_WARPS / 4;  // key-column quarters of a block, one per warp set
+constexpr int CW = KB / NQ;         // key columns per softmax thread (32)
+constexpr int TMA_WARP = SOFT_WARPS;
+constexpr int MMA_WARP = SOFT_WARPS + 1;
+constexpr int THREADS = (SOFT_WARPS + 2) * 32;
 // shared memory (bytes); every tile 1024-aligned for the 128-byte swizzle
 constexpr int Q_PLANE = QB * HD * 2;         // 16 KB
 constexpr int K_PLANE = KB * HD * 2;         // 16 KB
@@ -251,9 +254,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(o_done);
     }
   } else {
-    // ---- softmax warps: row r, key columns [c0, c0 + 64) of each block
+    // ---- softmax warps: row r, key columns [c0, c0 + 32) of each block
     const int r = (warp & 3) * 32 + lane;
-    const int half = warp >> 2, c0 = half * 64;
+    const int qt = warp >> 2, c0 = qt * CW;
     const int qi = q0 + r;               // query row
     const bool live = qi < a.T;
     const int pos = off + qi;            // keys 0 .. pos
@@ -264,90 +267,109 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < nkb && ok; ++j) {
       ok = mbar_wait_bounded(s_full, j & 1, a.status);
       tc_fence_after();
-      uint32_t v[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(trow + TM_S + c0 + 16 * c, v[c]);
+      uint32_t v[2][16];
+      tmem_ld16(trow + TM_S + c0, v[0]);
+      tmem_ld16(trow + TM_S + c0 + 16, v[1]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(s_free);
+      // every key of this block is visible to every row of the CTA: no mask
+      const bool open = j * KB + KB - 1 <= off + q0;
+      if (open) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int key = j * KB + c0 + 16 * c + e;
-          if (key <= pos) m = fmaxf(m, __fmul_rn(__uint_as_float(v[c][e]), a.scale));
-        }
+          for (int e = 0; e < 16; ++e) m = fmaxf(m, __fmul_rn(__uint_as_float(v[c][e]), a.scale));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int key = j * KB + c0 + 16 * c + e;
+            if (key <= pos) m = fmaxf(m, __fmul_rn(__uint_as_float(v[c][e]), a.scale));
+          }
+      }
     }
-    xrow[half * QB + r] = m;
+    xrow[qt * QB + r] = m;
     asm volatile("bar.sync 1, %0;" ::"n"(SOFT_WARPS * 32) : "memory");
-    m = fmaxf(m, xrow[(1 - half) * QB + r]);
+#pragma unroll
+    for (int o = 0; o < NQ; ++o) m = fmaxf(m, xrow[o * QB + r]);
     asm volatile("bar.sync 1, %0;" ::"n"(SOFT_WARPS * 32) : "memory");  // before P overwrites the exchange
     // pass 2: e = FastExp(s * scale - m) -> P (fp16 hi / lo), row sums
     float sum = 0.f;
-    uint8_t* ph = smem + OFF_P + half * (P_PLANE / 2);
+    // columns [c0, c0 + 32): atom column qt / 2, 16-byte chunks 4 (qt % 2) .. + 3
+    uint8_t* ph = smem + OFF_P + (qt >> 1) * (P_PLANE / 2);
     uint8_t* pl = ph + P_PLANE;
+    const int chunk0 = 4 * (qt & 1);
     for (int j = 0; j < nkb && ok; ++j) {
       ok = mbar_wait_bounded(s_full, (nkb + j) & 1, a.status);
       tc_fence_after();
-      uint32_t v[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(trow + TM_S + c0 + 16 * c, v[c]);
+      uint32_t v[2][16];
+      tmem_ld16(trow + TM_S + c0, v[0]);
+      tmem_ld16(trow + TM_S + c0 + 16, v[1]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(s_free);
+      const bool open = live && j * KB + KB - 1 <= off + q0;
+      float ev[32];
+      if (open) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            ev[16 * c + e] = pade_exp_fast(__fsub_rn(__fmul_rn(__uint_as_float(v[c][e]), a.scale), m));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int key = j * KB + c0 + 16 * c + e;
+            ev[16 * c + e] = (live && key <= pos)
+                                 ? pade_exp_fast(__fsub_rn(__fmul_rn(__uint_as_float(v[c][e]), a.scale), m))
+                                 : 0.f;
+          }
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) sum += ev[e];
       // the previous block's P must have been consumed before it is overwritten
       if (j > 0 && ok) ok = mbar_wait_bounded(p_free, (j - 1) & 1, a.status);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int hc = 0; hc < 4; ++hc) {  // 16-byte chunks of 8 keys
+        uint32_t hp[4], lp[4];
 #pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {  // two 16-byte chunks of 8 keys
-          uint32_t hp[4], lp[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float ev[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int e = 8 * hc + 2 * e2 + t;
-              const int key = j * KB + c0 + 16 * c + e;
-              ev[t] = (live && key <= pos)
-                          ? pade_exp_fast(__fsub_rn(__fmul_rn(__uint_as_float(v[c][e]), a.scale), m))
-                          : 0.f;
-              sum += ev[t];
-            }
-            const __half2 hh = __floats2half2_rn(ev[0], ev[1]);
-            const float2 hf = __half22float2(hh);
-            const __half2 ll = __floats2half2_rn(ev[0] - hf.x, ev[1] - hf.y);
-            hp[e2] = *(const uint32_t*)&hh;
-            lp[e2] = *(const uint32_t*)&ll;
-          }
-          const uint32_t o = sw_off(r, 2 * c + hc);
-          *(uint4*)(ph + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
-          *(uint4*)(pl + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const float v0 = ev[8 * hc + 2 * e2], v1 = ev[8 * hc + 2 * e2 + 1];
+          const __half2 hh = __floats2half2_rn(v0, v1);
+          const float2 hf = __half22float2(hh);
+          const __half2 ll = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+          hp[e2] = *(const uint32_t*)&hh;
+          lp[e2] = *(const uint32_t*)&ll;
         }
+        const uint32_t o = sw_off(r, chunk0 + hc);
+        *(uint4*)(ph + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+        *(uint4*)(pl + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(p_full);
     }
-    // ---- epilogue: O row r, dims [32 half, 32 half + 32); after o_done no MMA reads P
+    // ---- epilogue: O row r, dims [16 qt, 16 qt + 16); after o_done no MMA reads P
     ok = ok && mbar_wait_bounded(o_done, 0, a.status);
     tc_fence_after();
-    xrow[half * QB + r] = sum;
+    xrow[qt * QB + r] = sum;
     asm volatile("bar.sync 1, %0;" ::"n"(SOFT_WARPS * 32) : "memory");
-    sum += xrow[(1 - half) * QB + r];
-    uint32_t ov[2][16];
-    tmem_ld16(trow + TM_O + 32 * half, ov[0]);
-    tmem_ld16(trow + TM_O + 32 * half + 16, ov[1]);
+    sum = 0.f;
+#pragma unroll
+    for (int o = 0; o < NQ; ++o) sum += xrow[o * QB + r];
+    uint32_t ov[16];
+    tmem_ld16(trow + TM_O + 16 * qt, ov);
     tmem_wait_ld();
     if (ok && live) {
       const float inv = __fdiv_rn(1.f, sum);
-      float* o = a.out + (int64_t)qi * a.out_stride + h * HD + 32 * half;
+      float* o = a.out + (int64_t)qi * a.out_stride + h * HD + 16 * qt;
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          *(float4*)(o + 16 * c + e) =
-              make_float4(__uint_as_float(ov[c][e]) * inv, __uint_as_float(ov[c][e + 1]) * inv,
-                          __uint_as_float(ov[c][e + 2]) * inv, __uint_as_float(ov[c][e + 3]) * inv);
+      for (int e = 0; e < 16; e += 4)
+        *(float4*)(o + e) = make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
+                                        __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
     }
   }
   tc_fence_before();

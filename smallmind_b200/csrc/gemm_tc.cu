@@ -331,7 +331,9 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  // x-row tiles vary fastest: consecutive CTAs share one weight tile, which then
+  // comes from L2 for all the row tiles instead of from DRAM once per row tile
+  const int n0 = blockIdx.y * BN, m0 = blockIdx.x * BM;
   const int K = a.K;
   const int nk_all = K / BK;
   const int kt0 = (int)((int64_t)nk_all * blockIdx.z / a.kslices);
@@ -691,7 +693,7 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
         }
         a.partial = (float*)pbuf;
       }
-      dim3 grid(gn, gm, S);
+      dim3 grid(gm, gn, S);
       if (wt)
         gemm_tc_kernel<true><<<grid, Roles<true>::THREADS, SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
       else
