@@ -169,6 +169,14 @@ struct Consumer {
   int k = 0;  // stages consumed
   unsigned barrier_gen = 0;
   int ev = 0;
+  int lx = 0;  // load_x calls (trace: the sub-steps of calls 4..11 go to events 900..)
+  __device__ void stamp_at(int e) {
+    if (a.trace && tid == 0 && e < MEGA_TRACE_EVENTS) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.trace[(size_t)blockIdx.x * MEGA_TRACE_EVENTS + e] = t;
+    }
+  }
   __device__ void stamp() {
     if (a.trace && tid == 0 && ev < MEGA_TRACE_EVENTS) {
       unsigned long long t;
@@ -224,7 +232,9 @@ struct Consumer {
     x_gamma = gamma;
     x_K = K;
     pair = want_pair;
-    float xr[32];
+    const int lxe = (lx >= 4 && lx < 12) ? 900 + 8 * (lx - 4) : -1;
+    ++lx;
+    if (lxe >= 0) stamp_at(lxe);
     // warp w covers units (w % nwpp)*32 + lane of row phase w / nwpp, so a warp's
     // partials for one row can be reduced with shuffles inside the compute loop
     U = K >> 5;
@@ -240,39 +250,97 @@ struct Consumer {
     // different bank groups.
     float4* xs = (float4*)part;        // [K/4]
     float4* gs = (float4*)part + K / 4; // [K/4]
+    uint32_t* pls = (uint32_t*)(part + 2 * K);  // [U][28]: planes a, b, c (8 words each), inv, x16a, x16b
     for (int t = tid; t < K / 4; t += CT) {
       const int w = t >> 3, p = (w << 3) + (((t & 7) + w) & 7);
       xs[p] = __ldcg((const float4*)src + t);
       if (gamma) gs[p] = __ldg((const float4*)gamma + t);
     }
+    if (lxe >= 0) stamp_at(lxe + 1);
     cons_sync();
+    if (lxe >= 0) stamp_at(lxe + 2);
+    // The byte planes of every unit, built once per CTA: four threads per unit,
+    // eight elements each, from y = gamma * x (the RMS scale is a per-vector
+    // scalar and is folded into each unit's factor below); the same pass
+    // accumulates sum(x^2) for RMSNorm.
+    float sq = 0.f;
+    for (int t0 = (tid >> 5) * 32; t0 < 4 * U; t0 += CT) {
+      const int t = t0 + (tid & 31);
+      const bool on = t < 4 * U;
+      const int uu = on ? t >> 2 : 0, pp = t & 3;
+      const float4 v0 = xs[(uu << 3) + ((2 * pp + uu) & 7)], v1 = xs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+      float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      if (gamma) {
+        const float4 g0 = gs[(uu << 3) + ((2 * pp + uu) & 7)], g1 = gs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float4 v = xs[(u << 3) + ((c + u) & 7)];
-      xr[4 * c] = v.x; xr[4 * c + 1] = v.y; xr[4 * c + 2] = v.z; xr[4 * c + 3] = v.w;
-    }
-    if (gamma) {
-      float ss = 0.f;
-      if (ph == 0 && u_ok)
+        for (int i = 0; i < 8; ++i) {
+          if (on) sq = fmaf(y[i], y[i], sq);
+          y[i] = __fmul_rn(gv[i], y[i]);
+        }
+      }
+      float am = 0.f, sp = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ss = fmaf(xr[i], xr[i], ss);
-      ss = warp_sum(ss);
-      if ((tid & 31) == 0) sh.red[tid >> 5] = ss;
-      cons_sync();
-      float tot = 0.f;
-      for (int w = 0; w < CWARPS; ++w) tot += sh.red[w];
-      const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+      for (int i = 0; i < 8; i += 2) {
+        am = fmaxf(am, fmaxf(fabsf(y[i]), fabsf(y[i + 1])));
+        sp += y[i] + y[i + 1];
+      }
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      sp += __shfl_xor_sync(0xffffffffu, sp, 1);  // elements 0..15 (parts 0, 1) or 16..31 (2, 3)
+      int ex = 0;
+      frexpf(am, &ex);  // am < 2^ex
+      const float up = ldexpf(1.f, 23 - ex);
+      uint32_t X[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 gv = gs[(u << 3) + ((c + u) & 7)];
-        xr[4 * c] = __fmul_rn(gv.x, __fmul_rn(xr[4 * c], inv));
-        xr[4 * c + 1] = __fmul_rn(gv.y, __fmul_rn(xr[4 * c + 1], inv));
-        xr[4 * c + 2] = __fmul_rn(gv.z, __fmul_rn(xr[4 * c + 2], inv));
-        xr[4 * c + 3] = __fmul_rn(gv.w, __fmul_rn(xr[4 * c + 3], inv));
+      for (int i = 0; i < 8; ++i) X[i] = am > 0.f ? (uint32_t)__float2int_rn(y[i] * up) : 0u;
+      // PAIR: word pp = elements 8pp + 0, 2, 4, 6; word 4 + pp = 8pp + 1, 3, 5, 7.
+      // NATURAL: words 2pp, 2pp + 1 = elements 8pp .. 8pp + 3, 8pp + 4 .. + 7.
+      const int w0 = pair ? pp : 2 * pp, w1 = pair ? 4 + pp : 2 * pp + 1;
+      const uint32_t e0 = pair ? X[0] : X[0], e1 = pair ? X[2] : X[1], e2 = pair ? X[4] : X[2], e3 = pair ? X[6] : X[3];
+      const uint32_t o0 = pair ? X[1] : X[4], o1 = pair ? X[3] : X[5], o2 = pair ? X[5] : X[6], o3 = pair ? X[7] : X[7];
+      if (on) {
+        uint32_t* d = pls + uu * 28;
+        d[w0] = __byte_perm(__byte_perm(e0, e1, 0x0062), __byte_perm(e2, e3, 0x0062), 0x5410);
+        d[8 + w0] = __byte_perm(__byte_perm(e0, e1, 0x0051), __byte_perm(e2, e3, 0x0051), 0x5410);
+        d[16 + w0] = __byte_perm(__byte_perm(e0, e1, 0x0040), __byte_perm(e2, e3, 0x0040), 0x5410);
+        d[w1] = __byte_perm(__byte_perm(o0, o1, 0x0062), __byte_perm(o2, o3, 0x0062), 0x5410);
+        d[8 + w1] = __byte_perm(__byte_perm(o0, o1, 0x0051), __byte_perm(o2, o3, 0x0051), 0x5410);
+        d[16 + w1] = __byte_perm(__byte_perm(o0, o1, 0x0040), __byte_perm(o2, o3, 0x0040), 0x5410);
+        if (pp == 0) {
+          d[24] = __float_as_uint(ldexpf(1.f, ex - 23));
+          d[25] = __float_as_uint(sp);
+        }
+        if (pp == 2) d[26] = __float_as_uint(sp);
       }
     }
+    if (gamma) {
+      sq = warp_sum(sq);
+      if ((tid & 31) == 0) sh.red[tid >> 5] = sq;
+    }
+    if (lxe >= 0) stamp_at(lxe + 3);
+    cons_sync();
+    if (lxe >= 0) stamp_at(lxe + 4);
+    float inv = 1.f;
+    if (gamma) {
+      float tot = 0.f;
+      for (int w = 0; w < CWARPS; ++w) tot += sh.red[w];
+      inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    }
+    const uint4* q4 = (const uint4*)(pls + u * 28);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 va = q4[c], vb = q4[2 + c], vc = q4[4 + c];
+      xp.a[4 * c] = va.x; xp.a[4 * c + 1] = va.y; xp.a[4 * c + 2] = va.z; xp.a[4 * c + 3] = va.w;
+      xp.b[4 * c] = vb.x; xp.b[4 * c + 1] = vb.y; xp.b[4 * c + 2] = vb.z; xp.b[4 * c + 3] = vb.w;
+      xp.c[4 * c] = vc.x; xp.c[4 * c + 1] = vc.y; xp.c[4 * c + 2] = vc.z; xp.c[4 * c + 3] = vc.w;
+    }
+    const uint4 hd4 = q4[6];
+    xp.inv = __uint_as_float(hd4.x) * inv;
+    xp.x16a = __uint_as_float(hd4.y) * inv;
+    xp.x16b = __uint_as_float(hd4.z) * inv;
     cons_sync();  // staging area (part) and sh.red are reused next
-    make_planes(xr, pair, xp);
+    if (lxe >= 0) stamp_at(lxe + 5);
   }
 
   // one unit of a staged row (integer dot path); `auxp` is the row's staged scales / d
@@ -837,7 +905,7 @@ int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch) {
                                  (int64_t)cta_rows(a.V) * nwpp(a.H), (int64_t)MGMAX * (a.max_ctx / 2 + 64) + 4096,
                                  (int64_t)(MGMAX + 64) * (a.max_ctx / std::max(1, grid / a.nKv) + 2) + 4096 +
                                      (int64_t)std::max(1, grid / a.nKv) * MGMAX,
-                                 (int64_t)2 * std::max({a.H, a.qd, a.F})});
+                                 (int64_t)2 * std::max({a.H, a.qd, a.F}) + 28 * (std::max({a.H, a.qd, a.F}) / 32) + 64});
   a.part_floats = (int)part;
   const int shared_bytes = (int)((sizeof(Shared) + 127) / 128 * 128);
   a.ring_offset = (int)((shared_bytes + part * 4 + 127) / 128 * 128);
