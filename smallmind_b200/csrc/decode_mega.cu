@@ -169,6 +169,7 @@ struct Consumer {
   int k = 0;  // stages consumed
   unsigned barrier_gen = 0;
   int ev = 0;
+  int seq_v = 0;  // the sequence id (read once)
   int lx = 0;  // load_x calls (trace: the sub-steps of calls 4..11 go to events 900..)
   __device__ void stamp_at(int e) {
     if (a.trace && tid == 0 && e < MEGA_TRACE_EVENTS) {
@@ -539,7 +540,7 @@ struct Consumer {
     float* es = att_es();
     for (int t = tid; t < G * HD; t += CT) qs[t] = __ldcg(&a.q[g * G * HD + t]);
     cons_sync();
-    const int64_t seq = *a.seq;
+    const int64_t seq = seq_v;
     const float* kb = L.kc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
     const int sub = tid & 7, slot = tid >> 3;  // 60 key slots
     constexpr int SLOTS = CT / 8;
@@ -708,7 +709,13 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  const int len = a.kv_len[*a.seq] + 1;  // context including this token
+  // the sequence id is read once: every later use (attention, KV append, the L2
+  // prefetch of the layer's K/V rows) reads the shared copy
+  __shared__ int seq_s;
+  if (tid == 0) seq_s = *a.seq;
+  __syncthreads();
+  const int seqv = seq_s;
+  const int len = a.kv_len[seqv] + 1;  // context including this token
   if (len > a.max_ctx) {
     if (tid == 0 && blockIdx.x == 0) atomicExch(a.status, SM_ERR_SHAPE);
     return;
@@ -738,8 +745,9 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   // -------------------------------------------------------------- consumers
   Consumer c{a, sh, ring, slot_bytes, part};
   c.tid = tid;
+  c.seq_v = seqv;
   c.ep.pos = nullptr;
-  c.ep.seq = a.seq;
+  c.ep.seq = &seq_s;
   c.ep.head_dim = a.hd;
   c.ep.n_kv = a.nKv;
   c.ep.max_ctx = a.max_ctx;
@@ -768,17 +776,6 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     const MegaLayer& L = a.layers[l];
     // Q|K|V with RMSNorm; RoPE and the KV append in the epilogue
     if (l > 0 && !c.grid_barrier()) return;
-    // this CTA's attention chunks of the layer: K / V rows into L2 ahead of the attention phases
-    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
-      const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
-      const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
-      const int64_t off = ((int64_t)(*a.seq) * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
-      const int lines = (j1 - j0) * 2;  // 256-byte rows
-      for (int t = tid; t < 2 * lines; t += CT) {
-        const float* base = (t < lines ? L.kc : L.vc) + off;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
-      }
-    }
     c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, L.qkv[0].fmt != SM_Q8_0);
     if (tid == 0) sh.phase = 4 * l;
     {
@@ -787,6 +784,19 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
       const int s = blockIdx.x < cb[1] ? 0 : (blockIdx.x < cb[2] ? 1 : 2);
       if (!c.seg(L.qkv[s], a.H, a.stage_rows_h, nullptr, nullptr, cb[s], cb[s + 1])) return;
     }
+    // this CTA's attention chunks of the layer: K / V rows into L2 while it waits at
+    // the barrier (issued after the vector loads, which they would otherwise delay)
+    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
+      const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
+      const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
+      const int64_t off = ((int64_t)seqv * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
+      const int lines = (j1 - j0) * 2;  // 256-byte rows
+      for (int t = tid; t < 2 * lines; t += CT) {
+        const float* base = (t < lines ? L.kc : L.vc) + off;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
+      }
+    }
+
     if (!c.grid_barrier()) return;
     for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
     if (!c.grid_barrier()) return;
@@ -844,7 +854,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     }
     if (tid == 0) {
       *a.next_token = bi;
-      a.kv_len[*a.seq] = len;
+      a.kv_len[seqv] = len;
     }
   }
 }
