@@ -681,7 +681,8 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       const int nk = K / BK;
       int S = 1;
-      if (gn * gm < sms) S = std::max(1, std::min((sms + gn * gm - 1) / (gn * gm), nk / 2));
+      // (one wave: at most one CTA per SM)
+      if (gn * gm < sms) S = std::max(1, std::min(sms / (gn * gm), nk / 2));
       a.kslices = S;
       a.partial = nullptr;
       void* pbuf = nullptr;
