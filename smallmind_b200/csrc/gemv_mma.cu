@@ -70,19 +70,27 @@ struct MmaArgs {
   // behind each staged row (abytes per row)
   const uint16_t* aux = nullptr;
   int aux_stride = 0, abytes = 0;
+  // Q4_K with several x rows: M rows of x (stride K), y rows of stride ldy
+  int M = 1, ldy = 0;
 };
 
 constexpr int SCW = 9;  // per-warp scale scratch row stride (floats): rows g = 0..7 on distinct banks
 
+// MX x rows (1, 2 or 4): B holds three digit columns per x row (column 3 m + q),
+// NMMA = ceil(3 MX / 8) MMAs per unit share one A fragment; columns past 3 M
+// load a real column and meet a zero weight.
+template <int MX>
 __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __grid_constant__ MmaArgs a) {
+  constexpr int NC = 3 * MX;            // digit columns stored per unit
+  constexpr int NMMA = (NC + 7) / 8;    // MMAs per unit
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = (uint64_t*)smem;  // [8]
   uint64_t* empty = full + 8;        // [8]
-  uint32_t* planes = (uint32_t*)(smem + a.plane_offset);  // [U][3][4][2] words, then usum, bexp
-  float* red = (float*)(smem + a.red_offset);             // [nslots][NB][ROWS] block partials
-  float* scw_all = (float*)(smem + a.scw_offset);         // [MM_CWARPS][ROWS * SCW + 2 * ROWS]
+  uint2* planes = (uint2*)(smem + a.plane_offset);  // [U][NC][4 tig] (k 4 tig + i, k 16 + 4 tig + i) words
+  float* red = (float*)(smem + a.red_offset);       // [nslots][NB][MX][ROWS] block partials
+  float* scw_all = (float*)(smem + a.scw_offset);   // per warp: int [ROWS][SCW], msum [MX][ROWS], fdv [MX][ROWS]
   uint8_t* ring = smem + a.ring_offset;
-  const int K = a.K, U = K >> 5, NB = K >> 8;
+  const int K = a.K, U = K >> 5, NB = K >> 8, M = a.M;
   const uint32_t rbytes = (uint32_t)NB * Q4K_BLOCK_BYTES;
   const int rs = a.row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -90,8 +98,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
   const int g0 = (int)((int64_t)ngroups * blockIdx.x / gridDim.x);
   const int g1 = (int)((int64_t)ngroups * (blockIdx.x + 1) / gridDim.x);
   const int nst = g1 - g0;
-  float* usum = (float*)(planes + U * 24);  // [U] sum of x over the unit
-  float* bexp = usum + U;                   // [NB] 2^(e-21) of the block
+  float* usum = (float*)(planes + U * NC * 4);  // [MX][U] sum of x over the unit
+  float* bexp = usum + MX * U;                  // [MX][NB] 2^(e-21) of the block
   if (tid == 0) {
     for (int i = 0; i < a.nslots; ++i) {
       mbar_init(&full[i], 1);
@@ -124,12 +132,15 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
       if (!mbar_wait_bounded(&empty[slot], phase, a.status)) return;
       const int row0 = (g0 + k) * ROWS;
       const int n = min(ROWS, a.N - row0);
-      if (lane < n) {
-        const float* rd = red + (slot * NB) * ROWS + lane;
-        float s = 0.f;
-        for (int b = 0; b < NB; ++b) s += rd[b * ROWS];
-        float* dst = a.y + row0 + lane;
-        *dst = a.accumulate ? *dst + s : s;
+      for (int t = lane; t < M * ROWS; t += 32) {
+        const int m = t / ROWS, r = t - m * ROWS;
+        if (r < n) {
+          const float* rd = red + (slot * NB * MX + m) * ROWS + r;
+          float s = 0.f;
+          for (int b = 0; b < NB; ++b) s += rd[b * MX * ROWS];
+          float* dst = a.y + (int64_t)m * a.ldy + row0 + r;
+          *dst = a.accumulate ? *dst + s : s;
+        }
       }
       __syncwarp();
       if (next < nst) issue(next++);
@@ -138,11 +149,12 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
     return;
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // ---- digit planes of x: one warp per 256-element block, four lanes per
-  // unit, eight elements per lane; one exponent per block
-  for (int blk = warp; blk < NB; blk += MM_CWARPS) {
+  // ---- digit planes of x: one warp per (x row, 256-element block), four lanes
+  // per unit, eight elements per lane; one exponent per (row, block)
+  for (int it = warp; it < M * NB; it += MM_CWARPS) {
+    const int m = it / NB, blk = it - m * NB;
     const int u = blk * 8 + (lane >> 2), p = lane & 3;
-    const float4* xp = (const float4*)(a.x + 32 * u + 8 * p);
+    const float4* xp = (const float4*)(a.x + (int64_t)m * K + 32 * u + 8 * p);
     const float4 v0 = __ldcg(xp), v1 = __ldcg(xp + 1);
     const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     float amax = 0.f, sx = 0.f;
@@ -158,7 +170,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
     frexpf(amax, &ex);  // amax < 2^ex
     const float up = ldexpf(1.f, 21 - ex), uph = ldexpf(1.f, 17 - ex);
     // B fragment of lane (column q, tig): word 0 = values at k = 4 tig + i,
-    // word 1 = values at k = 16 + 4 tig + i; stored together at [u][q][tig][2]
+    // word 1 = values at k = 16 + 4 tig + i
     uint32_t pw[2][3] = {};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -177,22 +189,25 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
         pw[h][2] |= (uint32_t)(c & 255) << (8 * i);
       }
     }
-    uint2* d = (uint2*)(planes + u * 24) + p;
+    uint2* d = planes + (u * NC + 3 * m) * 4 + p;
 #pragma unroll
     for (int q = 0; q < 3; ++q) d[4 * q] = make_uint2(pw[0][q], pw[1][q]);
-    if (p == 0) usum[u] = sx;
-    if (lane == 0) bexp[blk] = ldexpf(1.f, ex - 21);
+    if (p == 0) usum[m * U + u] = sx;
+    if (lane == 0) bexp[m * NB + blk] = ldexpf(1.f, ex - 21);
   }
   csync();
   const int g = lane >> 2, tig = lane & 3;
-  // C columns: 0 = A (x 65536), 1 = B (x 256), 2 = C (x 1); lane tig holds columns 2 tig, 2 tig + 1
-  const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : 0.f);
-  const float fB = tig == 0 ? 256.f : 0.f;
-  // lanes of columns 3..7 load column g % 3 as well: their sums meet zero multipliers
-  const uint2* pl = (const uint2*)(planes + (g % 3) * 8) + tig;
-  float* scw = scw_all + warp * (ROWS * SCW + 2 * ROWS);
-  float* msum = scw + ROWS * SCW;
-  float* fdv = msum + ROWS;
+  // lane (g, tig), MMA mi: B column 8 mi + g (a real column when past 3 M);
+  // C columns 8 mi + 2 tig + {0, 1} = x row c / 3, digit c % 3 (x 65536, 256, 1)
+  const uint2* pl[NMMA];
+#pragma unroll
+  for (int mi = 0; mi < NMMA; ++mi) {
+    const int c = 8 * mi + g;
+    pl[mi] = planes + (c < 3 * M ? c : 0) * 4 + tig;
+  }
+  float* scw = scw_all + warp * (ROWS * SCW + 2 * MX * ROWS);
+  float* msum = scw + ROWS * SCW;  // [MX][ROWS]
+  float* fdv = msum + MX * ROWS;   // [MX][ROWS]
   const int sr = lane >> 1, sh = lane & 1;  // scale decode: row, half of the sub-blocks
   // item (tile k, block kb) = warp, warp + MM_CWARPS, ... of nst * NB, walked without divisions
   int k = 0, kb = warp, slot = 0;
@@ -210,62 +225,99 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
     {
       // sub-block scales and mins of row sr, sub-blocks 4 sh .. 4 sh + 3
       // (Q4KTensor.cs:109-132): six-bit scales kept as integers, the mins
-      // folded with the unit sums of x, d with the block's x exponent
+      // folded with each x row's unit sums, d with the row's block exponent
       const int4 hdr = *(const int4*)(st + min(sr, n - 1) * rs);
       const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
       const float dmin = __half2float(__ushort_as_half((unsigned short)((uint32_t)hdr.x >> 16)));
       const uint64_t sb = (uint32_t)hdr.y | ((uint64_t)((uint32_t)hdr.z & 0xFFFFu) << 32);
       const uint64_t mb = ((uint32_t)hdr.z >> 16) | ((uint64_t)(uint32_t)hdr.w << 16);
       const uint32_t s24 = (uint32_t)(sb >> (24 * sh)), m24 = (uint32_t)(mb >> (24 * sh));
-      const float4 q = *(const float4*)(usum + kb * 8 + 4 * sh);
       int* si = (int*)scw + sr * SCW + 4 * sh;
 #pragma unroll
       for (int j = 0; j < 4; ++j) si[j] = (s24 >> (6 * j)) & 63;
-      float mpart = (float)(m24 & 63) * q.x;
-      mpart = fmaf((float)((m24 >> 6) & 63), q.y, mpart);
-      mpart = fmaf((float)((m24 >> 12) & 63), q.z, mpart);
-      mpart = fmaf((float)((m24 >> 18) & 63), q.w, mpart);
-      mpart = dmin * (mpart + __shfl_xor_sync(0xffffffffu, mpart, 1));
-      if (sh == 0) {
-        msum[sr] = mpart;
-        fdv[sr] = d * bexp[kb];
+      const float m0 = (float)(m24 & 63), m1 = (float)((m24 >> 6) & 63), m2 = (float)((m24 >> 12) & 63),
+                  m3 = (float)((m24 >> 18) & 63);
+#pragma unroll
+      for (int m = 0; m < MX; ++m) {
+        if (m >= M) break;
+        const float4 q = *(const float4*)(usum + m * U + kb * 8 + 4 * sh);
+        float mpart = m0 * q.x;
+        mpart = fmaf(m1, q.y, mpart);
+        mpart = fmaf(m2, q.z, mpart);
+        mpart = fmaf(m3, q.w, mpart);
+        mpart = dmin * (mpart + __shfl_xor_sync(0xffffffffu, mpart, 1));
+        if (sh == 0) {
+          msum[m * ROWS + sr] = mpart;
+          fdv[m * ROWS + sr] = d * bexp[m * NB + kb];
+        }
       }
     }
     __syncwarp();
     const uint8_t* rg = st + min(g, n - 1) * rs + 16 + 4 * tig;
     const uint8_t* rg8 = st + min(g + 8, n - 1) * rs + 16 + 4 * tig;
-    const uint2* plu = pl + kb * 8 * 12;
+    const int ustride = NC * 4;  // uint2 per unit
+    const int ub = kb * 8 * ustride;
     const int* si = (const int*)scw;
-    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;  // C columns (2 tig, 2 tig + 1) of rows g and g + 8, scaled
-    // four independent MMAs in flight, then their epilogues
+    int t[NMMA][4];
+#pragma unroll
+    for (int mi = 0; mi < NMMA; ++mi) t[mi][0] = t[mi][1] = t[mi][2] = t[mi][3] = 0;
+    // four units in flight, then their epilogues
 #pragma unroll
     for (int j0 = 0; j0 < 8; j0 += 4) {
-      int dd[4][4];
+      int dd[4][NMMA][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t w0 = *(const uint32_t*)(rg + 16 * (j0 + j));
         const uint32_t w1 = *(const uint32_t*)(rg8 + 16 * (j0 + j));
-        const uint2 b = plu[12 * (j0 + j)];
-        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, w0, w1, b.x, b.y);
+        const uint32_t lo0 = w0 & 0x0F0F0F0Fu, lo1 = w1 & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int mi = 0; mi < NMMA; ++mi) {
+          const uint2 b = pl[mi][ub + (j0 + j) * ustride];
+          mma_u8s8(dd[j][mi][0], dd[j][mi][1], dd[j][mi][2], dd[j][mi][3], lo0, lo1, w0, w1, b.x, b.y);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int s0 = si[g * SCW + j0 + j], s1 = si[(g + 8) * SCW + j0 + j];
-        t0 += s0 * dd[j][0];
-        t1 += s0 * dd[j][1];
-        t2 += s1 * dd[j][2];
-        t3 += s1 * dd[j][3];
+#pragma unroll
+        for (int mi = 0; mi < NMMA; ++mi) {
+          t[mi][0] += s0 * dd[j][mi][0];
+          t[mi][1] += s0 * dd[j][mi][1];
+          t[mi][2] += s1 * dd[j][mi][2];
+          t[mi][3] += s1 * dd[j][mi][3];
+        }
       }
     }
-    // |t| < 2^29: columns 0 (x 65536), 1 (x 256) on lane tig 0, column 2 on tig 1
-    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
-    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    float* rd = red + (slot * NB) * ROWS;
-    if (tig == 0) {
-      rd[kb * ROWS + g] = fmaf(fdv[g], acc0, -msum[g]);
-      rd[kb * ROWS + g + 8] = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    // per x row: digit columns weighted (x 65536, 256, 1), then summed over the quad
+    float v0[MX], v1[MX];
+#pragma unroll
+    for (int m = 0; m < MX; ++m) v0[m] = v1[m] = 0.f;
+#pragma unroll
+    for (int mi = 0; mi < NMMA; ++mi)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 8 * mi + 2 * tig + e;
+        const float wgt = (c % 3 == 0) ? 65536.f : (c % 3 == 1 ? 256.f : 1.f);
+#pragma unroll
+        for (int m = 0; m < MX; ++m)
+          if (c / 3 == m && c < 3 * M) {
+            v0[m] = fmaf((float)t[mi][e], wgt, v0[m]);
+            v1[m] = fmaf((float)t[mi][2 + e], wgt, v1[m]);
+          }
+      }
+    float* rd = red + (slot * NB + kb) * MX * ROWS;
+#pragma unroll
+    for (int m = 0; m < MX; ++m) {
+      if (m >= M) break;
+      float a0 = v0[m], a1 = v1[m];
+      a0 += __shfl_xor_sync(0xffffffffu, a0, 1);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+      a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+      if (tig == 0) {
+        rd[m * ROWS + g] = fmaf(fdv[m * ROWS + g], a0, -msum[m * ROWS + g]);
+        rd[m * ROWS + g + 8] = fmaf(fdv[m * ROWS + g + 8], a1, -msum[m * ROWS + g + 8]);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -501,17 +553,19 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
 
 }  // namespace
 
-int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
-                        int* n_launch) {
-  if (W.scheme != SM_Q4_K || W.layout != SM_LAYOUT_INTENDED) return SM_ERR_UNSUPPORTED;
+namespace {
+template <int MX>
+int launch_q4k_mx(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate, int* status,
+                  cudaStream_t st, int* n_launch) {
   const int K = W.K(), N = W.N(), U = K / 32;
-  if (K % 256 || U > 1024) return SM_ERR_UNSUPPORTED;
   MmaArgs a;
   a.w = (const uint8_t*)W.data;
   a.x = x;
   a.y = y;
   a.N = N;
   a.K = K;
+  a.M = M;
+  a.ldy = ldy;
   a.accumulate = accumulate;
   a.status = status;
   const int NB = K / 256;
@@ -521,20 +575,25 @@ int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumu
   a.row_stride = (int)rbytes + ((NB % 2 == 0) ? 16 : 32);
   a.slot_bytes = (int64_t)ROWS * a.row_stride;
   a.plane_offset = 256;
-  a.red_offset = a.plane_offset + U * (24 * 4 + 8);
-  a.scw_offset = a.red_offset + 8 * NB * ROWS * 4;
-  a.ring_offset = a.scw_offset + MM_CWARPS * (ROWS * SCW + 2 * ROWS) * 4;
-  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
+  a.red_offset = a.plane_offset + U * 3 * MX * 4 * 8 + MX * (U + NB) * 4;
+  a.red_offset = (a.red_offset + 15) / 16 * 16;
   int optin = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  const int64_t budget = optin - 1024 - a.ring_offset;
-  a.nslots = (int)std::min<int64_t>(8, budget / a.slot_bytes);
-  if (a.nslots < 2) return SM_ERR_UNSUPPORTED;
+  const int64_t fixed = a.red_offset + MM_CWARPS * (ROWS * SCW + 2 * MX * ROWS) * 4 + 128;
+  const int64_t per_slot = a.slot_bytes + (int64_t)NB * MX * ROWS * 4;
+  const int nslots = (int)std::min<int64_t>(8, (optin - 1024 - fixed) / per_slot);
+  if (nslots < 2) return SM_ERR_UNSUPPORTED;
+  a.nslots = nslots;
+  a.scw_offset = a.red_offset + nslots * NB * MX * ROWS * 4;
+  a.ring_offset = a.scw_offset + MM_CWARPS * (ROWS * SCW + 2 * MX * ROWS) * 4;
+  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
   const size_t smem = (size_t)a.ring_offset + (size_t)a.nslots * a.slot_bytes;
+  if ((int64_t)smem > optin - 1024) return SM_ERR_UNSUPPORTED;
   static bool attr_set[64] = {};
   if (dev < 64 && !attr_set[dev]) {
-    SM_CUDA_TRY(cudaFuncSetAttribute(gemv_mma_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
+    SM_CUDA_TRY(
+        cudaFuncSetAttribute(gemv_mma_q4k_kernel<MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
     attr_set[dev] = true;
   }
   int sms = 148;
@@ -550,9 +609,37 @@ int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumu
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel, a));
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q4k_kernel<MX>, a));
   if (n_launch) ++*n_launch;
   return SM_OK;
+}
+}  // namespace
+
+int launch_gemv_mma_q4k_rows(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate,
+                             int* status, cudaStream_t st, int* n_launch) {
+  if (W.scheme != SM_Q4_K || W.layout != SM_LAYOUT_INTENDED || M < 1) return SM_ERR_UNSUPPORTED;
+  const int K = W.K();
+  if (K % 256 || K / 32 > 1024) return SM_ERR_UNSUPPORTED;
+  // passes of up to four x rows (the digit planes of four rows fit shared memory)
+  for (int m0 = 0; m0 < M; m0 += 4) {
+    const int mm = std::min(4, M - m0);
+    const float* xm = x + (int64_t)m0 * K;
+    float* ym = y + (int64_t)m0 * ldy;
+    int rc;
+    if (mm == 1)
+      rc = launch_q4k_mx<1>(W, xm, 1, ym, ldy, accumulate, status, st, n_launch);
+    else if (mm == 2)
+      rc = launch_q4k_mx<2>(W, xm, 2, ym, ldy, accumulate, status, st, n_launch);
+    else
+      rc = launch_q4k_mx<4>(W, xm, mm, ym, ldy, accumulate, status, st, n_launch);
+    if (rc != SM_OK) return rc;
+  }
+  return SM_OK;
+}
+
+int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
+                        int* n_launch) {
+  return launch_gemv_mma_q4k_rows(W, x, 1, y, W.N(), accumulate, status, st, n_launch);
 }
 
 int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
