@@ -331,10 +331,14 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     return launch_gemv1(a, st, n_launch);
   }
   {
-    // 2 <= M <= 15, Q4_K: the integer tensor-core GEMV over up to four x rows per pass
+    // 2 <= M <= 15, Q4_K / Q6_K: the integer tensor-core GEMV over up to four x rows per pass
     const char* em = std::getenv("SMALLMIND_GEMV_MMA");
     if (!(em && em[0] == '0') && W.scheme == SM_Q4_K && M > 1 && M < 16) {
       const int rc = launch_gemv_mma_q4k_rows(W, x, M, y, ldy, accumulate, nullptr, st, n_launch);
+      if (rc != SM_ERR_UNSUPPORTED) return rc;
+    }
+    if (!(em && em[0] == '0') && W.scheme == SM_Q6_K && M > 1 && M < 16) {
+      const int rc = launch_gemv_mma_q6k_rows(W, x, M, y, ldy, accumulate, nullptr, st, n_launch);
       if (rc != SM_ERR_UNSUPPORTED) return rc;
     }
   }

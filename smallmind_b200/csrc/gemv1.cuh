@@ -62,6 +62,9 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
 // Q4_K (INTENDED) y[m] (+)= W x[m] for M rows of x (stride K), y rows of stride ldy
 int launch_gemv_mma_q4k_rows(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate,
                              int* status, cudaStream_t st, int* n_launch);
+// Q6_K (INTENDED, row-padded d) y[m] (+)= W x[m] for M rows of x
+int launch_gemv_mma_q6k_rows(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate,
+                             int* status, cudaStream_t st, int* n_launch);
 // Q6_K (INTENDED, row-padded d) y = W x on the int8 tensor-core path
 int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
                         int* n_launch);

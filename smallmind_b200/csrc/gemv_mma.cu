@@ -346,15 +346,23 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q4k_kernel(const __gri
 // x is 22-bit fixed point relative to its 256-element block's largest |x|.
 constexpr int SCW2 = 9;  // int2 per scale row (8 units + 1): rows g = 0..7 on distinct banks
 
+// MX x rows (1, 2 or 4): six digit columns per x row (column 6 m + 3 h + q),
+// NMMA = ceil(6 MX / 8) MMAs per unit share the A fragments.
+template <int MX>
 __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __grid_constant__ MmaArgs a) {
+  constexpr int NC = 6 * MX;                // B columns: 6 per x row
+  // stored columns per unit: one row keeps all six (the other half's zeros
+  // included, no selects); more rows keep each lane's own half (3 per row)
+  constexpr int NS = MX == 1 ? 6 : 3 * MX;
+  constexpr int NMMA = (NC + 7) / 8;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = (uint64_t*)smem;  // [8]
   uint64_t* empty = full + 8;        // [8]
-  uint2* planes = (uint2*)(smem + a.plane_offset);  // [U][6 columns][4 tig] (even, odd) digit words, then hsum, bexp
-  float* red = (float*)(smem + a.red_offset);       // [nslots][NB][ROWS] block partials
-  uint8_t* scw_all = smem + a.scw_offset;           // per warp: int2 [ROWS][SCW2], float msum[ROWS], fdv[ROWS]
+  uint2* planes = (uint2*)(smem + a.plane_offset);  // [U][NS][4 tig] (even, odd) digit words, then hsum, bexp
+  float* red = (float*)(smem + a.red_offset);       // [nslots][NB][MX][ROWS] block partials
+  uint8_t* scw_all = smem + a.scw_offset;           // per warp: int2 [ROWS][SCW2], msum [MX][ROWS], fdv [MX][ROWS]
   uint8_t* ring = smem + a.ring_offset;
-  const int K = a.K, U = K >> 5, NB = K >> 8;
+  const int K = a.K, U = K >> 5, NB = K >> 8, M = a.M;
   const uint32_t rbytes = (uint32_t)NB * Q6K_BODY_BYTES;
   const int rs = a.row_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -362,8 +370,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
   const int g0 = (int)((int64_t)ngroups * blockIdx.x / gridDim.x);
   const int g1 = (int)((int64_t)ngroups * (blockIdx.x + 1) / gridDim.x);
   const int nst = g1 - g0;
-  float* hsum = (float*)(planes + U * 24);  // [U][2] sum of x over each 16-element half
-  float* bexp = hsum + 2 * U;               // [NB] 2^(e-22) of the block
+  float* hsum = (float*)(planes + U * NS * 4);  // [MX][U][2] sum of x over each 16-element half
+  float* bexp = hsum + MX * 2 * U;              // [MX][NB] 2^(e-22) of the block
   if (tid == 0) {
     for (int i = 0; i < a.nslots; ++i) {
       mbar_init(&full[i], 1);
@@ -395,12 +403,15 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
       if (!mbar_wait_bounded(&empty[slot], phase, a.status)) return;
       const int row0 = (g0 + k) * ROWS;
       const int n = min(ROWS, a.N - row0);
-      if (lane < n) {
-        const float* rd = red + (slot * NB) * ROWS + lane;
-        float s = 0.f;
-        for (int b = 0; b < NB; ++b) s += rd[b * ROWS];
-        float* dst = a.y + row0 + lane;
-        *dst = a.accumulate ? *dst + s : s;
+      for (int t = lane; t < M * ROWS; t += 32) {
+        const int m = t / ROWS, r = t - m * ROWS;
+        if (r < n) {
+          const float* rd = red + (slot * NB * MX + m) * ROWS + r;
+          float s = 0.f;
+          for (int b = 0; b < NB; ++b) s += rd[b * MX * ROWS];
+          float* dst = a.y + (int64_t)m * a.ldy + row0 + r;
+          *dst = a.accumulate ? *dst + s : s;
+        }
       }
       __syncwarp();
       if (next < nst) issue(next++);
@@ -409,10 +420,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
     return;
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // ---- digit columns of x: one warp per 256-element block, four lanes per unit
-  for (int blk = warp; blk < NB; blk += MM_CWARPS) {
+  // ---- digit columns of x: one warp per (x row, 256-element block), four lanes per unit
+  for (int it = warp; it < M * NB; it += MM_CWARPS) {
+    const int m = it / NB, blk = it - m * NB;
     const int u = blk * 8 + (lane >> 2), p = lane & 3;
-    const float4* xp = (const float4*)(a.x + 32 * u + 8 * p);
+    const float4* xp = (const float4*)(a.x + (int64_t)m * K + 32 * u + 8 * p);
     const float4 v0 = __ldcg(xp), v1 = __ldcg(xp + 1);
     const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     float amax = 0.f, sx = 0.f;
@@ -439,27 +451,44 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
       pw[eo][1] |= (uint32_t)(b & 255) << sh;
       pw[eo][2] |= (uint32_t)(c & 255) << sh;
     }
-    uint2* d = planes + u * 24 + p;
+    // digit q of row m at stored column 3 m + q; the B column of the other half
+    // is zero at this lane's k positions (applied by the consumer lanes)
     const int half = p >> 1;
+    if (MX == 1) {
+      uint2* d = planes + u * NS * 4 + p;
 #pragma unroll
-    for (int col = 0; col < 6; ++col) {
-      const bool mine = (col / 3) == half;
-      d[4 * col] = mine ? make_uint2(pw[0][col % 3], pw[1][col % 3]) : make_uint2(0u, 0u);
+      for (int col = 0; col < 6; ++col)
+        d[4 * col] = (col / 3) == half ? make_uint2(pw[0][col % 3], pw[1][col % 3]) : make_uint2(0u, 0u);
+    } else {
+      uint2* d = planes + (u * NS + 3 * m) * 4 + p;
+#pragma unroll
+      for (int q = 0; q < 3; ++q) d[4 * q] = make_uint2(pw[0][q], pw[1][q]);
     }
-    if ((p & 1) == 0) hsum[2 * u + half] = sx;
-    if (lane == 0) bexp[blk] = ldexpf(1.f, ex - 22);
+    if ((p & 1) == 0) hsum[(m * U + u) * 2 + half] = sx;
+    if (lane == 0) bexp[m * NB + blk] = ldexpf(1.f, ex - 22);
   }
   csync();
   const int g = lane >> 2, tig = lane & 3;
-  // C columns of lane tig: 2 tig, 2 tig + 1 -> (half, digit) weights
-  const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : (tig == 2 ? 256.f : 0.f));
-  const float fB = tig == 0 ? 256.f : (tig == 1 ? 65536.f : (tig == 2 ? 1.f : 0.f));
-  const bool s0_first = tig < 2, s1_first = tig == 0;  // which half's scale meets d0 / d1
-  const int hshift = 4 * (tig & 1);                    // high-bit byte fields of this lane's elements
-  const uint2* pl = planes + (g < 6 ? g : 0) * 4 + tig;
-  int2* scw = (int2*)(scw_all + warp * (ROWS * SCW2 * 8 + 2 * ROWS * 4));
-  float* msum = (float*)(scw + ROWS * SCW2);
-  float* fdv = msum + ROWS;
+  const int hshift = 4 * (tig & 1);  // high-bit byte fields of this lane's elements
+  // lane (g, tig), MMA mi: B column 8 mi + g (a real column when past 6 M);
+  // C column c = 8 mi + 2 tig + e: x row c / 6, half (c % 6) / 3, digit c % 3
+  const uint2* pl[NMMA];
+  bool bon[NMMA];  // this lane's half is the column's half (else the B words are zero)
+#pragma unroll
+  for (int mi = 0; mi < NMMA; ++mi) {
+    const int c = 8 * mi + g;
+    const bool real = c < 6 * M;
+    if (MX == 1) {
+      pl[mi] = planes + (real ? c : 0) * 4 + tig;
+      bon[mi] = true;
+    } else {
+      pl[mi] = planes + (real ? 3 * (c / 6) + c % 3 : 0) * 4 + tig;
+      bon[mi] = real && ((c % 6) / 3) == (tig >> 1);
+    }
+  }
+  int2* scw = (int2*)(scw_all + warp * (ROWS * SCW2 * 8 + 2 * MX * ROWS * 4));
+  float* msum = (float*)(scw + ROWS * SCW2);  // [MX][ROWS]
+  float* fdv = msum + MX * ROWS;              // [MX][ROWS]
   const int sr = lane >> 1, shh = lane & 1;  // scale decode: row, half of the units
   int k = 0, kb = warp, slot = 0;
   uint32_t phase = 0;
@@ -480,30 +509,43 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
       const int2 sc8 = *(const int2*)(rp + kb * Q6K_BODY_BYTES + 192 + 8 * shh);
       const float d = __half2float(__ushort_as_half(*(const unsigned short*)(rp + rbytes + 2 * kb)));
       const uint32_t sw[2] = {(uint32_t)sc8.x, (uint32_t)sc8.y};
-      const float* hs = hsum + 2 * (kb * 8 + 4 * shh);
-      float mpart = 0.f;
+      float sa[4], sb[4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        const int sa = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1))) & 0xFF);
-        const int sb = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1) + 8)) & 0xFF);
-        scw[sr * SCW2 + 4 * shh + jj] = make_int2(sa, sb);
-        mpart = fmaf((float)sa, hs[2 * jj], mpart);
-        mpart = fmaf((float)sb, hs[2 * jj + 1], mpart);
+        const int ia = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1))) & 0xFF);
+        const int ib = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1) + 8)) & 0xFF);
+        scw[sr * SCW2 + 4 * shh + jj] = make_int2(ia, ib);
+        sa[jj] = (float)ia;
+        sb[jj] = (float)ib;
       }
-      mpart += __shfl_xor_sync(0xffffffffu, mpart, 1);
-      if (shh == 0) {
-        msum[sr] = 32.f * d * mpart;
-        fdv[sr] = d * bexp[kb];
+#pragma unroll
+      for (int m = 0; m < MX; ++m) {
+        if (m >= M) break;
+        const float* hs = hsum + (m * U + kb * 8 + 4 * shh) * 2;
+        float mpart = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          mpart = fmaf(sa[jj], hs[2 * jj], mpart);
+          mpart = fmaf(sb[jj], hs[2 * jj + 1], mpart);
+        }
+        mpart += __shfl_xor_sync(0xffffffffu, mpart, 1);
+        if (shh == 0) {
+          msum[m * ROWS + sr] = 32.f * d * mpart;
+          fdv[m * ROWS + sr] = d * bexp[m * NB + kb];
+        }
       }
     }
     __syncwarp();
     const uint8_t* rg = blk0 + min(g, n - 1) * rs;
     const uint8_t* rg8 = blk0 + min(g + 8, n - 1) * rs;
-    const uint2* plu = pl + kb * 8 * 24;
-    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+    const int ustride = NS * 4;
+    const int ub = kb * 8 * ustride;
+    int t[NMMA][4];
+#pragma unroll
+    for (int mi = 0; mi < NMMA; ++mi) t[mi][0] = t[mi][1] = t[mi][2] = t[mi][3] = 0;
 #pragma unroll
     for (int j0 = 0; j0 < 8; j0 += 4) {
-      int dd[4][4];
+      int dd[4][NMMA][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int jj = j0 + j;
@@ -516,28 +558,55 @@ __global__ void __launch_bounds__(MM_THREADS, 1) gemv_mma_q6k_kernel(const __gri
         const uint32_t e1 = (w1 & 0x0F0F0F0Fu) | ((W1 << 4) & 0x30303030u);
         const uint32_t o0 = ((w0 >> 4) & 0x0F0F0F0Fu) | ((W0 << 2) & 0x30303030u);
         const uint32_t o1 = ((w1 >> 4) & 0x0F0F0F0Fu) | ((W1 << 2) & 0x30303030u);
-        const uint2 b = plu[24 * jj];
-        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], e0, e1, o0, o1, b.x, b.y);
+#pragma unroll
+        for (int mi = 0; mi < NMMA; ++mi) {
+          const uint2 b = pl[mi][ub + jj * ustride];
+          mma_u8s8(dd[j][mi][0], dd[j][mi][1], dd[j][mi][2], dd[j][mi][3], e0, e1, o0, o1, bon[mi] ? b.x : 0u,
+                   bon[mi] ? b.y : 0u);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int2 s0 = scw[g * SCW2 + j0 + j], s1 = scw[(g + 8) * SCW2 + j0 + j];
-        t0 += (s0_first ? s0.x : s0.y) * dd[j][0];
-        t1 += (s1_first ? s0.x : s0.y) * dd[j][1];
-        t2 += (s0_first ? s1.x : s1.y) * dd[j][2];
-        t3 += (s1_first ? s1.x : s1.y) * dd[j][3];
+#pragma unroll
+        for (int mi = 0; mi < NMMA; ++mi)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const bool hb = (((8 * mi + 2 * tig + e) % 6) / 3) != 0;  // second half's scale
+            t[mi][e] += (hb ? s0.y : s0.x) * dd[j][mi][e];
+            t[mi][2 + e] += (hb ? s1.y : s1.x) * dd[j][mi][2 + e];
+          }
       }
     }
-    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
-    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-    float* rd = red + (slot * NB) * ROWS;
-    if (tig == 0) {
-      rd[kb * ROWS + g] = fmaf(fdv[g], acc0, -msum[g]);
-      rd[kb * ROWS + g + 8] = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    float v0[MX], v1[MX];
+#pragma unroll
+    for (int m = 0; m < MX; ++m) v0[m] = v1[m] = 0.f;
+#pragma unroll
+    for (int mi = 0; mi < NMMA; ++mi)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int c = 8 * mi + 2 * tig + e;
+        const float wgt = (c % 3 == 0) ? 65536.f : (c % 3 == 1 ? 256.f : 1.f);
+#pragma unroll
+        for (int m = 0; m < MX; ++m)
+          if (c / 6 == m && c < 6 * M) {
+            v0[m] = fmaf((float)t[mi][e], wgt, v0[m]);
+            v1[m] = fmaf((float)t[mi][2 + e], wgt, v1[m]);
+          }
+      }
+    float* rd = red + (slot * NB + kb) * MX * ROWS;
+#pragma unroll
+    for (int m = 0; m < MX; ++m) {
+      if (m >= M) break;
+      float a0 = v0[m], a1 = v1[m];
+      a0 += __shfl_xor_sync(0xffffffffu, a0, 1);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+      a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+      if (tig == 0) {
+        rd[m * ROWS + g] = fmaf(fdv[m * ROWS + g], a0, -msum[m * ROWS + g]);
+        rd[m * ROWS + g + 8] = fmaf(fdv[m * ROWS + g + 8], a1, -msum[m * ROWS + g + 8]);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -621,8 +690,10 @@ int launch_gemv_mma_q4k_rows(const DevWeight& W, const float* x, int M, float* y
   const int K = W.K();
   if (K % 256 || K / 32 > 1024) return SM_ERR_UNSUPPORTED;
   // passes of up to four x rows (the digit planes of four rows fit shared memory)
-  for (int m0 = 0; m0 < M; m0 += 4) {
-    const int mm = std::min(4, M - m0);
+  // the widest pass whose digit planes and two ring slots fit shared memory
+  int width = 4;
+  for (int m0 = 0; m0 < M;) {
+    const int mm = std::min(width, M - m0);
     const float* xm = x + (int64_t)m0 * K;
     float* ym = y + (int64_t)m0 * ldy;
     int rc;
@@ -632,7 +703,12 @@ int launch_gemv_mma_q4k_rows(const DevWeight& W, const float* x, int M, float* y
       rc = launch_q4k_mx<2>(W, xm, 2, ym, ldy, accumulate, status, st, n_launch);
     else
       rc = launch_q4k_mx<4>(W, xm, mm, ym, ldy, accumulate, status, st, n_launch);
+    if (rc == SM_ERR_UNSUPPORTED && mm > 1) {
+      width = mm > 2 ? 2 : 1;
+      continue;
+    }
     if (rc != SM_OK) return rc;
+    m0 += mm;
   }
   return SM_OK;
 }
@@ -642,11 +718,11 @@ int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumu
   return launch_gemv_mma_q4k_rows(W, x, 1, y, W.N(), accumulate, status, st, n_launch);
 }
 
-int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
-                        int* n_launch) {
-  if (W.scheme != SM_Q6_K || W.layout != SM_LAYOUT_INTENDED || W.aux_stride <= 0) return SM_ERR_UNSUPPORTED;
+namespace {
+template <int MX>
+int launch_q6k_mx(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate, int* status,
+                  cudaStream_t st, int* n_launch) {
   const int K = W.K(), N = W.N(), U = K / 32;
-  if (K % 256 || U > 1024) return SM_ERR_UNSUPPORTED;
   MmaArgs a;
   a.w = (const uint8_t*)W.data;
   a.aux = (const uint16_t*)W.aux;
@@ -657,6 +733,8 @@ int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumu
   a.y = y;
   a.N = N;
   a.K = K;
+  a.M = M;
+  a.ldy = ldy;
   a.accumulate = accumulate;
   a.status = status;
   const int NB = K / 256;
@@ -668,21 +746,26 @@ int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumu
   a.row_stride = rs;
   a.slot_bytes = (int64_t)ROWS * a.row_stride;
   a.plane_offset = 256;
-  a.red_offset = a.plane_offset + U * (24 * 8 + 8) + NB * 4;
+  a.red_offset = a.plane_offset + U * (MX == 1 ? 6 : 3 * MX) * 4 * 8 + MX * (2 * U + NB) * 4;
   a.red_offset = (a.red_offset + 15) / 16 * 16;
-  a.scw_offset = a.red_offset + 8 * NB * ROWS * 4;
-  a.ring_offset = a.scw_offset + MM_CWARPS * (ROWS * SCW2 * 8 + 2 * ROWS * 4);
-  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
   int optin = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  const int64_t budget = optin - 1024 - a.ring_offset;
-  a.nslots = (int)std::min<int64_t>(8, budget / a.slot_bytes);
-  if (a.nslots < 2) return SM_ERR_UNSUPPORTED;
+  const int64_t scw_bytes = (int64_t)MM_CWARPS * (ROWS * SCW2 * 8 + 2 * MX * ROWS * 4);
+  const int64_t fixed = a.red_offset + scw_bytes + 128;
+  const int64_t per_slot = a.slot_bytes + (int64_t)NB * MX * ROWS * 4;
+  const int nslots = (int)std::min<int64_t>(8, (optin - 1024 - fixed) / per_slot);
+  if (nslots < 2) return SM_ERR_UNSUPPORTED;
+  a.nslots = nslots;
+  a.scw_offset = a.red_offset + nslots * NB * MX * ROWS * 4;
+  a.ring_offset = a.scw_offset + (int)scw_bytes;
+  a.ring_offset = (a.ring_offset + 127) / 128 * 128;
   const size_t smem = (size_t)a.ring_offset + (size_t)a.nslots * a.slot_bytes;
+  if ((int64_t)smem > optin - 1024) return SM_ERR_UNSUPPORTED;
   static bool attr_set[64] = {};
   if (dev < 64 && !attr_set[dev]) {
-    SM_CUDA_TRY(cudaFuncSetAttribute(gemv_mma_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
+    SM_CUDA_TRY(
+        cudaFuncSetAttribute(gemv_mma_q6k_kernel<MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024));
     attr_set[dev] = true;
   }
   int sms = 148;
@@ -698,9 +781,44 @@ int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumu
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q6k_kernel, a));
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_mma_q6k_kernel<MX>, a));
   if (n_launch) ++*n_launch;
   return SM_OK;
+}
+}  // namespace
+
+int launch_gemv_mma_q6k_rows(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate,
+                             int* status, cudaStream_t st, int* n_launch) {
+  if (W.scheme != SM_Q6_K || W.layout != SM_LAYOUT_INTENDED || W.aux_stride <= 0 || M < 1)
+    return SM_ERR_UNSUPPORTED;
+  const int K = W.K();
+  if (K % 256 || K / 32 > 1024) return SM_ERR_UNSUPPORTED;
+  // the widest pass whose digit planes and two ring slots fit shared memory
+  int width = 4;
+  for (int m0 = 0; m0 < M;) {
+    const int mm = std::min(width, M - m0);
+    const float* xm = x + (int64_t)m0 * K;
+    float* ym = y + (int64_t)m0 * ldy;
+    int rc;
+    if (mm == 1)
+      rc = launch_q6k_mx<1>(W, xm, 1, ym, ldy, accumulate, status, st, n_launch);
+    else if (mm == 2)
+      rc = launch_q6k_mx<2>(W, xm, 2, ym, ldy, accumulate, status, st, n_launch);
+    else
+      rc = launch_q6k_mx<4>(W, xm, mm, ym, ldy, accumulate, status, st, n_launch);
+    if (rc == SM_ERR_UNSUPPORTED && mm > 1) {
+      width = mm > 2 ? 2 : 1;
+      continue;
+    }
+    if (rc != SM_OK) return rc;
+    m0 += mm;
+  }
+  return SM_OK;
+}
+
+int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
+                        int* n_launch) {
+  return launch_gemv_mma_q6k_rows(W, x, 1, y, W.N(), accumulate, status, st, n_launch);
 }
 
 }  // namespace sm
