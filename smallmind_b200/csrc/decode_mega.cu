@@ -201,8 +201,10 @@ struct Consumer {
     stamp();
     ++barrier_gen;
     if (tid == 0) {
-      __threadfence();
-      atomicAdd(&a.sync[0], 1u);
+      // release-ordered arrival without waiting for a return value: this CTA's
+      // stores (ordered before it by the CTA barrier) are visible before the
+      // count moves, and the poll below starts one L2 round trip earlier
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.sync), "r"(1u) : "memory");
       const unsigned target = barrier_gen * gridDim.x;
       const long long t0 = clock64();
       int ok = 1;
