@@ -893,6 +893,7 @@ int mega_args(sm_model* m, sm_kv* kv, MegaArgs& a) {
       t.ffn_norm = L.ffn_norm;
       t.kc = kc;
       t.vc = vc;
+      mega_layer_split(t, c.hidden, grid);
     }
     if (!kv->mega_layers) SM_CUDA_TRY(cudaMalloc(&kv->mega_layers, sizeof(MegaLayer) * c.n_layers));
     if (!kv->mega_sync) SM_CUDA_TRY(cudaMalloc(&kv->mega_sync, 64 * sizeof(unsigned)));

@@ -30,6 +30,7 @@
 #include "decode_mega.cuh"
 #include "gemv_units.cuh"
 #include "mbar.cuh"
+#include "mma_i8.cuh"
 
 namespace sm {
 namespace {
@@ -43,7 +44,7 @@ constexpr long long kSpin = 4000000000LL;
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
 
-__device__ __forceinline__ int64_t row_bytes_fmt(int fmt, int K) {
+__host__ __device__ __forceinline__ int64_t row_bytes_fmt(int fmt, int K) {
   switch (fmt) {
     case SM_Q4_K: return (int64_t)(K >> 8) * Q4K_BLOCK_BYTES;
     case SM_Q6_K: return (int64_t)(K >> 8) * Q6K_BODY_BYTES;
@@ -53,7 +54,7 @@ __device__ __forceinline__ int64_t row_bytes_fmt(int fmt, int K) {
 }
 
 // bytes of one padded row of scales / d (0: the format has none)
-__device__ __forceinline__ int64_t aux_row_bytes(const MegaSeg& s) {
+__host__ __device__ __forceinline__ int64_t aux_row_bytes(const MegaSeg& s) {
   if (s.fmt == SM_Q4_K) return 0;
   return (int64_t)s.aux_stride * (s.fmt == SM_Q6_K ? 2 : 4);
 }
@@ -61,29 +62,56 @@ __device__ __forceinline__ int64_t aux_row_bytes(const MegaSeg& s) {
 // output rows per stage: as many as fit one ring slot (weights + scales, gate + up for GLU)
 __device__ __forceinline__ int stage_rows(const MegaSeg& s, int K, int64_t slot_bytes) {
   const int mult = s.mode == GEMV_GLU ? 2 : 1;
-  const int64_t per = mult * (row_bytes_fmt(s.fmt, K) + aux_row_bytes(s));
-  return (int)max((int64_t)1, min((int64_t)64, slot_bytes / per));
+  const unsigned per = (unsigned)(mult * (row_bytes_fmt(s.fmt, K) + aux_row_bytes(s)));
+  return (int)max(1u, min(64u, (unsigned)slot_bytes / per));  // a slot and a row are far below 2^32 bytes
 }
 
 // rows of a segment for CTA i of n: whole row pairs, balanced
 __device__ __forceinline__ void seg_rows(int rows, int i, int n, int& r0, int& r1) {
   const int pairs = (rows + 1) / 2;
-  r0 = min(rows, 2 * (int)((int64_t)pairs * i / n));
-  r1 = min(rows, 2 * (int)((int64_t)pairs * (i + 1) / n));
+  // pairs * (i + 1) stays far below 2^31 (rows < 2^20, at most 1024 CTAs)
+  r0 = min(rows, 2 * (int)((unsigned)(pairs * i) / (unsigned)n));
+  r1 = min(rows, 2 * (int)((unsigned)(pairs * (i + 1)) / (unsigned)n));
+}
+
+// MMA segments (Q4_K, Q6_K with row-padded d): the GEMV runs on the int8
+// tensor-core path of gemv_mma.cu.  A stage is one 16-row tile of the CTA's rows
+// (a gate and an up tile for GLU) over a range of 256-weight blocks; every row
+// is its own bulk copy into a padded slot row (an odd number of 16-byte units,
+// so the 8 rows of a fragment load fall on distinct bank quads), with the
+// Q6_K d row after the largest block range.
+struct MGeo {
+  int nT, bb, abytes, NB, nkbs, rs, nch;
+};
+
+__device__ __forceinline__ bool mma_seg(const MegaArgs& a, const MegaSeg& s) {
+  if (!a.use_mma) return false;
+  return s.fmt == SM_Q4_K || (s.fmt == SM_Q6_K && s.aux_stride > 0 && (s.aux_stride * 2) % 16 == 0);
+}
+
+__device__ __forceinline__ MGeo mgeo(const MegaSeg& s, int K, int64_t slot_bytes) {
+  MGeo m;
+  m.nT = s.mode == GEMV_GLU ? 2 : 1;
+  m.bb = s.fmt == SM_Q4_K ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES;
+  m.abytes = s.fmt == SM_Q6_K ? s.aux_stride * 2 : 0;
+  m.NB = K >> 8;
+  auto stride = [&](int nk) {
+    int rs = nk * m.bb + m.abytes;
+    if (((rs >> 4) & 1) == 0) rs += 16;
+    return rs;
+  };
+  for (m.nkbs = m.NB; m.nkbs > 1; --m.nkbs)
+    if ((int64_t)m.nT * 16 * stride(m.nkbs) <= slot_bytes) break;
+  m.rs = stride(m.nkbs);
+  m.nch = (m.NB + m.nkbs - 1) / m.nkbs;
+  return m;
 }
 
 // Q|K|V: CTAs [cb[s], cb[s+1]) take segment s, in proportion to its bytes, so
 // every CTA runs one segment (one stage stream, one epilogue) per phase.
-__device__ __forceinline__ void qkv_split(const MegaLayer& L, int K, int grid, int (&cb)[4]) {
-  int64_t b[3], tot = 0;
-  for (int i = 0; i < 3; ++i) {
-    b[i] = (int64_t)L.qkv[i].rows * (row_bytes_fmt(L.qkv[i].fmt, K) + aux_row_bytes(L.qkv[i]));
-    tot += b[i];
-  }
-  cb[0] = 0;
-  cb[1] = (int)min((int64_t)grid - 2, max((int64_t)1, (grid * b[0] + tot / 2) / tot));
-  cb[2] = (int)min((int64_t)grid - 1, max((int64_t)cb[1] + 1, cb[1] + (grid * b[1] + tot / 2) / tot));
-  cb[3] = grid;
+__device__ __forceinline__ void qkv_split(const MegaLayer& L, int /*K*/, int /*grid*/, int (&cb)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cb[i] = L.qkv_cb[i];
 }
 
 // segment rows of CTA `i` when CTAs [c0, c1) share the segment (none outside)
@@ -98,6 +126,7 @@ __device__ __forceinline__ void seg_rows_in(int rows, int i, int c0, int c1, int
 struct Shared {
   uint64_t full[16];
   uint64_t empty[16];
+  MegaLayer lay;  // the consumers' copy of the current layer's table entry
   float red[MW * MGMAX];
   float vec[4 * MGMAX];
   int flag[4];
@@ -115,6 +144,38 @@ struct Producer {
   int k = 0;  // stages issued
   bool ok = true;
 
+  // MMA segment: 16-row tiles x block ranges, one bulk copy per row (and per d row)
+  __device__ void mseg(const MegaSeg& s, int K, int r0, int r1) {
+    const MGeo m = mgeo(s, K, slot_bytes);
+    const int64_t rbytes = (int64_t)m.NB * m.bb;
+    for (int row = r0; row < r1; row += 16) {
+      const int n = min(16, r1 - row);
+      for (int c = 0; c < m.nch; ++c) {
+        const int kb0 = c * m.nkbs, nkb = min(m.nkbs, m.NB - kb0);
+        const int slot = k % a.nslots;
+        if (k >= a.nslots) {
+          if (!mbar_wait_bounded(&sh.empty[slot], ((k / a.nslots) - 1) & 1, a.status) || sh.abort) {
+            ok = false;
+            return;
+          }
+        }
+        uint8_t* dst = ring + slot * slot_bytes;
+        const uint32_t per_row = (uint32_t)(nkb * m.bb + m.abytes);
+        mbar_expect_tx(&sh.full[slot], (uint32_t)(m.nT * n) * per_row);
+        for (int tt = 0; tt < m.nT; ++tt) {
+          const uint8_t* src = tt ? s.data2 : s.data;
+          const uint8_t* asrc = (const uint8_t*)(tt ? s.aux2 : s.aux);
+          for (int r = 0; r < n; ++r) {
+            uint8_t* d = dst + (tt * 16 + r) * m.rs;
+            bulk_g2s(d, src + (row + r) * rbytes + kb0 * m.bb, (uint32_t)(nkb * m.bb), &sh.full[slot]);
+            if (m.abytes) bulk_g2s(d + m.nkbs * m.bb, asrc + (int64_t)(row + r) * m.abytes, m.abytes, &sh.full[slot]);
+          }
+        }
+        ++k;
+      }
+    }
+  }
+
   __device__ void seg(const MegaSeg& s, int K, int /*rb*/, int phase, int c0 = 0, int c1 = -1) {
     if (!ok) return;
     const int rb = stage_rows(s, K, slot_bytes);
@@ -128,6 +189,10 @@ struct Producer {
     }
     int r0, r1;
     seg_rows_in(s.rows, blockIdx.x, c0, c1 < 0 ? (int)gridDim.x : c1, r0, r1);
+    if (mma_seg(a, s)) {
+      mseg(s, K, r0, r1);
+      return;
+    }
     const int64_t rbytes = row_bytes_fmt(s.fmt, K);
     const bool glu = s.mode == GEMV_GLU;
     for (int row = r0; row < r1; row += rb) {
@@ -188,6 +253,13 @@ struct Consumer {
   }
   // this thread's slice of the current input vector, as dp4a byte planes
   XPlanes xp;
+  // MMA segments: the staged vector as the B operand of the int8 tensor-core path
+  int mfmt = 0;            // SM_Q4_K / SM_Q6_K: mpl holds that format's digit columns
+  const uint2* mpl = nullptr;  // [U][3 (Q4_K) or 6 (Q6_K)][4 tig] word pairs
+  const float* msx = nullptr;  // Q4_K: [U] unit sums; Q6_K: [U][2] half sums
+  const float* mbx = nullptr;  // [NB] 2^(e-21) (Q4_K) or 2^(e-22) (Q6_K) of each block
+  int mend = 0;                // first float of part past the digit planes
+  float x_inv = 1.f;           // RMSNorm scale of the staged vector (not folded into the planes)
   bool pair = true;  // plane packing (PAIR for K-quants / Q4_0, NATURAL for Q8_0)
   const float* x_src = nullptr;
   const float* x_gamma = nullptr;
@@ -195,10 +267,14 @@ struct Consumer {
   int U = 1, u = 0, ph = 0, P = 1, nwpp = 1;
   bool u_ok = false;
 
-  __device__ bool grid_barrier() {
+  __device__ bool grid_barrier(const MegaLayer* next = nullptr) {
     // all consumer stores of this CTA are done before thread 0 arrives
     cons_sync();
     stamp();
+    // the next layer's table entry comes on chip while thread 0 waits (the
+    // current entry is no longer read past the first CTA barrier)
+    if (next && tid >= 32 && tid < 32 + (int)(sizeof(MegaLayer) / 4))
+      ((int*)&sh.lay)[tid - 32] = __ldg((const int*)next + (tid - 32));
     ++barrier_gen;
     if (tid == 0) {
       // release-ordered arrival without waiting for a return value: this CTA's
@@ -230,11 +306,12 @@ struct Consumer {
   }
 
   // x slice for a phase with K inputs (optionally RMS-normalised with gamma)
-  __device__ void load_x(const float* src, const float* gamma, int K, bool want_pair = true) {
+  __device__ void load_x(const float* src, const float* gamma, int K, bool want_pair = true, int mma = 0) {
     x_src = src;
     x_gamma = gamma;
     x_K = K;
     pair = want_pair;
+    mfmt = 0;
     const int lxe = (lx >= 4 && lx < 12) ? 900 + 8 * (lx - 4) : -1;
     ++lx;
     if (lxe >= 0) stamp_at(lxe);
@@ -262,6 +339,10 @@ struct Consumer {
     if (lxe >= 0) stamp_at(lxe + 1);
     cons_sync();
     if (lxe >= 0) stamp_at(lxe + 2);
+    if (mma) {
+      build_mma_planes(K, gamma, mma);
+      return;
+    }
     // The byte planes of every unit, built once per CTA: four threads per unit,
     // eight elements each, from y = gamma * x (the RMS scale is a per-vector
     // scalar and is folded into each unit's factor below); the same pass
@@ -346,6 +427,313 @@ struct Consumer {
     if (lxe >= 0) stamp_at(lxe + 5);
   }
 
+  // Digit columns of the staged vector for the int8 tensor-core path, built once
+  // per CTA: four threads per 32-element unit, a warp per 256-element block (one
+  // power-of-two exponent per block).  y = gamma * x; the RMS scale is a scalar
+  // kept in x_inv.  Q4_K: B holds L - H at the low-nibble positions and H at the
+  // raw-byte positions (L: 21-bit low elements, H: 17-bit high elements), see
+  // gemv_mma.cu; Q6_K: 22-bit values, six columns (three per 16-element half,
+  // zero at the other half's positions).
+  __device__ void build_mma_planes(int K, const float* gamma, int fmt) {
+    const int U = K >> 5, NB = K >> 8, lane = tid & 31;
+    const float4* xs = (const float4*)part;
+    const float4* gs = (const float4*)part + K / 4;  // staged gamma (when given)
+    const int pbase = gamma ? 2 * K : K;
+    uint2* mp = (uint2*)(part + pbase);        // [U][6][4] at most
+    float* sx = part + pbase + 48 * U;         // [U][2] at most
+    float* bx = sx + 2 * U;                    // [NB]
+    mend = pbase + 50 * U + NB;
+    float sq = 0.f;
+    for (int t0 = (tid >> 5) * 32; t0 < 4 * U; t0 += CT) {  // 4U is a multiple of 32: whole warps
+      const int t = t0 + lane, uu = t >> 2, pp = t & 3;
+      const float4 v0 = xs[(uu << 3) + ((2 * pp + uu) & 7)], v1 = xs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+      float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      if (gamma) {
+        const float4 g0 = gs[(uu << 3) + ((2 * pp + uu) & 7)], g1 = gs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          sq = fmaf(y[i], y[i], sq);
+          y[i] = __fmul_rn(gv[i], y[i]);
+        }
+      }
+      float am = 0.f, su = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        am = fmaxf(am, fmaxf(fabsf(y[i]), fabsf(y[i + 1])));
+        su += y[i] + y[i + 1];
+      }
+      am = warp_max(am);  // the warp's 8 units are one block
+      int ex = 0;
+      frexpf(am, &ex);  // am < 2^ex
+      uint32_t pw[2][3] = {};
+      auto digits = [&](int X, int h, int byte) {
+        const int c = ((X + 128) & 255) - 128;
+        const int X1 = (X - c) >> 8;
+        const int b = ((X1 + 128) & 255) - 128;
+        const int hi = (X1 - b) >> 8;
+        pw[h][0] |= (uint32_t)(hi & 255) << (8 * byte);
+        pw[h][1] |= (uint32_t)(b & 255) << (8 * byte);
+        pw[h][2] |= (uint32_t)(c & 255) << (8 * byte);
+      };
+      if (fmt == SM_Q4_K) {
+        const float up = ldexpf(1.f, 21 - ex), uph = ldexpf(1.f, 17 - ex);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int L = am > 0.f ? __float2int_rn(y[2 * i] * up) : 0;
+          const int H = am > 0.f ? __float2int_rn(y[2 * i + 1] * uph) : 0;
+          digits(L - H, 0, i);
+          digits(H, 1, i);
+        }
+#pragma unroll
+        for (int q = 0; q < 3; ++q) mp[(uu * 3 + q) * 4 + pp] = make_uint2(pw[0][q], pw[1][q]);
+        su += __shfl_xor_sync(0xffffffffu, su, 1);
+        su += __shfl_xor_sync(0xffffffffu, su, 2);
+        if (pp == 0) sx[uu] = su;
+        if (lane == 0) bx[uu >> 3] = ldexpf(1.f, ex - 21);
+      } else {
+        const float up = ldexpf(1.f, 22 - ex);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) digits(am > 0.f ? __float2int_rn(y[i] * up) : 0, i & 1, i >> 1);
+        const int half = pp >> 1;
+#pragma unroll
+        for (int col = 0; col < 6; ++col)
+          mp[(uu * 6 + col) * 4 + pp] =
+              (col / 3) == half ? make_uint2(pw[0][col % 3], pw[1][col % 3]) : make_uint2(0u, 0u);
+        su += __shfl_xor_sync(0xffffffffu, su, 1);
+        if ((pp & 1) == 0) sx[uu * 2 + half] = su;
+        if (lane == 0) bx[uu >> 3] = ldexpf(1.f, ex - 22);
+      }
+    }
+    if (gamma) {
+      sq = warp_sum(sq);
+      if (lane == 0) sh.red[tid >> 5] = sq;
+    }
+    cons_sync();
+    float inv = 1.f;
+    if (gamma) {
+      float tot = 0.f;
+      for (int w = 0; w < CWARPS; ++w) tot += sh.red[w];
+      inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    }
+    x_inv = inv;
+    mpl = mp;
+    msx = sx;
+    mbx = bx;
+    mfmt = fmt;
+    (void)NB;
+    cons_sync();  // sh.red is reused next
+  }
+
+  // per-warp scratch of an MMA item: int2 scales [16][9], msum [16], fdv [16]
+  static constexpr int WS = 16 * 9 * 2 + 32;
+
+  // One (16-row tile, 256-weight block) item of a Q4_K MMA segment: the
+  // tile's rows start at tb with stride rs; the block is staged at kbl, global
+  // block kb.  Returns rows g and g + 8 on lanes with tig == 0.
+  __device__ void item_q4k(const uint8_t* tb, int rs, int kbl, int kb, int n, float* ws, float& out0, float& out1) {
+    const int lane = tid & 31, g = lane >> 2, tig = lane & 3, sr = lane >> 1, sh2 = lane & 1;
+    int* si = (int*)ws;  // [16][9]
+    float* msum = ws + 16 * 9 * 2;
+    float* fdv = msum + 16;
+    {
+      const int4 hdr = *(const int4*)(tb + min(sr, n - 1) * rs + kbl * Q4K_BLOCK_BYTES);
+      const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((unsigned short)((uint32_t)hdr.x >> 16)));
+      const uint64_t sb = (uint32_t)hdr.y | ((uint64_t)((uint32_t)hdr.z & 0xFFFFu) << 32);
+      const uint64_t mb = ((uint32_t)hdr.z >> 16) | ((uint64_t)(uint32_t)hdr.w << 16);
+      const uint32_t s24 = (uint32_t)(sb >> (24 * sh2)), m24 = (uint32_t)(mb >> (24 * sh2));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) si[sr * 9 + 4 * sh2 + j] = (s24 >> (6 * j)) & 63;
+      const float* q = msx + kb * 8 + 4 * sh2;
+      float mpart = (float)(m24 & 63) * q[0];
+      mpart = fmaf((float)((m24 >> 6) & 63), q[1], mpart);
+      mpart = fmaf((float)((m24 >> 12) & 63), q[2], mpart);
+      mpart = fmaf((float)((m24 >> 18) & 63), q[3], mpart);
+      mpart = dmin * x_inv * (mpart + __shfl_xor_sync(0xffffffffu, mpart, 1));
+      if (sh2 == 0) {
+        msum[sr] = mpart;
+        fdv[sr] = d * mbx[kb] * x_inv;
+      }
+    }
+    __syncwarp();
+    const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : 0.f);
+    const float fB = tig == 0 ? 256.f : 0.f;
+    const uint8_t* rg = tb + min(g, n - 1) * rs + kbl * Q4K_BLOCK_BYTES + 16 + 4 * tig;
+    const uint8_t* rg8 = tb + min(g + 8, n - 1) * rs + kbl * Q4K_BLOCK_BYTES + 16 + 4 * tig;
+    const uint2* plu = mpl + (kb * 8 * 3 + (g % 3)) * 4 + tig;
+    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+#pragma unroll
+    for (int j0 = 0; j0 < 8; j0 += 4) {
+      int dd[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w0 = *(const uint32_t*)(rg + 16 * (j0 + j));
+        const uint32_t w1 = *(const uint32_t*)(rg8 + 16 * (j0 + j));
+        const uint2 b = plu[12 * (j0 + j)];
+        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, w0, w1, b.x, b.y);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int s0 = si[g * 9 + j0 + j], s1 = si[(g + 8) * 9 + j0 + j];
+        t0 += s0 * dd[j][0];
+        t1 += s0 * dd[j][1];
+        t2 += s1 * dd[j][2];
+        t3 += s1 * dd[j][3];
+      }
+    }
+    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
+    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    out0 = fmaf(fdv[g], acc0, -msum[g]);
+    out1 = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    __syncwarp();
+  }
+
+  // Q6_K item: as item_q4k; the d row sits at dofs in every staged row.
+  __device__ void item_q6k(const uint8_t* tb, int rs, int kbl, int kb, int n, int dofs, float* ws, float& out0,
+                           float& out1) {
+    const int lane = tid & 31, g = lane >> 2, tig = lane & 3, sr = lane >> 1, sh2 = lane & 1;
+    int2* scw = (int2*)ws;  // [16][9]
+    float* msum = ws + 16 * 9 * 2;
+    float* fdv = msum + 16;
+    {
+      const uint8_t* rp = tb + min(sr, n - 1) * rs;
+      const int2 sc8 = *(const int2*)(rp + kbl * Q6K_BODY_BYTES + 192 + 8 * sh2);
+      const float d = __half2float(__ushort_as_half(*(const unsigned short*)(rp + dofs + 2 * kb)));
+      const uint32_t sw[2] = {(uint32_t)sc8.x, (uint32_t)sc8.y};
+      const float* hs = msx + 2 * (kb * 8 + 4 * sh2);
+      float mpart = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int sa = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1))) & 0xFF);
+        const int sb = (int)(int8_t)((sw[jj >> 1] >> (16 * (jj & 1) + 8)) & 0xFF);
+        scw[sr * 9 + 4 * sh2 + jj] = make_int2(sa, sb);
+        mpart = fmaf((float)sa, hs[2 * jj], mpart);
+        mpart = fmaf((float)sb, hs[2 * jj + 1], mpart);
+      }
+      mpart += __shfl_xor_sync(0xffffffffu, mpart, 1);
+      if (sh2 == 0) {
+        msum[sr] = 32.f * d * x_inv * mpart;
+        fdv[sr] = d * mbx[kb] * x_inv;
+      }
+    }
+    __syncwarp();
+    const float fA = tig == 0 ? 65536.f : (tig == 1 ? 1.f : (tig == 2 ? 256.f : 0.f));
+    const float fB = tig == 0 ? 256.f : (tig == 1 ? 65536.f : (tig == 2 ? 1.f : 0.f));
+    const bool s0_first = tig < 2, s1_first = tig == 0;
+    const int hshift = 4 * (tig & 1);
+    const uint8_t* rg = tb + min(g, n - 1) * rs + kbl * Q6K_BODY_BYTES;
+    const uint8_t* rg8 = tb + min(g + 8, n - 1) * rs + kbl * Q6K_BODY_BYTES;
+    const uint2* plu = mpl + (kb * 8 * 6 + (g < 6 ? g : 0)) * 4 + tig;
+    int t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+#pragma unroll
+    for (int j0 = 0; j0 < 8; j0 += 4) {
+      int dd[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int jj = j0 + j;
+        const uint32_t w0 = *(const uint32_t*)(rg + 16 * jj + 4 * tig);
+        const uint32_t w1 = *(const uint32_t*)(rg8 + 16 * jj + 4 * tig);
+        const uint32_t W0 = *(const uint32_t*)(rg + 128 + 8 * jj + 4 * (tig >> 1)) >> hshift;
+        const uint32_t W1 = *(const uint32_t*)(rg8 + 128 + 8 * jj + 4 * (tig >> 1)) >> hshift;
+        const uint32_t e0 = (w0 & 0x0F0F0F0Fu) | ((W0 << 4) & 0x30303030u);
+        const uint32_t e1 = (w1 & 0x0F0F0F0Fu) | ((W1 << 4) & 0x30303030u);
+        const uint32_t o0 = ((w0 >> 4) & 0x0F0F0F0Fu) | ((W0 << 2) & 0x30303030u);
+        const uint32_t o1 = ((w1 >> 4) & 0x0F0F0F0Fu) | ((W1 << 2) & 0x30303030u);
+        const uint2 b = plu[24 * jj];
+        mma_u8s8(dd[j][0], dd[j][1], dd[j][2], dd[j][3], e0, e1, o0, o1, b.x, b.y);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int2 s0 = scw[g * 9 + j0 + j], s1 = scw[(g + 8) * 9 + j0 + j];
+        t0 += (s0_first ? s0.x : s0.y) * dd[j][0];
+        t1 += (s1_first ? s0.x : s0.y) * dd[j][1];
+        t2 += (s0_first ? s1.x : s1.y) * dd[j][2];
+        t3 += (s1_first ? s1.x : s1.y) * dd[j][3];
+      }
+    }
+    float acc0 = fmaf((float)t0, fA, (float)t1 * fB);
+    float acc1 = fmaf((float)t2, fA, (float)t3 * fB);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    out0 = fmaf(fdv[g], acc0, -msum[g]);
+    out1 = fmaf(fdv[g + 8], acc1, -msum[g + 8]);
+    __syncwarp();
+  }
+
+  // MMA segment body: the CTA's (tile, block) items, round-robin over the warps
+  // and in stage order; every warp arrives on each stage's empty barrier once,
+  // after its last item there.  Block partials go to red [tiles][nT][NB][16].
+  __device__ bool seg_mma_body(const MegaSeg& s, int K, int r0, int r1, float*& red_out) {
+    const MGeo m = mgeo(s, K, slot_bytes);
+    const int nout = r1 - r0, ntiles = (nout + 15) / 16, nst = ntiles * m.nch;
+    const int red_n = ntiles * m.nT * m.NB * 16;
+    // red and the warp scratch: in the dead staging area when they fit, else after the planes
+    float* base = (red_n + CWARPS * WS <= K) ? part : part + ((mend + 3) & ~3);  // int2 scratch: 16 B aligned
+    if ((base - part) + red_n + CWARPS * WS > a.part_floats) {  // host sizing covers every phase
+      if (tid == 0) atomicExch(a.status, SM_ERR_UNSUPPORTED);
+      sh.abort = 1;
+      return false;
+    }
+    float* red = base;
+    float* ws = base + red_n + (tid >> 5) * WS;
+    const int lane = tid & 31, warp = tid >> 5;
+    // walk the stages without divisions: stage st = (tile t, block chunk c) holds
+    // per = nT * nkb items; this warp's items are warp, warp + CWARPS, ...
+    int st = 0, t = 0, c = 0, nkb = min(m.nkbs, m.NB), per = m.nT * nkb, loc = warp;
+    int slot = k % a.nslots;
+    uint32_t par = (uint32_t)(k / a.nslots) & 1u;
+    bool waited = false;
+    while (true) {
+      while (st < nst && loc >= per) {
+        // leave stage st: a stage this warp had no item in is released only once it
+        // has filled, so the arrival cannot reach the slot's previous use
+        if (!waited && !mbar_wait_spin(&sh.full[slot], par, a.status)) {
+          sh.abort = 1;
+          return false;
+        }
+        if (lane == 0) mbar_arrive(&sh.empty[slot]);
+        waited = false;
+        loc -= per;
+        ++st;
+        if (++c == m.nch) c = 0, ++t;
+        nkb = min(m.nkbs, m.NB - c * m.nkbs);
+        per = m.nT * nkb;
+        if (++slot == a.nslots) slot = 0, par ^= 1u;
+      }
+      if (st >= nst) break;
+      if (!waited) {
+        if (!mbar_wait_spin(&sh.full[slot], par, a.status)) {
+          sh.abort = 1;
+          return false;
+        }
+        waited = true;
+      }
+      const int tt = loc >= nkb ? 1 : 0, kbl = loc - tt * nkb, kb = c * m.nkbs + kbl;
+      const int n = min(16, nout - 16 * t);
+      const uint8_t* tb = ring + slot * slot_bytes + tt * 16 * m.rs;
+      float o0, o1;
+      if (s.fmt == SM_Q4_K)
+        item_q4k(tb, m.rs, kbl, kb, n, ws, o0, o1);
+      else
+        item_q6k(tb, m.rs, kbl, kb, n, m.nkbs * m.bb, ws, o0, o1);
+      if ((lane & 3) == 0) {
+        float* rd = red + ((t * m.nT + tt) * m.NB + kb) * 16;
+        rd[lane >> 2] = o0;
+        rd[(lane >> 2) + 8] = o1;
+      }
+      loc += CWARPS;
+    }
+    __syncwarp();
+    k += nst;
+    red_out = red;
+    return true;
+  }
+
   // one unit of a staged row (integer dot path); `auxp` is the row's staged scales / d
   __device__ float dot(int fmt, int bs, const uint8_t* rowp, const uint8_t* auxp) {
     switch (fmt) {
@@ -408,7 +796,16 @@ struct Consumer {
     const int64_t rbytes = row_bytes_fmt(s.fmt, K);
     const bool glu = s.mode == GEMV_GLU;
     const GemvSeg g = to_gemv(s);
-    if ((s.fmt != SM_Q8_0) != pair) load_x(x_src, x_gamma, x_K, s.fmt != SM_Q8_0);
+    const bool use_mma = mma_seg(a, s);
+    float* mred = nullptr;
+    const MGeo mg = mgeo(s, K, slot_bytes);
+    if (use_mma) {
+      if (mfmt != s.fmt) load_x(x_src, x_gamma, x_K, true, s.fmt);
+      stamp();
+      stamp();
+      if (!seg_mma_body(s, K, r0, r1, mred)) return false;
+    } else {
+    if ((s.fmt != SM_Q8_0) != pair || mfmt) load_x(x_src, x_gamma, x_K, s.fmt != SM_Q8_0);
     stamp();
     for (int row = r0; row < r1; row += rb) {
       const int n = min(rb, r1 - row);
@@ -451,6 +848,7 @@ struct Consumer {
       ++k;
     }
     if (r0 == r1) stamp();
+    }
     stamp();
     cons_sync();
     const bool pairs = s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE;
@@ -472,7 +870,14 @@ struct Consumer {
       }
       for (int q = 0; q < nr; ++q) {
         float t = 0.f;
-        for (int j = 0; j < nwpp; ++j) t += part[rin[q] * nwpp + j];
+        if (mred) {
+          // MMA partials: row rin of the gate (or, past nout, the up) tiles, blocks in order
+          const int tt = rin[q] >= nout ? 1 : 0, lr = rin[q] - tt * nout;
+          const float* rd = mred + (((lr >> 4) * mg.nT + tt) * mg.NB) * 16 + (lr & 15);
+          for (int b = 0; b < mg.NB; ++b) t += rd[b * 16];
+        } else {
+          for (int j = 0; j < nwpp; ++j) t += part[rin[q] * nwpp + j];
+        }
         v[q] = t;
       }
       if (glu)
@@ -762,6 +1167,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     rope_s[0][t] = a.sin_t[(int64_t)(len - 1) * half + t];
     rope_s[1][t] = a.cos_t[(int64_t)(len - 1) * half + t];
   }
+  if (tid < (int)(sizeof(MegaLayer) / 4)) ((int*)&sh.lay)[tid] = __ldg((const int*)&a.layers[0] + tid);
   cons_sync();
   c.ep.pos = &pos_s;
   // epilogue reads table[pos * half + i]: point at the shared row shifted back by pos * half
@@ -775,10 +1181,15 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   const int chunks = max(1, (int)gridDim.x / a.nKv);
   (void)G;
   for (int l = 0; l < a.n_layers; ++l) {
-    const MegaLayer& L = a.layers[l];
+    const MegaLayer& L = sh.lay;
     // Q|K|V with RMSNorm; RoPE and the KV append in the epilogue
-    if (l > 0 && !c.grid_barrier()) return;
-    c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, L.qkv[0].fmt != SM_Q8_0);
+    if (l > 0 && !c.grid_barrier(&a.layers[l])) return;
+    {
+      int cbq[4];
+      qkv_split(L, a.H, gridDim.x, cbq);
+      const MegaSeg& sq = L.qkv[blockIdx.x < cbq[1] ? 0 : (blockIdx.x < cbq[2] ? 1 : 2)];
+      c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, sq.fmt != SM_Q8_0, mma_seg(a, sq) ? sq.fmt : 0);
+    }
     if (tid == 0) sh.phase = 4 * l;
     {
       int cb[4];
@@ -806,20 +1217,20 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     if (!c.grid_barrier()) return;
     c.attn_combine(chunks);
     if (!c.grid_barrier()) return;
-    c.load_x(a.att, nullptr, a.qd, L.o.fmt != SM_Q8_0);
+    c.load_x(a.att, nullptr, a.qd, L.o.fmt != SM_Q8_0, mma_seg(a, L.o) ? L.o.fmt : 0);
     if (tid == 0) sh.phase = 4 * l + 1;
     if (!c.seg(L.o, a.qd, a.stage_rows_h)) return;
     if (!c.grid_barrier()) return;
-    c.load_x(a.x, L.ffn_norm, a.H, L.gu.fmt != SM_Q8_0);
+    c.load_x(a.x, L.ffn_norm, a.H, L.gu.fmt != SM_Q8_0, mma_seg(a, L.gu) ? L.gu.fmt : 0);
     if (tid == 0) sh.phase = 4 * l + 2;
     if (!c.seg(L.gu, a.H, a.stage_rows_h)) return;
     if (!c.grid_barrier()) return;
-    c.load_x(a.act, nullptr, a.F, L.down.fmt != SM_Q8_0);
+    c.load_x(a.act, nullptr, a.F, L.down.fmt != SM_Q8_0, mma_seg(a, L.down) ? L.down.fmt : 0);
     if (tid == 0) sh.phase = 4 * l + 3;
     if (!c.seg(L.down, a.F, a.stage_rows_f)) return;
   }
   if (!c.grid_barrier()) return;
-  c.load_x(a.x, a.out_norm, a.H, a.head.fmt != SM_Q8_0);
+  c.load_x(a.x, a.out_norm, a.H, a.head.fmt != SM_Q8_0, mma_seg(a, a.head) ? a.head.fmt : 0);
   if (tid == 0) sh.phase = 4 * a.n_layers;
   if (!c.seg(a.head, a.H, a.stage_rows_v, &a.amax_val[blockIdx.x], &a.amax_idx[blockIdx.x])) return;
   c.stamp();
@@ -883,6 +1294,19 @@ bool mega_supported(const MegaArgs& a) {
   return true;
 }
 
+void mega_layer_split(MegaLayer& L, int K, int grid) {
+  int64_t b[3], tot = 0;
+  for (int i = 0; i < 3; ++i) {
+    b[i] = (int64_t)L.qkv[i].rows * (row_bytes_fmt(L.qkv[i].fmt, K) + aux_row_bytes(L.qkv[i]));
+    tot += b[i];
+  }
+  int* cb = L.qkv_cb;
+  cb[0] = 0;
+  cb[1] = (int)std::min<int64_t>(grid - 2, std::max<int64_t>(1, (grid * b[0] + tot / 2) / tot));
+  cb[2] = (int)std::min<int64_t>(grid - 1, std::max<int64_t>(cb[1] + 1, cb[1] + (grid * b[1] + tot / 2) / tot));
+  cb[3] = grid;
+}
+
 bool mega_seg_supported(const MegaSeg& s) {
   if (s.fmt == SM_Q4_K) return true;
   return (s.fmt == SM_Q6_K || s.fmt == SM_Q8_0 || s.fmt == SM_Q4_0) && s.aux_stride > 0;
@@ -912,13 +1336,24 @@ int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch) {
   // partials: the most rows any CTA holds in one segment (GLU: gate + up) x units
   auto cta_rows = [&](int rows) { return 2 * (((rows + 1) / 2 + grid - 1) / grid); };
   auto nwpp = [](int K) { return (int64_t)((K / 32 + 31) / 32); };
-  const int64_t part = std::max({(int64_t)2 * cta_rows(a.F) * nwpp(a.H), (int64_t)cta_rows(a.qd) * nwpp(a.H),
+  const int64_t part0 = std::max({(int64_t)2 * cta_rows(a.F) * nwpp(a.H), (int64_t)cta_rows(a.qd) * nwpp(a.H),
                                  (int64_t)cta_rows(a.H) * std::max(nwpp(a.qd), nwpp(a.F)),
                                  (int64_t)cta_rows(a.V) * nwpp(a.H), (int64_t)MGMAX * (a.max_ctx / 2 + 64) + 4096,
                                  (int64_t)(MGMAX + 64) * (a.max_ctx / std::max(1, grid / a.nKv) + 2) + 4096 +
                                      (int64_t)std::max(1, grid / a.nKv) * MGMAX,
                                  (int64_t)2 * std::max({a.H, a.qd, a.F}) + 28 * (std::max({a.H, a.qd, a.F}) / 32) + 64});
+  // MMA segments: digit planes (50 floats per unit + 1 per block) after the
+  // staged vector, then the block partials and the warps' scratch
+  auto mma_part = [&](int K, int rows, int nT, bool gamma) {
+    const int64_t tiles = (rows / nT + 15) / 16;
+    return (int64_t)(gamma ? 2 : 1) * K + 50 * (K / 32) + K / 256 + 4 + tiles * nT * (K / 256) * 16 + (int64_t)CWARPS * 320;
+  };
+  const int64_t part = std::max({part0, mma_part(a.H, cta_rows(2 * a.F), 2, true),
+                                 mma_part(a.H, cta_rows(4 * a.qd), 1, true), mma_part(a.H, cta_rows(a.V), 1, true),
+                                 mma_part(a.qd, cta_rows(a.H), 1, false), mma_part(a.F, cta_rows(a.H), 1, false)});
   a.part_floats = (int)part;
+  a.use_mma = 1;  // SMALLMIND_MEGA_MMA=0: Q4_K / Q6_K phases on the dp4a path
+  if (const char* e = std::getenv("SMALLMIND_MEGA_MMA")) a.use_mma = atoi(e);
   const int shared_bytes = (int)((sizeof(Shared) + 127) / 128 * 128);
   a.ring_offset = (int)((shared_bytes + part * 4 + 127) / 128 * 128);
   const int64_t ring = smem_total - a.ring_offset;

@@ -26,6 +26,7 @@ struct MegaLayer {
   const float* ffn_norm = nullptr;
   const float* kc = nullptr;  // layer bases of the head-major cache
   const float* vc = nullptr;
+  int qkv_cb[4] = {0, 0, 0, 0};  // CTAs [qkv_cb[s], qkv_cb[s + 1]) run segment s (mega_layer_split)
 };
 
 struct MegaArgs {
@@ -59,6 +60,7 @@ struct MegaArgs {
   // schedule
   int nslots = 0, ring_offset = 0, part_floats = 0, smem_bytes = 0;
   int stage_rows_h = 1, stage_rows_f = 1, stage_rows_v = 1;
+  int use_mma = 1;    // Q4_K / Q6_K phases on the int8 tensor-core path
   int lookahead = 1;  // 0: the producer only issues a phase's stages once the consumers entered it  // stage rows for K = H / qd, K = F, LM head
 };
 
@@ -67,6 +69,8 @@ constexpr int MEGA_TRACE_EVENTS = 1024;
 // Sizes of the scratch the launcher expects (floats / ints) for a given grid.
 size_t mega_scratch_floats(int nH, int nKv, int hd, int max_ctx, int grid);
 bool mega_supported(const MegaArgs& a);
+// Q|K|V CTA ranges of a layer for a grid of `grid` CTAs, in proportion to each segment's bytes
+void mega_layer_split(MegaLayer& L, int K, int grid);
 bool mega_seg_supported(const MegaSeg& s);
 int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch);
 int mega_grid_size();
