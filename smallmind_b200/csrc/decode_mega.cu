@@ -340,7 +340,7 @@ struct Consumer {
     cons_sync();
     if (lxe >= 0) stamp_at(lxe + 2);
     if (mma) {
-      build_mma_planes(K, gamma, mma);
+      build_mma_planes(K, gamma, mma, lxe);
       return;
     }
     // The byte planes of every unit, built once per CTA: four threads per unit,
@@ -434,7 +434,7 @@ struct Consumer {
   // raw-byte positions (L: 21-bit low elements, H: 17-bit high elements), see
   // gemv_mma.cu; Q6_K: 22-bit values, six columns (three per 16-element half,
   // zero at the other half's positions).
-  __device__ void build_mma_planes(int K, const float* gamma, int fmt) {
+  __device__ void build_mma_planes(int K, const float* gamma, int fmt, int lxe) {
     const int U = K >> 5, NB = K >> 8, lane = tid & 31;
     const float4* xs = (const float4*)part;
     const float4* gs = (const float4*)part + K / 4;  // staged gamma (when given)
@@ -509,7 +509,9 @@ struct Consumer {
       sq = warp_sum(sq);
       if (lane == 0) sh.red[tid >> 5] = sq;
     }
+    if (lxe >= 0) stamp_at(lxe + 3);
     cons_sync();
+    if (lxe >= 0) stamp_at(lxe + 4);
     float inv = 1.f;
     if (gamma) {
       float tot = 0.f;
@@ -523,6 +525,7 @@ struct Consumer {
     mfmt = fmt;
     (void)NB;
     cons_sync();  // sh.red is reused next
+    if (lxe >= 0) stamp_at(lxe + 5);
   }
 
   // per-warp scratch of an MMA item: int2 scales [16][9], msum [16], fdv [16]
@@ -1131,16 +1134,21 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     // ------------------------------------------------------------ producer
     if ((tid & 31) == 0) {
       Producer p{a, sh, ring, slot_bytes};
-      for (int l = 0; l < a.n_layers; ++l) {
-        const MegaLayer& L = a.layers[l];
-        int cb[4];
-        qkv_split(L, a.H, gridDim.x, cb);
-        for (int s = 0; s < 3; ++s) p.seg(L.qkv[s], a.H, a.stage_rows_h, 4 * l, cb[s], cb[s + 1]);
-        p.seg(L.o, a.qd, a.stage_rows_h, 4 * l + 1);
-        p.seg(L.gu, a.H, a.stage_rows_h, 4 * l + 2);
-        p.seg(L.down, a.F, a.stage_rows_f, 4 * l + 3);
+      // one call site per kind of work keeps the kernel's code small (phase p:
+      // layer p / 4, Q|K|V, O, gate|up, down; the last one is the LM head)
+      for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
+        const int l = ph >> 2, kind = ph & 3;
+        const bool head = l == a.n_layers;
+        const MegaLayer& L = a.layers[head ? 0 : l];
+        const int ns = (kind == 0 && !head) ? 3 : 1;
+        for (int s = 0; s < ns; ++s) {
+          const MegaSeg& sg = head ? a.head : (kind == 0 ? L.qkv[s] : (kind == 1 ? L.o : (kind == 2 ? L.gu : L.down)));
+          const int K = (kind == 1 && !head) ? a.qd : ((kind == 3 && !head) ? a.F : a.H);
+          const int rb = head ? a.stage_rows_v : (kind == 3 ? a.stage_rows_f : a.stage_rows_h);
+          const int c0 = ns == 3 ? L.qkv_cb[s] : 0, c1 = ns == 3 ? L.qkv_cb[s + 1] : -1;
+          p.seg(sg, K, rb, ph, c0, c1);
+        }
       }
-      p.seg(a.head, a.H, a.stage_rows_v, 4 * a.n_layers);
       // drain: wait (bounded) until every stage issued has landed before exiting
       if (!p.ok) {
         for (int kk = max(0, p.k - a.nslots); kk < p.k; ++kk)
@@ -1180,59 +1188,54 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   const int G = a.nH / a.nKv;
   const int chunks = max(1, (int)gridDim.x / a.nKv);
   (void)G;
-  for (int l = 0; l < a.n_layers; ++l) {
+  // one call site per kind of work keeps the kernel's code small: phase p is
+  // layer p / 4, kind Q|K|V (attention follows), O, gate|up, down; the last
+  // phase is the LM head
+  for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
+    const int l = ph >> 2, kind = ph & 3;
+    const bool head = l == a.n_layers;
     const MegaLayer& L = sh.lay;
-    // Q|K|V with RMSNorm; RoPE and the KV append in the epilogue
-    if (l > 0 && !c.grid_barrier(&a.layers[l])) return;
-    {
-      int cbq[4];
-      qkv_split(L, a.H, gridDim.x, cbq);
-      const MegaSeg& sq = L.qkv[blockIdx.x < cbq[1] ? 0 : (blockIdx.x < cbq[2] ? 1 : 2)];
-      c.load_x(l == 0 ? emb : a.x, L.attn_norm, a.H, sq.fmt != SM_Q8_0, mma_seg(a, sq) ? sq.fmt : 0);
+    if (kind == 1) {
+      if (!c.grid_barrier()) return;
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
+      if (!c.grid_barrier()) return;
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_pv(L, it / chunks, it % chunks, chunks, len);
+      if (!c.grid_barrier()) return;
+      c.attn_combine(chunks);
     }
-    if (tid == 0) sh.phase = 4 * l;
-    {
-      int cb[4];
-      qkv_split(L, a.H, gridDim.x, cb);
-      const int s = blockIdx.x < cb[1] ? 0 : (blockIdx.x < cb[2] ? 1 : 2);
-      if (!c.seg(L.qkv[s], a.H, a.stage_rows_h, nullptr, nullptr, cb[s], cb[s + 1])) return;
+    // the layer's table entry comes on chip during the barrier before its Q|K|V
+    if (ph > 0 && !c.grid_barrier(kind == 0 && !head ? &a.layers[l] : nullptr)) return;
+    int s = 0, c0 = 0, c1 = -1;
+    if (kind == 0 && !head) {
+      s = blockIdx.x < L.qkv_cb[1] ? 0 : (blockIdx.x < L.qkv_cb[2] ? 1 : 2);
+      c0 = L.qkv_cb[s];
+      c1 = L.qkv_cb[s + 1];
     }
-    // this CTA's attention chunks of the layer: K / V rows into L2 while it waits at
-    // the barrier (issued after the vector loads, which they would otherwise delay)
-    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
-      const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
-      const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
-      const int64_t off = ((int64_t)seqv * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
-      const int lines = (j1 - j0) * 2;  // 256-byte rows
-      for (int t = tid; t < 2 * lines; t += CT) {
-        const float* base = (t < lines ? L.kc : L.vc) + off;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
+    const MegaSeg& sg = head ? a.head : (kind == 0 ? L.qkv[s] : (kind == 1 ? L.o : (kind == 2 ? L.gu : L.down)));
+    // RMSNorm (Q|K|V, gate|up, head) on the residual stream; O reads the attention output, down the GLU
+    const float* src = kind == 1 ? a.att : (kind == 3 ? a.act : (ph == 0 ? emb : a.x));
+    const float* gamma = head ? a.out_norm : (kind == 0 ? L.attn_norm : (kind == 2 ? L.ffn_norm : nullptr));
+    const int K = (kind == 1 && !head) ? a.qd : ((kind == 3 && !head) ? a.F : a.H);
+    const int rb = head ? a.stage_rows_v : (kind == 3 ? a.stage_rows_f : a.stage_rows_h);
+    c.load_x(src, gamma, K, sg.fmt != SM_Q8_0, mma_seg(a, sg) ? sg.fmt : 0);
+    if (tid == 0) sh.phase = ph;
+    if (!c.seg(sg, K, rb, head ? &a.amax_val[blockIdx.x] : nullptr, head ? &a.amax_idx[blockIdx.x] : nullptr, c0, c1))
+      return;
+    if (kind == 0 && !head) {
+      // this CTA's attention chunks of the layer: K / V rows into L2 while it waits at
+      // the barrier (issued after the vector loads, which they would otherwise delay)
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
+        const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
+        const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
+        const int64_t off = ((int64_t)seqv * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
+        const int lines = (j1 - j0) * 2;  // 256-byte rows
+        for (int t = tid; t < 2 * lines; t += CT) {
+          const float* base = (t < lines ? L.kc : L.vc) + off;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
+        }
       }
     }
-
-    if (!c.grid_barrier()) return;
-    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
-    if (!c.grid_barrier()) return;
-    for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_pv(L, it / chunks, it % chunks, chunks, len);
-    if (!c.grid_barrier()) return;
-    c.attn_combine(chunks);
-    if (!c.grid_barrier()) return;
-    c.load_x(a.att, nullptr, a.qd, L.o.fmt != SM_Q8_0, mma_seg(a, L.o) ? L.o.fmt : 0);
-    if (tid == 0) sh.phase = 4 * l + 1;
-    if (!c.seg(L.o, a.qd, a.stage_rows_h)) return;
-    if (!c.grid_barrier()) return;
-    c.load_x(a.x, L.ffn_norm, a.H, L.gu.fmt != SM_Q8_0, mma_seg(a, L.gu) ? L.gu.fmt : 0);
-    if (tid == 0) sh.phase = 4 * l + 2;
-    if (!c.seg(L.gu, a.H, a.stage_rows_h)) return;
-    if (!c.grid_barrier()) return;
-    c.load_x(a.act, nullptr, a.F, L.down.fmt != SM_Q8_0, mma_seg(a, L.down) ? L.down.fmt : 0);
-    if (tid == 0) sh.phase = 4 * l + 3;
-    if (!c.seg(L.down, a.F, a.stage_rows_f)) return;
   }
-  if (!c.grid_barrier()) return;
-  c.load_x(a.x, a.out_norm, a.H, a.head.fmt != SM_Q8_0, mma_seg(a, a.head) ? a.head.fmt : 0);
-  if (tid == 0) sh.phase = 4 * a.n_layers;
-  if (!c.seg(a.head, a.H, a.stage_rows_v, &a.amax_val[blockIdx.x], &a.amax_idx[blockIdx.x])) return;
   c.stamp();
   // greedy argmax over the CTAs' partial maxima (lowest id on ties); the last CTA commits
   __threadfence();
