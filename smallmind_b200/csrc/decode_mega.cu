@@ -109,11 +109,6 @@ __device__ __forceinline__ MGeo mgeo(const MegaSeg& s, int K, int64_t slot_bytes
 
 // Q|K|V: CTAs [cb[s], cb[s+1]) take segment s, in proportion to its bytes, so
 // every CTA runs one segment (one stage stream, one epilogue) per phase.
-__device__ __forceinline__ void qkv_split(const MegaLayer& L, int /*K*/, int /*grid*/, int (&cb)[4]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) cb[i] = L.qkv_cb[i];
-}
-
 // segment rows of CTA `i` when CTAs [c0, c1) share the segment (none outside)
 __device__ __forceinline__ void seg_rows_in(int rows, int i, int c0, int c1, int& r0, int& r1) {
   if (i < c0 || i >= c1) {
@@ -328,6 +323,11 @@ struct Consumer {
     // 16-byte chunk c of unit w is stored at chunk (c + w) % 8 of that unit, so the
     // 8 lanes of a quarter-warp reading chunk c of 8 consecutive units hit 8
     // different bank groups.
+    if (mma) {
+      // the tensor-core path needs no staged copy: each lane reads its own elements
+      build_mma_planes(src, K, gamma, mma, lxe);
+      return;
+    }
     float4* xs = (float4*)part;        // [K/4]
     float4* gs = (float4*)part + K / 4; // [K/4]
     uint32_t* pls = (uint32_t*)(part + 2 * K);  // [U][28]: planes a, b, c (8 words each), inv, x16a, x16b
@@ -339,10 +339,6 @@ struct Consumer {
     if (lxe >= 0) stamp_at(lxe + 1);
     cons_sync();
     if (lxe >= 0) stamp_at(lxe + 2);
-    if (mma) {
-      build_mma_planes(K, gamma, mma, lxe);
-      return;
-    }
     // The byte planes of every unit, built once per CTA: four threads per unit,
     // eight elements each, from y = gamma * x (the RMS scale is a per-vector
     // scalar and is folded into each unit's factor below); the same pass
@@ -434,11 +430,9 @@ struct Consumer {
   // raw-byte positions (L: 21-bit low elements, H: 17-bit high elements), see
   // gemv_mma.cu; Q6_K: 22-bit values, six columns (three per 16-element half,
   // zero at the other half's positions).
-  __device__ void build_mma_planes(int K, const float* gamma, int fmt, int lxe) {
+  __device__ void build_mma_planes(const float* src, int K, const float* gamma, int fmt, int lxe) {
     const int U = K >> 5, NB = K >> 8, lane = tid & 31;
-    const float4* xs = (const float4*)part;
-    const float4* gs = (const float4*)part + K / 4;  // staged gamma (when given)
-    const int pbase = gamma ? 2 * K : K;
+    const int pbase = K;  // part [0, K) stays free for the block partials
     uint2* mp = (uint2*)(part + pbase);        // [U][6][4] at most
     float* sx = part + pbase + 48 * U;         // [U][2] at most
     float* bx = sx + 2 * U;                    // [NB]
@@ -446,10 +440,13 @@ struct Consumer {
     float sq = 0.f;
     for (int t0 = (tid >> 5) * 32; t0 < 4 * U; t0 += CT) {  // 4U is a multiple of 32: whole warps
       const int t = t0 + lane, uu = t >> 2, pp = t & 3;
-      const float4 v0 = xs[(uu << 3) + ((2 * pp + uu) & 7)], v1 = xs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+      // the vector was written by other CTAs: bypass L1
+      const float4* xg = (const float4*)(src + 32 * uu + 8 * pp);
+      const float4 v0 = __ldcg(xg), v1 = __ldcg(xg + 1);
       float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       if (gamma) {
-        const float4 g0 = gs[(uu << 3) + ((2 * pp + uu) & 7)], g1 = gs[(uu << 3) + ((2 * pp + 1 + uu) & 7)];
+        const float4* gg = (const float4*)(gamma + 32 * uu + 8 * pp);
+        const float4 g0 = __ldg(gg), g1 = __ldg(gg + 1);
         const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -524,7 +521,6 @@ struct Consumer {
     mbx = bx;
     mfmt = fmt;
     (void)NB;
-    cons_sync();  // sh.red is reused next
     if (lxe >= 0) stamp_at(lxe + 5);
   }
 
