@@ -798,13 +798,18 @@ struct Consumer {
     const bool use_mma = mma_seg(a, s);
     float* mred = nullptr;
     const MGeo mg = mgeo(s, K, slot_bytes);
+    // the caller staged the vector for this segment's path (one staging call site
+    // keeps the kernel small): a mismatch is a scheduling error
+    if (use_mma ? mfmt != s.fmt : (mfmt != 0 || (s.fmt != SM_Q8_0) != pair)) {
+      if (tid == 0) atomicExch(a.status, SM_ERR_UNSUPPORTED);
+      sh.abort = 1;
+      return false;
+    }
     if (use_mma) {
-      if (mfmt != s.fmt) load_x(x_src, x_gamma, x_K, true, s.fmt);
       stamp();
       stamp();
       if (!seg_mma_body(s, K, r0, r1, mred)) return false;
     } else {
-    if ((s.fmt != SM_Q8_0) != pair || mfmt) load_x(x_src, x_gamma, x_K, s.fmt != SM_Q8_0);
     stamp();
     for (int row = r0; row < r1; row += rb) {
       const int n = min(rb, r1 - row);
@@ -944,7 +949,7 @@ struct Consumer {
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
     float* qs = att_pp(per);  // [G][64]
     float* es = att_es();
-    for (int t = tid; t < G * HD; t += CT) qs[t] = __ldcg(&a.q[g * G * HD + t]);
+    for (int t = tid; t < G * HD / 4; t += CT) ((float4*)qs)[t] = __ldcg((const float4*)&a.q[g * G * HD] + t);
     cons_sync();
     const int64_t seq = seq_v;
     const float* kb = L.kc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
@@ -1073,15 +1078,38 @@ struct Consumer {
     float* vals = part;                  // [n][chunks]
     float* tots = part + n * chunks;     // [2][chunks] partial sums of the (at most two) heads spanned
     const int h0 = o0 / 64;
-    for (int t = tid; t < n * chunks; t += CT) {
-      const int o = o0 + t / chunks, c = t % chunks;
-      const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
-      vals[t] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
-    }
     const int nh = (o1 - 1) / 64 - h0 + 1;
-    for (int t = tid; t < nh * chunks; t += CT) {
-      const int h = h0 + t / chunks, c = t % chunks, g = h / G, hh = h % G;
-      tots[t] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
+    // every partial of this slice in one batch of loads (one L2 round trip, not one per pass)
+    const int nv = n * chunks, nt = nh * chunks;
+    constexpr int B = 4;
+    float lv[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int t = tid + b * CT;
+      lv[b] = 0.f;
+      if (t < nv) {
+        const int o = o0 + t / chunks, c = t % chunks;
+        const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
+        lv[b] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
+      } else if (t < nv + nt) {
+        const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
+        lv[b] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int t = tid + b * CT;
+      if (t < nv + nt) vals[t] = lv[b];  // tots follows vals
+    }
+    for (int t = tid + B * CT; t < nv + nt; t += CT) {  // more partials than the batch holds
+      if (t < nv) {
+        const int o = o0 + t / chunks, c = t % chunks;
+        const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
+        vals[t] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
+      } else {
+        const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
+        vals[t] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
+      }
     }
     cons_sync();
     for (int t = tid; t < n; t += CT) {
