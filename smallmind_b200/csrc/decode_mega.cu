@@ -118,10 +118,26 @@ __device__ __forceinline__ void seg_rows_in(int rows, int i, int c0, int c1, int
   seg_rows(rows, i - c0, c1 - c0, r0, r1);
 }
 
+// What a GEMV phase of the consumers needs besides the data: worked out by one
+// thread while the CTA waits at the grid barrier before the phase.
+struct SegPlan {
+  const MegaSeg* s;
+  const float* src;    // input vector
+  const float* gamma;  // RMSNorm weight (null: none)
+  float* amax_v;       // LM head: this CTA's argmax slot
+  int* amax_i;
+  int K, rb, r0, r1;   // inputs, dp4a stage rows, this CTA's output rows
+  int mma;             // the int8 tensor-core path
+  MGeo mg;
+  int nst, red_n, red_off;  // MMA: stages, block partials, their offset in part
+  int slot0, par0;          // ring slot and parity of the segment's first stage
+};
+
 struct Shared {
   uint64_t full[16];
   uint64_t empty[16];
-  MegaLayer lay;  // the consumers' copy of the current layer's table entry
+  MegaLayer lay[2];  // the consumers' copies of the layer table (layer l in lay[l & 1])
+  SegPlan plan;      // the next GEMV phase
   float red[MW * MGMAX];
   float vec[4 * MGMAX];
   int flag[4];
@@ -262,14 +278,55 @@ struct Consumer {
   int U = 1, u = 0, ph = 0, P = 1, nwpp = 1;
   bool u_ok = false;
 
-  __device__ bool grid_barrier(const MegaLayer* next = nullptr) {
+  // Plan GEMV phase ph (layer ph / 4; kind Q|K|V, O, gate|up, down; the last one
+  // is the LM head) into sh.plan.  Runs on one thread.
+  __device__ void prepare(int ph, const float* emb) {
+    SegPlan& P = sh.plan;
+    const int l = ph >> 2, kind = ph & 3;
+    const bool head = l == a.n_layers;
+    const MegaLayer& L = sh.lay[l & 1];
+    int si = 0, c0 = 0, c1 = (int)gridDim.x;
+    if (kind == 0 && !head) {
+      si = blockIdx.x < L.qkv_cb[1] ? 0 : (blockIdx.x < L.qkv_cb[2] ? 1 : 2);
+      c0 = L.qkv_cb[si];
+      c1 = L.qkv_cb[si + 1];
+    }
+    const MegaSeg& sg = head ? a.head : (kind == 0 ? L.qkv[si] : (kind == 1 ? L.o : (kind == 2 ? L.gu : L.down)));
+    P.s = &sg;
+    // RMSNorm (Q|K|V, gate|up, head) on the residual stream; O reads the attention output, down the GLU
+    P.src = (kind == 1 && !head) ? a.att : ((kind == 3 && !head) ? a.act : (ph == 0 ? emb : a.x));
+    P.gamma = head ? a.out_norm : (kind == 0 ? L.attn_norm : (kind == 2 ? L.ffn_norm : nullptr));
+    P.amax_v = head ? &a.amax_val[blockIdx.x] : nullptr;
+    P.amax_i = head ? &a.amax_idx[blockIdx.x] : nullptr;
+    const int K = (kind == 1 && !head) ? a.qd : ((kind == 3 && !head) ? a.F : a.H);
+    P.K = K;
+    P.rb = stage_rows(sg, K, slot_bytes);
+    seg_rows_in(sg.rows, blockIdx.x, c0, c1, P.r0, P.r1);
+    P.mma = mma_seg(a, sg);
+    P.slot0 = k % a.nslots;
+    P.par0 = (k / a.nslots) & 1;
+    if (P.mma) {
+      const MGeo m = mgeo(sg, K, slot_bytes);
+      P.mg = m;
+      const int ntiles = (P.r1 - P.r0 + 15) / 16;
+      P.nst = ntiles * m.nch;
+      P.red_n = ntiles * m.nT * m.NB * 16;
+      // block partials and the warp scratch: below the digit planes when they fit, else after them
+      const int mend = K + 50 * (K >> 5) + (K >> 8);
+      P.red_off = (P.red_n + CWARPS * WS <= K) ? 0 : ((mend + 3) & ~3);
+    }
+  }
+
+  // `next`: a layer table entry to bring on chip into lay[next_slot]; `prep`: the
+  // GEMV phase to plan (thread 64), both while thread 0 waits
+  __device__ bool grid_barrier(const MegaLayer* next = nullptr, int next_slot = 0, int prep = -1,
+                               const float* emb = nullptr) {
     // all consumer stores of this CTA are done before thread 0 arrives
     cons_sync();
     stamp();
-    // the next layer's table entry comes on chip while thread 0 waits (the
-    // current entry is no longer read past the first CTA barrier)
     if (next && tid >= 32 && tid < 32 + (int)(sizeof(MegaLayer) / 4))
-      ((int*)&sh.lay)[tid - 32] = __ldg((const int*)next + (tid - 32));
+      ((int*)&sh.lay[next_slot])[tid - 32] = __ldg((const int*)next + (tid - 32));
+    if (prep >= 0 && tid == 64) prepare(prep, emb);
     ++barrier_gen;
     if (tid == 0) {
       // release-ordered arrival without waiting for a return value: this CTA's
@@ -667,13 +724,11 @@ struct Consumer {
   // MMA segment body: the CTA's (tile, block) items, round-robin over the warps
   // and in stage order; every warp arrives on each stage's empty barrier once,
   // after its last item there.  Block partials go to red [tiles][nT][NB][16].
-  __device__ bool seg_mma_body(const MegaSeg& s, int K, int r0, int r1, float*& red_out) {
-    const MGeo m = mgeo(s, K, slot_bytes);
-    const int nout = r1 - r0, ntiles = (nout + 15) / 16, nst = ntiles * m.nch;
-    const int red_n = ntiles * m.nT * m.NB * 16;
-    // red and the warp scratch: in the dead staging area when they fit, else after the planes
-    float* base = (red_n + CWARPS * WS <= K) ? part : part + ((mend + 3) & ~3);  // int2 scratch: 16 B aligned
-    if ((base - part) + red_n + CWARPS * WS > a.part_floats) {  // host sizing covers every phase
+  __device__ bool seg_mma_body(const MegaSeg& s, const SegPlan& PL, float*& red_out) {
+    const MGeo m = PL.mg;
+    const int nout = PL.r1 - PL.r0, nst = PL.nst, red_n = PL.red_n;
+    float* base = part + PL.red_off;
+    if (PL.red_off + red_n + CWARPS * WS > a.part_floats) {  // host sizing covers every phase
       if (tid == 0) atomicExch(a.status, SM_ERR_UNSUPPORTED);
       sh.abort = 1;
       return false;
@@ -684,8 +739,8 @@ struct Consumer {
     // walk the stages without divisions: stage st = (tile t, block chunk c) holds
     // per = nT * nkb items; this warp's items are warp, warp + CWARPS, ...
     int st = 0, t = 0, c = 0, nkb = min(m.nkbs, m.NB), per = m.nT * nkb, loc = warp;
-    int slot = k % a.nslots;
-    uint32_t par = (uint32_t)(k / a.nslots) & 1u;
+    int slot = PL.slot0;
+    uint32_t par = (uint32_t)PL.par0;
     bool waited = false;
     while (true) {
       while (st < nst && loc >= per) {
@@ -786,18 +841,18 @@ struct Consumer {
   }
 
   // GEMV rows of this CTA for one segment; `amax` (head only) tracks the local argmax.
-  __device__ bool seg(const MegaSeg& s, int K, int /*rb*/, float* amax_v = nullptr, int* amax_i = nullptr,
-                      int c0 = 0, int c1 = -1) {
-    const int rb = stage_rows(s, K, slot_bytes);
-    int r0, r1;
-    seg_rows_in(s.rows, blockIdx.x, c0, c1 < 0 ? (int)gridDim.x : c1, r0, r1);
+  __device__ bool seg(const SegPlan& PL) {
+    const MegaSeg& s = *PL.s;
+    const int K = PL.K, rb = PL.rb, r0 = PL.r0, r1 = PL.r1;
+    float* amax_v = PL.amax_v;
+    int* amax_i = PL.amax_i;
     const int nout = r1 - r0;
     const int64_t rbytes = row_bytes_fmt(s.fmt, K);
     const bool glu = s.mode == GEMV_GLU;
     const GemvSeg g = to_gemv(s);
-    const bool use_mma = mma_seg(a, s);
+    const bool use_mma = PL.mma;
     float* mred = nullptr;
-    const MGeo mg = mgeo(s, K, slot_bytes);
+    const MGeo mg = PL.mg;
     // the caller staged the vector for this segment's path (one staging call site
     // keeps the kernel small): a mismatch is a scheduling error
     if (use_mma ? mfmt != s.fmt : (mfmt != 0 || (s.fmt != SM_Q8_0) != pair)) {
@@ -808,7 +863,7 @@ struct Consumer {
     if (use_mma) {
       stamp();
       stamp();
-      if (!seg_mma_body(s, K, r0, r1, mred)) return false;
+      if (!seg_mma_body(s, PL, mred)) return false;
     } else {
     stamp();
     for (int row = r0; row < r1; row += rb) {
@@ -1199,7 +1254,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     rope_s[0][t] = a.sin_t[(int64_t)(len - 1) * half + t];
     rope_s[1][t] = a.cos_t[(int64_t)(len - 1) * half + t];
   }
-  if (tid < (int)(sizeof(MegaLayer) / 4)) ((int*)&sh.lay)[tid] = __ldg((const int*)&a.layers[0] + tid);
+  if (tid < (int)(sizeof(MegaLayer) / 4)) ((int*)&sh.lay[0])[tid] = __ldg((const int*)&a.layers[0] + tid);
   cons_sync();
   c.ep.pos = &pos_s;
   // epilogue reads table[pos * half + i]: point at the shared row shifted back by pos * half
@@ -1215,10 +1270,12 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   // one call site per kind of work keeps the kernel's code small: phase p is
   // layer p / 4, kind Q|K|V (attention follows), O, gate|up, down; the last
   // phase is the LM head
+  if (tid == 64) c.prepare(0, emb);
+  cons_sync();
   for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
     const int l = ph >> 2, kind = ph & 3;
     const bool head = l == a.n_layers;
-    const MegaLayer& L = sh.lay;
+    const MegaLayer& L = sh.lay[l & 1];
     if (kind == 1) {
       if (!c.grid_barrier()) return;
       for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
@@ -1227,24 +1284,16 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
       if (!c.grid_barrier()) return;
       c.attn_combine(chunks);
     }
-    // the layer's table entry comes on chip during the barrier before its Q|K|V
-    if (ph > 0 && !c.grid_barrier(kind == 0 && !head ? &a.layers[l] : nullptr)) return;
-    int s = 0, c0 = 0, c1 = -1;
-    if (kind == 0 && !head) {
-      s = blockIdx.x < L.qkv_cb[1] ? 0 : (blockIdx.x < L.qkv_cb[2] ? 1 : 2);
-      c0 = L.qkv_cb[s];
-      c1 = L.qkv_cb[s + 1];
+    // the barrier before a GEMV phase also plans it; the one before a layer's
+    // gate|up brings the next layer's table entry on chip
+    if (ph > 0) {
+      const bool nx = kind == 2 && l + 1 < a.n_layers;
+      if (!c.grid_barrier(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb)) return;
     }
-    const MegaSeg& sg = head ? a.head : (kind == 0 ? L.qkv[s] : (kind == 1 ? L.o : (kind == 2 ? L.gu : L.down)));
-    // RMSNorm (Q|K|V, gate|up, head) on the residual stream; O reads the attention output, down the GLU
-    const float* src = kind == 1 ? a.att : (kind == 3 ? a.act : (ph == 0 ? emb : a.x));
-    const float* gamma = head ? a.out_norm : (kind == 0 ? L.attn_norm : (kind == 2 ? L.ffn_norm : nullptr));
-    const int K = (kind == 1 && !head) ? a.qd : ((kind == 3 && !head) ? a.F : a.H);
-    const int rb = head ? a.stage_rows_v : (kind == 3 ? a.stage_rows_f : a.stage_rows_h);
-    c.load_x(src, gamma, K, sg.fmt != SM_Q8_0, mma_seg(a, sg) ? sg.fmt : 0);
+    const SegPlan& P = sh.plan;
+    c.load_x(P.src, P.gamma, P.K, P.s->fmt != SM_Q8_0, P.mma ? P.s->fmt : 0);
     if (tid == 0) sh.phase = ph;
-    if (!c.seg(sg, K, rb, head ? &a.amax_val[blockIdx.x] : nullptr, head ? &a.amax_idx[blockIdx.x] : nullptr, c0, c1))
-      return;
+    if (!c.seg(P)) return;
     if (kind == 0 && !head) {
       // this CTA's attention chunks of the layer: K / V rows into L2 while it waits at
       // the barrier (issued after the vector loads, which they would otherwise delay)
