@@ -320,10 +320,25 @@ struct Consumer {
   // `next`: a layer table entry to bring on chip into lay[next_slot]; `prep`: the
   // GEMV phase to plan (thread 64), both while thread 0 waits
   __device__ bool grid_barrier(const MegaLayer* next = nullptr, int next_slot = 0, int prep = -1,
-                               const float* emb = nullptr) {
+                               const float* emb = nullptr, const MegaLayer* kvl = nullptr, int chunks = 0,
+                               int len = 0) {
     // all consumer stores of this CTA are done before thread 0 arrives
     cons_sync();
     stamp();
+    // this CTA's attention chunks of the layer: K / V rows into L2 while thread 0
+    // waits (after the CTA barrier, so its arrival does not wait for them)
+    if (kvl && tid > 0) {
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
+        const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
+        const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
+        const int64_t off = ((int64_t)seq_v * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
+        const int lines = (j1 - j0) * 2;  // 256-byte rows
+        for (int t = tid - 1; t < 2 * lines; t += CT - 1) {
+          const float* base = (t < lines ? kvl->kc : kvl->vc) + off;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
+        }
+      }
+    }
     if (next && tid >= 32 && tid < 32 + (int)(sizeof(MegaLayer) / 4))
       ((int*)&sh.lay[next_slot])[tid - 32] = __ldg((const int*)next + (tid - 32));
     if (prep >= 0 && tid == 64) prepare(prep, emb);
@@ -852,6 +867,9 @@ struct Consumer {
     const GemvSeg g = to_gemv(s);
     const bool use_mma = PL.mma;
     float* mred = nullptr;
+    // ADD: this thread's residual row, read before the GEMV rather than after it
+    const bool addm = s.mode == GEMV_ADD;
+    const float resid = (addm && tid < nout) ? __ldcg(&s.y[r0 + tid]) : 0.f;
     const MGeo mg = PL.mg;
     // the caller staged the vector for this segment's path (one staging call site
     // keeps the kernel small): a mismatch is a scheduling error
@@ -939,7 +957,9 @@ struct Consumer {
         }
         v[q] = t;
       }
-      if (glu)
+      if (addm && it == tid)
+        s.y[r0 + it] = resid + v[0];
+      else if (glu)
         group_store<2>(ep, g, r0 + it, v);
       else if (pairs)
         group_store<2>(ep, g, (r0 >> 1) + it, v);
@@ -1274,10 +1294,9 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   cons_sync();
   for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
     const int l = ph >> 2, kind = ph & 3;
-    const bool head = l == a.n_layers;
     const MegaLayer& L = sh.lay[l & 1];
     if (kind == 1) {
-      if (!c.grid_barrier()) return;
+      if (!c.grid_barrier(nullptr, 0, -1, nullptr, &L, chunks, len)) return;
       for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
       if (!c.grid_barrier()) return;
       for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_pv(L, it / chunks, it % chunks, chunks, len);
@@ -1294,20 +1313,6 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     c.load_x(P.src, P.gamma, P.K, P.s->fmt != SM_Q8_0, P.mma ? P.s->fmt : 0);
     if (tid == 0) sh.phase = ph;
     if (!c.seg(P)) return;
-    if (kind == 0 && !head) {
-      // this CTA's attention chunks of the layer: K / V rows into L2 while it waits at
-      // the barrier (issued after the vector loads, which they would otherwise delay)
-      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
-        const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
-        const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
-        const int64_t off = ((int64_t)seqv * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
-        const int lines = (j1 - j0) * 2;  // 256-byte rows
-        for (int t = tid; t < 2 * lines; t += CT) {
-          const float* base = (t < lines ? L.kc : L.vc) + off;
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
-        }
-      }
-    }
   }
   c.stamp();
   // greedy argmax over the CTAs' partial maxima (lowest id on ties); the last CTA commits
