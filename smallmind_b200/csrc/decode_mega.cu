@@ -1024,12 +1024,19 @@ struct Consumer {
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
     float* qs = att_pp(per);  // [G][64]
     float* es = att_es();
-    for (int t = tid; t < G * HD / 4; t += CT) ((float4*)qs)[t] = __ldcg((const float4*)&a.q[g * G * HD] + t);
-    cons_sync();
     const int64_t seq = seq_v;
     const float* kb = L.kc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
     const int sub = tid & 7, slot = tid >> 3;  // 60 key slots
     constexpr int SLOTS = CT / 8;
+    // the first pass's key rows load together with the queries (one round trip)
+    float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), k1 = k0;
+    if (slot < n) {
+      const float4* kp = (const float4*)(kb + (int64_t)(j0 + slot) * HD + sub * 8);
+      k0 = __ldcg(kp);
+      k1 = __ldcg(kp + 1);
+    }
+    for (int t = tid; t < G * HD / 4; t += CT) ((float4*)qs)[t] = __ldcg((const float4*)&a.q[g * G * HD] + t);
+    cons_sync();
     float lmax[MGMAX];
 #pragma unroll
     for (int h = 0; h < MGMAX; ++h) lmax[h] = -FLT_MAX;
@@ -1037,16 +1044,15 @@ struct Consumer {
     for (int p = 0; p < (n + SLOTS - 1) / SLOTS; ++p) {
       const int jj = p * SLOTS + slot;
       const bool valid = jj < n;
-      float kv[8];
-      if (valid) {
-        const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * HD + sub * 8);
-        const float4 t0 = __ldcg(kp), t1 = __ldcg(kp + 1);
-        kv[0] = t0.x; kv[1] = t0.y; kv[2] = t0.z; kv[3] = t0.w;
-        kv[4] = t1.x; kv[5] = t1.y; kv[6] = t1.z; kv[7] = t1.w;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) kv[i] = 0.f;
+      if (p > 0) {
+        k0 = k1 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) {
+          const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * HD + sub * 8);
+          k0 = __ldcg(kp);
+          k1 = __ldcg(kp + 1);
+        }
       }
+      const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
       for (int h = 0; h < MGMAX; ++h) {
         if (h >= G) break;
@@ -1136,10 +1142,14 @@ struct Consumer {
       for (int p = 0; p < PH; ++p) s += pp[(p * MGMAX + h) * 64 + dd];
       a.pacc[(int64_t)(base + h) * 64 + dd] = s;
     }
-    if (tid < G) {
-      float s = 0.f;
-      for (int jj = 0; jj < n; ++jj) s += es[tid * per + jj];
-      a.psum[base + tid] = s;
+    {
+      const int w = tid >> 5, ln = tid & 31;
+      if (w < G) {
+        float s = 0.f;
+        for (int jj = ln; jj < n; jj += 32) s += es[w * per + jj];
+        s = warp_sum(s);
+        if (ln == 0) a.psum[base + w] = s;
+      }
     }
     cons_sync();
   }
