@@ -582,6 +582,7 @@ struct sm_kv {
   unsigned* mega_sync = nullptr;     // grid barrier / combine counters
   unsigned long long* mega_trace = nullptr;  // SMALLMIND_MEGA_TRACE: per-CTA phase timestamps
   int mega_generation = -1;
+  bool mega_mma_only = false;  // every segment of the layer table has the tensor-core path
   size_t layer_stride() const { return (size_t)max_seqs * m->cfg.n_kv_heads * max_tokens * m->cfg.head_dim; }
 };
 
@@ -895,12 +896,17 @@ int mega_args(sm_model* m, sm_kv* kv, MegaArgs& a) {
       t.vc = vc;
       mega_layer_split(t, c.hidden, grid);
     }
+    kv->mega_mma_only = mega_seg_mma_ok(mega_seg(*m->output, nullptr, GEMV_STORE, w.logits));
+    for (const MegaLayer& t : hl)
+      for (const MegaSeg* sg : {&t.qkv[0], &t.qkv[1], &t.qkv[2], &t.o, &t.gu, &t.down})
+        kv->mega_mma_only = kv->mega_mma_only && mega_seg_mma_ok(*sg);
     if (!kv->mega_layers) SM_CUDA_TRY(cudaMalloc(&kv->mega_layers, sizeof(MegaLayer) * c.n_layers));
     if (!kv->mega_sync) SM_CUDA_TRY(cudaMalloc(&kv->mega_sync, 64 * sizeof(unsigned)));
     SM_CUDA_TRY(cudaMemcpy(kv->mega_layers, hl.data(), sizeof(MegaLayer) * c.n_layers, cudaMemcpyHostToDevice));
     kv->mega_generation = w.generation;
   }
   a.layers = kv->mega_layers;
+  a.mma_only = kv->mega_mma_only ? 1 : 0;
   a.head = mega_seg(*m->output, nullptr, GEMV_STORE, w.logits);
   if (!mega_seg_supported(a.head)) return SM_ERR_UNSUPPORTED;
   for (const auto& L : m->layers)

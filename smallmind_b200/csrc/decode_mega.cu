@@ -234,6 +234,9 @@ struct Producer {
 };
 
 // ---------------------------------------------------------------- consumers
+// AM: every GEMV segment runs on the tensor-core path (the dp4a path is not compiled in,
+// which keeps the kernel's code small)
+template <bool AM>
 struct Consumer {
   const MegaArgs& a;
   Shared& sh;
@@ -395,7 +398,7 @@ struct Consumer {
     // 16-byte chunk c of unit w is stored at chunk (c + w) % 8 of that unit, so the
     // 8 lanes of a quarter-warp reading chunk c of 8 consecutive units hit 8
     // different bank groups.
-    if (mma) {
+    if (AM || mma) {
       // the tensor-core path needs no staged copy: each lane reads its own elements
       build_mma_planes(src, K, gamma, mma, lxe);
       return;
@@ -533,37 +536,33 @@ struct Consumer {
         su += y[i] + y[i + 1];
       }
       am = warp_max(am);  // the warp's 8 units are one block
-      int ex = 0;
-      frexpf(am, &ex);  // am < 2^ex
-      uint32_t pw[2][3] = {};
-      auto digits = [&](int X, int h, int byte) {
-        const int c = ((X + 128) & 255) - 128;
-        const int X1 = (X - c) >> 8;
-        const int b = ((X1 + 128) & 255) - 128;
-        const int hi = (X1 - b) >> 8;
-        pw[h][0] |= (uint32_t)(hi & 255) << (8 * byte);
-        pw[h][1] |= (uint32_t)(b & 255) << (8 * byte);
-        pw[h][2] |= (uint32_t)(c & 255) << (8 * byte);
-      };
+      const int ex = block_exp(am);  // am < 2^ex
+      uint32_t pw[2][3];  // [low / high positions][digit hi, b, c]
       if (fmt == SM_Q4_K) {
-        const float up = ldexpf(1.f, 21 - ex), uph = ldexpf(1.f, 17 - ex);
+        const float up = pow2i(21 - ex), uph = pow2i(17 - ex);
+        int X[2][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int L = am > 0.f ? __float2int_rn(y[2 * i] * up) : 0;
-          const int H = am > 0.f ? __float2int_rn(y[2 * i + 1] * uph) : 0;
-          digits(L - H, 0, i);
-          digits(H, 1, i);
+          const int L = __float2int_rn(y[2 * i] * up);
+          const int H = __float2int_rn(y[2 * i + 1] * uph);
+          X[0][i] = L - H;
+          X[1][i] = H;
         }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) digits4(X[h][0], X[h][1], X[h][2], X[h][3], pw[h][0], pw[h][1], pw[h][2]);
 #pragma unroll
         for (int q = 0; q < 3; ++q) mp[(uu * 3 + q) * 4 + pp] = make_uint2(pw[0][q], pw[1][q]);
         su += __shfl_xor_sync(0xffffffffu, su, 1);
         su += __shfl_xor_sync(0xffffffffu, su, 2);
         if (pp == 0) sx[uu] = su;
-        if (lane == 0) bx[uu >> 3] = ldexpf(1.f, ex - 21);
+        if (lane == 0) bx[uu >> 3] = pow2i(ex - 21);
       } else {
-        const float up = ldexpf(1.f, 22 - ex);
+        const float up = pow2i(22 - ex);
+        int X[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) digits(am > 0.f ? __float2int_rn(y[i] * up) : 0, i & 1, i >> 1);
+        for (int i = 0; i < 8; ++i) X[i] = __float2int_rn(y[i] * up);
+        digits4(X[0], X[2], X[4], X[6], pw[0][0], pw[0][1], pw[0][2]);  // even elements
+        digits4(X[1], X[3], X[5], X[7], pw[1][0], pw[1][1], pw[1][2]);  // odd elements
         const int half = pp >> 1;
 #pragma unroll
         for (int col = 0; col < 6; ++col)
@@ -571,7 +570,7 @@ struct Consumer {
               (col / 3) == half ? make_uint2(pw[0][col % 3], pw[1][col % 3]) : make_uint2(0u, 0u);
         su += __shfl_xor_sync(0xffffffffu, su, 1);
         if ((pp & 1) == 0) sx[uu * 2 + half] = su;
-        if (lane == 0) bx[uu >> 3] = ldexpf(1.f, ex - 22);
+        if (lane == 0) bx[uu >> 3] = pow2i(ex - 22);
       }
     }
     if (gamma) {
@@ -873,12 +872,12 @@ struct Consumer {
     const MGeo mg = PL.mg;
     // the caller staged the vector for this segment's path (one staging call site
     // keeps the kernel small): a mismatch is a scheduling error
-    if (use_mma ? mfmt != s.fmt : (mfmt != 0 || (s.fmt != SM_Q8_0) != pair)) {
+    if ((AM && !use_mma) || (use_mma ? mfmt != s.fmt : (mfmt != 0 || (s.fmt != SM_Q8_0) != pair))) {
       if (tid == 0) atomicExch(a.status, SM_ERR_UNSUPPORTED);
       sh.abort = 1;
       return false;
     }
-    if (use_mma) {
+    if (AM || use_mma) {
       stamp();
       stamp();
       if (!seg_mma_body(s, PL, mred)) return false;
@@ -1210,6 +1209,7 @@ struct Consumer {
   }
 };
 
+template <bool AM>
 __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constant__ MegaArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Shared& sh = *(Shared*)smem_raw;
@@ -1267,7 +1267,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     return;
   }
   // -------------------------------------------------------------- consumers
-  Consumer c{a, sh, ring, slot_bytes, part};
+  Consumer<AM> c{a, sh, ring, slot_bytes, part};
   c.tid = tid;
   c.seq_v = seqv;
   c.ep.pos = nullptr;
@@ -1398,6 +1398,10 @@ void mega_layer_split(MegaLayer& L, int K, int grid) {
   cb[3] = grid;
 }
 
+bool mega_seg_mma_ok(const MegaSeg& s) {
+  return s.fmt == SM_Q4_K || (s.fmt == SM_Q6_K && s.aux_stride > 0 && (s.aux_stride * 2) % 16 == 0);
+}
+
 bool mega_seg_supported(const MegaSeg& s) {
   if (s.fmt == SM_Q4_K) return true;
   return (s.fmt == SM_Q6_K || s.fmt == SM_Q8_0 || s.fmt == SM_Q4_0) && s.aux_stride > 0;
@@ -1460,7 +1464,8 @@ int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    SM_CUDA_TRY(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_total));
+    SM_CUDA_TRY(cudaFuncSetAttribute(decode_mega_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_total));
+    SM_CUDA_TRY(cudaFuncSetAttribute(decode_mega_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_total));
     attr_set[dev] = true;
   }
   SM_CUDA_TRY(cudaMemsetAsync(a.sync, 0, 64 * sizeof(unsigned), st));
@@ -1474,7 +1479,10 @@ int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_mega_kernel, a));
+  if (a.use_mma && a.mma_only)
+    SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_mega_kernel<true>, a));
+  else
+    SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_mega_kernel<false>, a));
   if (n_launch) *n_launch += 1;
   return SM_OK;
 }

@@ -61,6 +61,7 @@ struct MegaArgs {
   int nslots = 0, ring_offset = 0, part_floats = 0, smem_bytes = 0;
   int stage_rows_h = 1, stage_rows_f = 1, stage_rows_v = 1;
   int use_mma = 1;    // Q4_K / Q6_K phases on the int8 tensor-core path
+  int mma_only = 0;   // every GEMV segment can take that path (mega_seg_mma_ok): the kernel without the dp4a path runs
   int lookahead = 1;  // 0: the producer only issues a phase's stages once the consumers entered it  // stage rows for K = H / qd, K = F, LM head
 };
 
@@ -71,6 +72,8 @@ size_t mega_scratch_floats(int nH, int nKv, int hd, int max_ctx, int grid);
 bool mega_supported(const MegaArgs& a);
 // Q|K|V CTA ranges of a layer for a grid of `grid` CTAs, in proportion to each segment's bytes
 void mega_layer_split(MegaLayer& L, int K, int grid);
+// the segment's format has the int8 tensor-core path (Q4_K; Q6_K with a 16-byte multiple d row)
+bool mega_seg_mma_ok(const MegaSeg& s);
 bool mega_seg_supported(const MegaSeg& s);
 int launch_decode_mega(MegaArgs& a, cudaStream_t st, int* n_launch);
 int mega_grid_size();
