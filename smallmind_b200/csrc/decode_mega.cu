@@ -1123,6 +1123,8 @@ struct Consumer {
       float acc[MGMAX];
 #pragma unroll
       for (int h = 0; h < MGMAX; ++h) acc[h] = 0.f;
+      // unrolled so the shared-memory loads of several keys are in flight together
+#pragma unroll 4
       for (int jj = kp; jj < n; jj += PH) {
         const float v = vs[jj * HD + d];
 #pragma unroll
