@@ -310,11 +310,13 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(
 // (the Pade exp of the reference is not multiplicative), and the partial sums
 // and e.V accumulators are reduced into CTA rank 0 the same way.  No global
 // scratch, one launch.
-constexpr int CL = 16;          // CTAs per cluster (non-portable size)
+// CL CTAs per cluster (1..16; 16 is a non-portable size): many CTAs per
+// sequence for long contexts at small batch, one CTA per (sequence, kv head)
+// when the batch alone fills the GPU.
 constexpr int CT = 256;         // threads per CTA
 constexpr int CMAXG = 8;        // q heads per kv head
 
-template <int HD>
+template <int HD, int CL>
 __global__ void __launch_bounds__(CT) decode_cluster_kernel(
     const float* __restrict__ q, int q_stride, const float* __restrict__ kc, const float* __restrict__ vc,
     int64_t seq_stride, int64_t row_stride, int64_t head_stride, const int* __restrict__ lens,
@@ -416,6 +418,7 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
   float acc[CMAXG];
 #pragma unroll
   for (int h = 0; h < CMAXG; ++h) acc[h] = 0.f;
+#pragma unroll 4
   for (int jj = ph; jj < n; jj += PH) {
     const float v = __ldg(vb + (int64_t)(j0 + jj) * row_stride + d);
 #pragma unroll
@@ -432,10 +435,15 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
     for (int p = 0; p < PH; ++p) s += part[(p * CMAXG + h) * HD + dd];
     pacc[h * HD + dd] = s;
   }
-  if (threadIdx.x < G) {
-    float s = 0.f;
-    for (int jj = 0; jj < n; ++jj) s += sc[threadIdx.x * chunk_cap + jj];
-    stat[CMAXG + threadIdx.x] = s;
+  {
+    // slice sum of each head: warp h over the slice, then a warp sum
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    for (int h = w; h < G; h += CT / 32) {
+      float s = 0.f;
+      for (int jj = ln; jj < n; jj += 32) s += sc[h * chunk_cap + jj];
+      s = warp_sum(s);
+      if (ln == 0) stat[CMAXG + h] = s;
+    }
   }
   cluster.sync();
   // rank 0 reduces the slices and writes out = (sum e.V) / (sum e)
@@ -487,66 +495,100 @@ int launch_attention_decode(const float* q, int q_stride, const float* kc, const
 
 // Single-launch cluster variant (no scratch).  Returns SM_ERR_UNSUPPORTED when
 // the shape does not fit it (caller falls back to launch_attention_decode).
+namespace {
+
+template <int CL>
+int launch_decode_cluster_cl(const float* q, int q_stride, const float* kc, const float* vc, int64_t seq_stride,
+                             int64_t row_stride, int64_t head_stride, int max_ctx, float* out, int out_stride,
+                             const int* lens, const int* seq_map, int B, int nH, int nKv, int hd, cudaStream_t st,
+                             int* n_launch) {
+  const int chunk_cap = (max_ctx + CL - 1) / CL;
+  const size_t smem = sizeof(float) * (CMAXG * 64 * 2 + CMAXG * (size_t)chunk_cap + 2 * CMAXG + (CT / 64) * CMAXG * 64);
+  if (smem > 200 * 1024 / 4) return SM_ERR_UNSUPPORTED;
+  auto kern = decode_cluster_kernel<64, CL>;
+  static bool attr_set[64] = {};
+  static int cluster_ok[64] = {};  // 0 unknown, 1 usable, -1 not schedulable on this device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return SM_ERR_UNSUPPORTED;
+  if (!attr_set[dev]) {
+    if (CL > 8) SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set[dev] = true;
+  }
+  if (cluster_ok[dev] == 0) {
+    cudaLaunchConfig_t probe = {};
+    probe.gridDim = dim3(CL, 1, 1);
+    probe.blockDim = dim3(CT);
+    probe.dynamicSmemBytes = 200 * 1024 / 4;
+    cudaLaunchAttribute pa[1];
+    pa[0].id = cudaLaunchAttributeClusterDimension;
+    pa[0].val.clusterDim.x = CL;
+    pa[0].val.clusterDim.y = 1;
+    pa[0].val.clusterDim.z = 1;
+    probe.attrs = pa;
+    probe.numAttrs = 1;
+    int nclusters = 0;
+    cudaError_t oe = cudaOccupancyMaxActiveClusters(&nclusters, (void*)kern, &probe);
+    cluster_ok[dev] = (oe == cudaSuccess && nclusters > 0) ? 1 : -1;
+    if (oe != cudaSuccess) cudaGetLastError();
+  }
+  if (cluster_ok[dev] < 0) return SM_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, nKv, B);
+  cfg.blockDim = dim3(CT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const float scale = 1.0f / sqrtf((float)hd);
+  SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, q_stride, kc, vc, seq_stride, row_stride, head_stride, lens,
+                                 seq_map, nH, nKv, scale, out, out_stride, chunk_cap));
+  if (n_launch) *n_launch += 1;
+  return SM_OK;
+}
+
+}  // namespace
+
+// Single-launch cluster variant (no scratch).  Returns SM_ERR_UNSUPPORTED when
+// the shape does not fit it (caller falls back to launch_attention_decode).
+// Cluster size: as many CTAs per (sequence, kv head) as keep about two waves of
+// CTAs on the GPU (16 for one sequence, 1 once the batch fills the SMs), and at
+// least as many as the context's score rows need to fit shared memory.
 int launch_attention_decode_cluster(const float* q, int q_stride, const float* kc, const float* vc,
                                     int64_t seq_stride, int64_t row_stride, int64_t head_stride, int max_ctx,
                                     float* out, int out_stride, const int* lens, const int* seq_map, int B, int nH,
                                     int nKv, int hd, cudaStream_t st, int* n_launch) {
-  if (hd != 64 || nH % nKv) return SM_ERR_UNSUPPORTED;
-  if (nH / nKv <= CMAXG) {
-    const int chunk_cap = (max_ctx + CL - 1) / CL;
-    const size_t smem = sizeof(float) * (CMAXG * 64 * 2 + CMAXG * (size_t)chunk_cap + 2 * CMAXG + (CT / 64) * CMAXG * 64);
-    if (smem <= 200 * 1024) {
-      auto kern = decode_cluster_kernel<64>;
-      static bool attr_set[64] = {};
-      int dev = 0;
-      cudaGetDevice(&dev);
-      static int cluster_ok[64] = {};  // 0 unknown, 1 usable, -1 not schedulable on this device
-      if (dev < 64 && !attr_set[dev]) {
-        SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        SM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set[dev] = true;
-      }
-      if (dev >= 64) return SM_ERR_UNSUPPORTED;
-      if (cluster_ok[dev] == 0) {
-        cudaLaunchConfig_t probe = {};
-        probe.gridDim = dim3(CL, 1, 1);
-        probe.blockDim = dim3(CT);
-        probe.dynamicSmemBytes = 200 * 1024 / 4;
-        cudaLaunchAttribute pa[1];
-        pa[0].id = cudaLaunchAttributeClusterDimension;
-        pa[0].val.clusterDim.x = CL;
-        pa[0].val.clusterDim.y = 1;
-        pa[0].val.clusterDim.z = 1;
-        probe.attrs = pa;
-        probe.numAttrs = 1;
-        int nclusters = 0;
-        cudaError_t oe = cudaOccupancyMaxActiveClusters(&nclusters, (void*)kern, &probe);
-        cluster_ok[dev] = (oe == cudaSuccess && nclusters > 0) ? 1 : -1;
-        if (oe != cudaSuccess) cudaGetLastError();
-      }
-      if (cluster_ok[dev] < 0 || smem > 200 * 1024 / 4) return SM_ERR_UNSUPPORTED;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(CL, nKv, B);
-      cfg.blockDim = dim3(CT);
-      cfg.dynamicSmemBytes = smem;
-      cfg.stream = st;
-      cudaLaunchAttribute attr[2];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = CL;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[1].val.programmaticStreamSerializationAllowed = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 2;
-      const float scale = 1.0f / sqrtf((float)hd);
-      SM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, q_stride, kc, vc, seq_stride, row_stride, head_stride, lens,
-                                     seq_map, nH, nKv, scale, out, out_stride, chunk_cap));
-      if (n_launch) *n_launch += 1;
-      return SM_OK;
-    }
+  if (hd != 64 || nH % nKv || nH / nKv > CMAXG) return SM_ERR_UNSUPPORTED;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int cl = 16;
+  while (cl > 1 && (int64_t)cl * nKv * B > 2 * sms) cl >>= 1;
+  auto fits = [&](int c) {
+    const int64_t cap = (max_ctx + c - 1) / c;
+    return sizeof(float) * (CMAXG * 64 * 2 + CMAXG * cap + 2 * CMAXG + (CT / 64) * CMAXG * 64) <= 200 * 1024 / 4;
+  };
+  while (cl < 16 && !fits(cl)) cl <<= 1;
+  switch (cl) {
+    case 1: return launch_decode_cluster_cl<1>(q, q_stride, kc, vc, seq_stride, row_stride, head_stride, max_ctx, out,
+                                               out_stride, lens, seq_map, B, nH, nKv, hd, st, n_launch);
+    case 2: return launch_decode_cluster_cl<2>(q, q_stride, kc, vc, seq_stride, row_stride, head_stride, max_ctx, out,
+                                               out_stride, lens, seq_map, B, nH, nKv, hd, st, n_launch);
+    case 4: return launch_decode_cluster_cl<4>(q, q_stride, kc, vc, seq_stride, row_stride, head_stride, max_ctx, out,
+                                               out_stride, lens, seq_map, B, nH, nKv, hd, st, n_launch);
+    case 8: return launch_decode_cluster_cl<8>(q, q_stride, kc, vc, seq_stride, row_stride, head_stride, max_ctx, out,
+                                               out_stride, lens, seq_map, B, nH, nKv, hd, st, n_launch);
+    default: return launch_decode_cluster_cl<16>(q, q_stride, kc, vc, seq_stride, row_stride, head_stride, max_ctx,
+                                                 out, out_stride, lens, seq_map, B, nH, nKv, hd, st, n_launch);
   }
-  return SM_ERR_UNSUPPORTED;
 }
 
 int launch_attention_prefill(const float* q, int q_stride, const float* k, const float* v, int64_t row_stride,
