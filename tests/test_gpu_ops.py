@@ -55,6 +55,37 @@ def test_attention_prefill(ctx, O, T, S, nH, nKv):
     assert rel_err(out, ref) < 1e-4
 
 
+@pytest.mark.parametrize("B", [8, 32, 64])
+def test_attention_decode_batch_cluster_sizes(ctx, O, B):
+    """Batches that select 8, 2 and 1 CTAs per (sequence, kv head), short ragged contexts."""
+    import torch
+
+    import smallmind_b200 as sm
+    nH, nKv, hd, max_ctx = 32, 4, 64, 256
+    rs = np.random.RandomState(B)
+    lens = rs.randint(1, max_ctx + 1, B).astype(np.int32)
+    lens[0] = 1
+    lens[-1] = max_ctx
+    kc = rs.randn(B, nKv, max_ctx, hd).astype(np.float32)
+    vc = rs.randn(B, nKv, max_ctx, hd).astype(np.float32)
+    q = rs.randn(B, nH * hd).astype(np.float32)
+    dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, kc, vc))
+    dl = torch.from_numpy(lens).cuda()
+    out = torch.empty(B, nH * hd, device="cuda")
+    torch.cuda.synchronize()
+    rc = sm.lib().sm_attention_decode(ctx.handle, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), out.data_ptr(),
+                                      dl.data_ptr(), B, max_ctx, nH, nKv, hd)
+    assert rc == 0, sm.last_error()
+    ctx.sync()
+    got = out.cpu().numpy()
+    for b in range(B):
+        L = int(lens[b])
+        kk = np.ascontiguousarray(kc[b, :, :L].transpose(1, 0, 2).reshape(L, nKv * hd))
+        vv = np.ascontiguousarray(vc[b, :, :L].transpose(1, 0, 2).reshape(L, nKv * hd))
+        ref = O.attention(q[b:b + 1], kk, vv, 1, L, nH, nKv, hd)
+        assert rel_err(got[b:b + 1], ref) < 1e-4, b
+
+
 def test_attention_decode_ragged_batch(ctx, O):
     """16 sequences, lengths U[256, 2048], head-major cache."""
     import torch
