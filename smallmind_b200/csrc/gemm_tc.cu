@@ -457,27 +457,54 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
     const bool ok = mbar_wait_bounded(done, 0, a.status);
     tc_fence_after();
     if (ok) {
-      const int m = m0 + warp * 32 + lane;
       const bool part = a.kslices > 1;
       int sg = 0;
       while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
       const int nb = a.seg_n0[sg], ne = a.seg_n0[sg + 1];
       // partial sums: [slice][M][N total]; final: the segment's own output, column n - nb
-      float* yr = part ? a.partial + ((int64_t)blockIdx.z * a.M + m) * a.N
-                       : a.seg_y[sg] + (int64_t)m * a.seg_ldy[sg] - nb;
+      // The accumulator rows go through shared memory (the stage buffers are free
+      // once `done` has fired) so that each store instruction writes one whole
+      // 512-byte output row: lane = 4 consecutive columns, not lane = row.
+      // Row stride 132 floats: the 8 rows of a quarter-warp's 16-byte writes
+      // land in distinct bank groups.
+      constexpr int SR = BN + 4;
+      float* stile = (float*)smem + warp * 32 * SR;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-        if (m < a.M) {
+        float4* d = (float4*)(stile + lane * SR + c0);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int n = n0 + c0 + e;
-            if (n < ne) {
-              const float r = __uint_as_float(v[e]);
-              yr[n] = (a.accumulate && !part) ? yr[n] + r : r;
-            }
+        for (int e = 0; e < 4; ++e)
+          d[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]), __uint_as_float(v[4 * e + 2]),
+                             __uint_as_float(v[4 * e + 3]));
+      }
+      __syncwarp();
+      const bool rmw = a.accumulate && !part;
+      const int nc = n0 + 4 * lane;  // this lane's 4 columns
+      const bool full = nc + 3 < ne;
+#pragma unroll 1
+      for (int rr = 0; rr < 32; ++rr) {
+        const int mr = m0 + warp * 32 + rr;
+        if (mr >= a.M) break;
+        float* yrow = part ? a.partial + ((int64_t)blockIdx.z * a.M + mr) * a.N
+                           : a.seg_y[sg] + (int64_t)mr * a.seg_ldy[sg] - nb;
+        float4 t = *(const float4*)(stile + rr * SR + 4 * lane);
+        float* dst = yrow + nc;
+        if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+          if (rmw) {
+            const float4 o = *(const float4*)dst;
+            t.x += o.x;
+            t.y += o.y;
+            t.z += o.z;
+            t.w += o.w;
           }
+          *(float4*)dst = t;
+        } else {
+          const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (nc + e < ne) dst[e] = rmw ? dst[e] + tv[e] : tv[e];
         }
       }
     }
