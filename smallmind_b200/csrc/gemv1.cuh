@@ -69,6 +69,9 @@ int launch_gemv_mma_q6k_rows(const DevWeight& W, const float* x, int M, float* y
 int launch_gemv_mma_q6k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
                         int* n_launch);
 // Q4_K (INTENDED) y = W x on the int8 tensor-core path (mma.sync m16n8k32)
+// Q8_0 / Q4_0, M = 1, on the int8 tensor cores (gemv_mma_q8.cu); SM_ERR_UNSUPPORTED when the shape does not fit
+int launch_gemv_mma_q80(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
+                        int* n_launch);
 int launch_gemv_mma_q4k(const DevWeight& W, const float* x, float* y, int accumulate, int* status, cudaStream_t st,
                         int* n_launch);
 

@@ -164,3 +164,18 @@ def test_full_size_sweep_against_device_dequant(ctx, O, scheme, kn):
         ref = (a.double() @ deq.view(N, K).double().T)
         assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= TOL
     sm.lib().sm_weight_destroy(h)
+
+
+@pytest.mark.parametrize("scheme", ["Q8_0", "Q4_0"])
+@pytest.mark.parametrize("bs,k,n", [(64, 2304, 37), (32, 256, 16), (128, 1024, 300)])
+def test_gemv_m1_block_sizes_vs_oracle(ctx, O, scheme, bs, k, n):
+    """M = 1 (the int8 tensor-core GEMV for Q8_0 / Q4_0) at scale blocks of 32, 64 and 128."""
+    import smallmind_b200 as sm
+    sch = getattr(O, scheme)
+    t = O.quantize(O.fill_normal(n * k, 91, 0.02), sch, n, k, bs)
+    a = np.random.RandomState(bs).randn(1, k).astype(np.float32)
+    ref = O.matmul(t, a, 1, k, n, mode=1)
+    w = sm.CudaWeightTensor.from_qtensor(ctx, t)
+    out = np.empty((1, n), np.float32)
+    w.MatMul(a, out, 1, k, n)
+    assert rel_err(out, ref) <= TOL
