@@ -35,6 +35,9 @@ sys.path.insert(0, ROOT)
 TINYLLAMA = dict(vocab_size=32000, hidden=2048, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64,
                  ffn_hidden=5632, max_context=2048 + 512, norm_eps=1e-5, rope_theta=10000.0)
 PROMPT = 2048
+# SmolLM-135M-shaped LLaMA, every linear Q8_0 (the reference quantizer's default block 64)
+SMOLLM = dict(vocab_size=49152, hidden=576, n_layers=30, n_heads=9, n_kv_heads=3, head_dim=64, ffn_hidden=1536,
+              max_context=128 + 128 + 16, norm_eps=1e-5, rope_theta=10000.0)
 SCHEMES = dict(wq="Q4_K", wk="Q4_K", wv="Q6_K", wo="Q4_K", w_gate="Q4_K", w_up="Q4_K", w_down="Q6_K", output="Q6_K")
 METRIC = "decode tok/s (bs1, bs64) + Q4_K GEMV HBM GB/s vs peak; prefill tok/s"
 BYTES = {"Q4_K": 144 / 256, "Q6_K": 210 / 256, "Q8_0": 1.0 + 4 / 32, "Q4_0": 0.5 + 4 / 32}
@@ -120,7 +123,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- model build on the GPU
-def build_gpu_model(sm, ctx, cfg, seed=1234):
+def build_gpu_model(sm, ctx, cfg, seed=1234, schemes=None, block_size=32):
     import ctypes as C
 
     import torch
@@ -131,19 +134,20 @@ def build_gpu_model(sm, ctx, cfg, seed=1234):
     weights = {}
 
     def make(name, rows, cols):
-        sch = int(getattr(sm.QuantScheme, SCHEMES[name]))
+        sch = int(getattr(sm.QuantScheme, (schemes or SCHEMES)[name]))
         n = rows * cols
         src = torch.randn(n, generator=gen, device="cuda") * 0.02
         nbytes = {6: n // 256 * 144, 7: n // 256 * 210, 2: n, 3: n // 2}[sch]
         data = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-        scales = torch.empty(max(1, n // 32), dtype=torch.float32, device="cuda")
+        bs = block_size
+        scales = torch.empty(max(1, n // bs), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()
-        L.check(lib.sm_quantize(ctx.handle, sch, src.data_ptr(), n, 32, data.data_ptr(), scales.data_ptr()),
+        L.check(lib.sm_quantize(ctx.handle, sch, src.data_ptr(), n, bs, data.data_ptr(), scales.data_ptr()),
                 "quantize")
         h = C.c_void_p()
-        L.check(lib.sm_weight_upload_device(ctx.handle, sch, rows, cols, 32, data.data_ptr(), nbytes,
+        L.check(lib.sm_weight_upload_device(ctx.handle, sch, rows, cols, bs, data.data_ptr(), nbytes,
                                             scales.data_ptr() if sch in (2, 3) else None,
-                                            n // 32 if sch in (2, 3) else 0, L.LAYOUT_INTENDED, C.byref(h)),
+                                            n // bs if sch in (2, 3) else 0, L.LAYOUT_INTENDED, C.byref(h)),
                 "upload")
         w = sm.CudaWeightTensor.__new__(sm.CudaWeightTensor)
         w.ctx, w.handle, w._rows, w._cols = ctx, h, rows, cols
@@ -492,6 +496,24 @@ def run_ours(args):
     bs64_tps = bs * n64 / (e0.elapsed_time(e1) / 1000.0)
     kv3.close()
 
+    # SmolLM-135M-shaped Q8_0, 128-token prompt, 128 greedy bs1 decode steps
+    smol = dict(SMOLLM)
+    model_s, _ = build_gpu_model(sm, ctx, smol, seed=77, schemes={k: "Q8_0" for k in SCHEMES}, block_size=64)
+    kv4 = sm.KVCache(model_s, 1, smol["max_context"])
+    kv4.prefill(0, rs.randint(0, smol["vocab_size"], 128).astype(np.int32), want_logits=False)
+    tok_s = torch.tensor([1], dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        kv4.decode_device(seq.data_ptr(), tok_s.data_ptr(), 1, None, tok_s.data_ptr())
+    stream.synchronize()
+    e0.record(stream)
+    for _ in range(125):
+        kv4.decode_device(seq.data_ptr(), tok_s.data_ptr(), 1, None, tok_s.data_ptr())
+    e1.record(stream)
+    e1.synchronize()
+    smol_tps = 125 / (e0.elapsed_time(e1) / 1000.0)
+    kv4.close()
+    model_s.close()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         steps = 20
@@ -528,6 +550,7 @@ def run_ours(args):
                      "q6k_gbs": round(d_bytes / (d_ms * 1e-3) / 1e9, 1)},
             "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
             "bs64_decode_tok_s": round(bs64_tps, 1),
+            "smollm_q8_bs1_decode_tok_s": round(smol_tps, 1),
             "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
             "gpu_launches": int(launches_timed),
             "clocks": clk,
