@@ -159,3 +159,21 @@ def test_batched_decode_20_sequences(ctx, O):
         ref = O.model_forward(host, np.array(hist[s], np.int32), 1)[0]
         assert cosine(lg[s], ref) >= 0.9999
         assert int(toks[s]) == int(np.argmax(ref))
+
+
+def test_q8_model_hidden_576_bs1_decode_matches_oracle(ctx, O):
+    """SmolLM-shaped widths (hidden 576 = 18 units, 9 q / 3 kv heads), bs1 greedy decode."""
+    import smallmind_b200 as sm
+    cfg = dict(TINY, hidden=576, n_heads=9, n_kv_heads=3, ffn_hidden=1536, vocab_size=400, max_context=40)
+    schemes = {k: O.Q8_0 for k in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "output")}
+    host = O.make_model(cfg, schemes, seed=21, block_size=64)
+    model = sm.CudaModel.from_host(ctx, host)
+    kv = sm.KVCache(model, 1, 40)
+    prompt = np.random.RandomState(4).randint(0, cfg["vocab_size"], 11).astype(np.int32)
+    toks, logits = sm.InferenceSession(kv).generate(prompt, 5, return_logits=True)
+    hist = list(prompt)
+    for step, lg in enumerate(logits):
+        ref = O.model_forward(host, np.array(hist, np.int32), 1)[0]
+        assert cosine(lg, ref) >= 0.9999, step
+        assert toks[step] == int(np.argmax(ref)), step
+        hist.append(toks[step])
