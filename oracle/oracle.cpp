@@ -4,6 +4,7 @@
 #include "oracle.h"
 
 #include <algorithm>
+#include <limits>
 #include <cmath>
 #include <cstring>
 #include <thread>
@@ -288,6 +289,89 @@ void or_q4_dequantize(const uint8_t* data, const float* scales, int64_t n, int b
   }
 }
 
+// Q4_1Tensor.cs:47-112 (block 32 fixed): per block min and max, scale =
+// range > 0 ? range/15f : 1f, q = (int)round_half_even(clamp((x - min) * (1/scale), 0, 15)),
+// nibbles packed by global index (even -> low).  Scales and mins are two arrays.
+int or_q41_quantize(const float* src, int64_t n, uint8_t* data, float* scales, float* mins) {
+  if (n <= 0) return -1;
+  const int bs = 32;
+  const int64_t nb = (n + bs - 1) / bs;
+  for (int64_t b = 0; b < nb; ++b) {
+    const int64_t s = b * bs, e = std::min<int64_t>(s + bs, n);
+    float lo = std::numeric_limits<float>::max(), hi = std::numeric_limits<float>::lowest();
+    for (int64_t i = s; i < e; ++i) {
+      if (src[i] < lo) lo = src[i];
+      if (src[i] > hi) hi = src[i];
+    }
+    const float range = hi - lo;
+    const float scale = range > 0.f ? range / 15.f : 1.f;
+    scales[b] = scale;
+    mins[b] = lo;
+    const float inv = 1.f / scale;
+    for (int64_t i = s; i < e; ++i) {
+      const float nv = (src[i] - lo) * inv;
+      const int c = (int)round_half_even(clampf(nv, 0.f, 15.f));
+      const int64_t bi = i / 2;
+      if (i % 2 == 0)
+        data[bi] = (uint8_t)(c & 0xF);
+      else
+        data[bi] = (uint8_t)((data[bi] & 0x0F) | ((c & 0xF) << 4));
+    }
+  }
+  return 0;
+}
+
+// Q4_1Tensor.cs:129-160: w = q * scale + min (q the unsigned nibble).
+void or_q41_dequantize(const uint8_t* data, const float* scales, const float* mins, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    const uint8_t p = data[i / 2];
+    const int q = (i % 2 == 0) ? (p & 0xF) : ((p >> 4) & 0xF);
+    out[i] = (float)q * scales[i / 32] + mins[i / 32];
+  }
+}
+
+// Q5_0Tensor.cs:47-130 (block 32 fixed): scale = maxAbs > 0 ? maxAbs/15f : 1f,
+// q = (int)round_half_even(clamp(x * (1/scale), -16, 15)) + 16; the low nibble packed
+// by global index, bit (i - blockStart) of the block's little-endian 32-bit word the high bit.
+int or_q50_quantize(const float* src, int64_t n, uint8_t* low, uint8_t* high, float* scales) {
+  if (n <= 0) return -1;
+  const int bs = 32;
+  const int64_t nb = (n + bs - 1) / bs;
+  for (int64_t b = 0; b < nb; ++b) {
+    const int64_t s = b * bs, e = std::min<int64_t>(s + bs, n);
+    float maxAbs = 0.f;
+    for (int64_t i = s; i < e; ++i) maxAbs = std::max(maxAbs, std::fabs(src[i]));
+    const float scale = maxAbs > 0.f ? maxAbs / 15.f : 1.f;
+    scales[b] = scale;
+    const float inv = 1.f / scale;
+    uint32_t hb = 0;
+    for (int64_t i = s; i < e; ++i) {
+      const int c = (int)round_half_even(clampf(src[i] * inv, -16.f, 15.f)) + 16;
+      const int64_t bi = i / 2;
+      if (i % 2 == 0)
+        low[bi] = (uint8_t)(c & 0xF);
+      else
+        low[bi] = (uint8_t)((low[bi] & 0x0F) | ((c & 0xF) << 4));
+      hb |= (uint32_t)((c >> 4) & 1) << (i - s);
+    }
+    for (int k = 0; k < 4; ++k) high[4 * b + k] = (uint8_t)(hb >> (8 * k));
+  }
+  return 0;
+}
+
+// Q5_0Tensor.cs:136-182: w = (((low | high << 4)) - 16) * scale.
+void or_q50_dequantize(const uint8_t* low, const uint8_t* high, const float* scales, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t b = i / 32;
+    const uint32_t hb = (uint32_t)high[4 * b] | ((uint32_t)high[4 * b + 1] << 8) | ((uint32_t)high[4 * b + 2] << 16) |
+                        ((uint32_t)high[4 * b + 3] << 24);
+    const uint8_t p = low[i / 2];
+    const int lo4 = (i % 2 == 0) ? (p & 0xF) : ((p >> 4) & 0xF);
+    const int q = (lo4 | (int)(((hb >> (i - 32 * b)) & 1) << 4)) - 16;
+    out[i] = (float)q * scales[b];
+  }
+}
+
 // Q4_K quantizer (this build's own; the reference has none).  Emits the
 // reference's byte layout (Q4KTensor.cs:84-147): per 32-element sub-block a
 // 6-bit scale and 6-bit min under fp16 super-scales d/dmin, w ~= d*s*q - dmin*m.
@@ -393,8 +477,23 @@ void or_q6k_dequantize(const uint8_t* src, int64_t n, float* out) {
 
 // ---------------------------------------------------------------------------
 // Quantized matmul.
+// Element li of a Q4_1 / Q5_0 tensor of n_total elements.  Q4_1: `scales` holds
+// the block scales then the block mins; Q5_0: `data` holds the low nibbles then
+// the 4-byte high-bit words of the blocks.
+static float q41_q50_elem(int scheme, const void* data, const float* scales, int64_t n_total, int64_t li) {
+  const uint8_t* q = (const uint8_t*)data;
+  const int64_t b = li / 32, nb = (n_total + 31) / 32;
+  const uint8_t p = q[li / 2];
+  const int lo4 = (li % 2 == 0) ? (p & 0xF) : ((p >> 4) & 0xF);
+  if (scheme == OR_Q4_1) return (float)lo4 * scales[b] + scales[nb + b];
+  const uint8_t* high = q + (n_total + 1) / 2 + 4 * b;
+  const uint32_t hb = (uint32_t)high[0] | ((uint32_t)high[1] << 8) | ((uint32_t)high[2] << 16) | ((uint32_t)high[3] << 24);
+  const int v = (lo4 | (int)(((hb >> (li - 32 * b)) & 1) << 4)) - 16;
+  return (float)v * scales[b];
+}
+
 static void decode_row_intended(int scheme, const void* data, const float* scales, int bs, int64_t n, int K,
-                                float* w) {
+                                float* w, int64_t n_total) {
   // Row n of W[N][K] in linear-index order (Q*Tensor.Dequantize element formulas).
   int64_t base = n * (int64_t)K;
   switch (scheme) {
@@ -414,6 +513,11 @@ static void decode_row_intended(int scheme, const void* data, const float* scale
         int nib = (i % 2 == 0) ? (p & 0xF) : ((p >> 4) & 0xF);
         w[k] = (float)or_q4_decode_nibble(nib) * scales[i / bs];
       }
+      break;
+    }
+    case OR_Q4_1:
+    case OR_Q5_0: {
+      for (int k = 0; k < K; ++k) w[k] = q41_q50_elem(scheme, data, scales, n_total, base + k);
       break;
     }
     case OR_Q4_K: {
@@ -436,7 +540,7 @@ int or_matmul(int scheme, int mode, const void* data, const float* scales, int b
   if (mode == 1) {
     std::vector<float> w(K);
     for (int n = 0; n < N; ++n) {
-      decode_row_intended(scheme, data, scales, bs, n, K, w.data());
+      decode_row_intended(scheme, data, scales, bs, n, K, w.data(), (int64_t)N * K);
       for (int m = 0; m < M; ++m) {
         const float* a = A + (int64_t)m * K;
         float s = 0.f;
@@ -484,6 +588,22 @@ int or_matmul(int scheme, int mode, const void* data, const float* scales, int b
           if (C64) C64[(int64_t)m * N + n] += (double)av * (double)q * (double)sc;
         }
       }
+    }
+    return 0;
+  }
+  if (scheme == OR_Q4_1 || scheme == OR_Q5_0) {
+    // FusedQ4_1MatMul.cs:356-385 / FusedQ5_0MatMul.cs:388-426 (scalar paths): bkj =
+    // the dequantized element at linear index k*N + j, C[i][j] += a[i][k] * bkj, k ascending
+    const int64_t nt = (int64_t)K * N;
+    for (int m = 0; m < M; ++m) {
+      const float* a = A + (int64_t)m * K;
+      float* c = C + (int64_t)m * N;
+      for (int k = 0; k < K; ++k)
+        for (int n = 0; n < N; ++n) {
+          const float bkj = q41_q50_elem(scheme, data, scales, nt, (int64_t)k * N + n);
+          c[n] += a[k] * bkj;
+          if (C64) C64[(int64_t)m * N + n] += (double)a[k] * (double)bkj;
+        }
     }
     return 0;
   }
@@ -641,7 +761,7 @@ static void linear_fwd(const or_linear& L, const float* x, float* y, int M, int 
     int n0 = (int)((int64_t)N * c / chunks), n1 = (int)((int64_t)N * (c + 1) / chunks);
     std::vector<float> w(K);
     for (int n = n0; n < n1; ++n) {
-      decode_row_intended(L.scheme, L.data, L.scales, L.block_size, n, K, w.data());
+      decode_row_intended(L.scheme, L.data, L.scales, L.block_size, n, K, w.data(), (int64_t)N * K);
       for (int m = 0; m < M; ++m) {
         const float* a = x + (int64_t)m * K;
         float s = 0.f;

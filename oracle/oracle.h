@@ -50,6 +50,13 @@ void or_q8_dequantize(const int8_t* data, const float* scales, int64_t n, int bl
 int  or_q4_decode_nibble(int nibble);
 int  or_q4_quantize(const float* src, int64_t n, int block_size, uint8_t* data, float* scales);
 void or_q4_dequantize(const uint8_t* data, const float* scales, int64_t n, int block_size, float* out);
+/* ---- Q4_1 (Q4_1Tensor.cs) and Q5_0 (Q5_0Tensor.cs), block size 32 ----
+ * In or_matmul: Q4_1 `scales` = the block scales followed by the block mins;
+ * Q5_0 `data` = the low nibbles ((n+1)/2 bytes) followed by the 4-byte high-bit words. */
+int  or_q41_quantize(const float* src, int64_t n, uint8_t* data, float* scales, float* mins);
+void or_q41_dequantize(const uint8_t* data, const float* scales, const float* mins, int64_t n, float* out);
+int  or_q50_quantize(const float* src, int64_t n, uint8_t* low, uint8_t* high, float* scales);
+void or_q50_dequantize(const uint8_t* low, const uint8_t* high, const float* scales, int64_t n, float* out);
 /* ---- Q4_K / Q6_K (Q4KTensor.cs, Q6KTensor.cs); quantizers are this build's own ---- */
 void or_q4k_quantize(const float* src, int64_t n, uint8_t* out);
 void or_q4k_dequantize(const uint8_t* src, int64_t n, float* out);

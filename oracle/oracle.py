@@ -78,6 +78,10 @@ def _declare(L):
         "or_q8_dequantize": (None, [vp, vp, i64, i, vp]),
         "or_q4_decode_nibble": (i, [i]),
         "or_q4_quantize": (i, [vp, i64, i, vp, vp]),
+        "or_q41_quantize": (i, [vp, i64, vp, vp, vp]),
+        "or_q41_dequantize": (None, [vp, vp, vp, i64, vp]),
+        "or_q50_quantize": (i, [vp, i64, vp, vp, vp]),
+        "or_q50_dequantize": (None, [vp, vp, vp, i64, vp]),
         "or_q4_dequantize": (None, [vp, vp, i64, i, vp]),
         "or_q4k_quantize": (None, [vp, i64, vp]),
         "or_q4k_dequantize": (None, [vp, i64, vp]),
@@ -151,6 +155,20 @@ def quantize(x: np.ndarray, scheme: int, rows: int, cols: int, block_size: int =
         scales = np.empty((n + block_size - 1) // block_size, np.float32)
         assert L.or_q4_quantize(_p(x), n, block_size, _p(data), _p(scales)) == 0
         return QTensor(scheme, rows, cols, data, scales, block_size)
+    if scheme == Q4_1:
+        # QTensor convention: data = nibbles, scales = block scales then block mins (block 32)
+        nb = (n + 31) // 32
+        data = np.zeros((n + 1) // 2, np.uint8)
+        sc = np.empty(2 * nb, np.float32)
+        assert L.or_q41_quantize(_p(x), n, _p(data), _p(sc[:nb]), sc[nb:].ctypes.data_as(C.c_void_p)) == 0
+        return QTensor(scheme, rows, cols, data, sc, 32)
+    if scheme == Q5_0:
+        # QTensor convention: data = low nibbles then the 4-byte high-bit words, scales (block 32)
+        nb = (n + 31) // 32
+        data = np.zeros((n + 1) // 2 + 4 * nb, np.uint8)
+        sc = np.empty(nb, np.float32)
+        assert L.or_q50_quantize(_p(x), n, _p(data), data[(n + 1) // 2:].ctypes.data_as(C.c_void_p), _p(sc)) == 0
+        return QTensor(scheme, rows, cols, data, sc, 32)
     if scheme == Q4_K:
         assert cols % 256 == 0
         data = np.empty(n // 256 * 144, np.uint8)
@@ -174,6 +192,11 @@ def dequantize(t: QTensor) -> np.ndarray:
         L.or_q8_dequantize(_p(t.data), _p(t.scales), n, t.block_size, _p(out))
     elif t.scheme == Q4_0:
         L.or_q4_dequantize(_p(t.data), _p(t.scales), n, t.block_size, _p(out))
+    elif t.scheme == Q4_1:
+        nb = (n + 31) // 32
+        L.or_q41_dequantize(_p(t.data), _p(t.scales), t.scales[nb:].ctypes.data_as(C.c_void_p), n, _p(out))
+    elif t.scheme == Q5_0:
+        L.or_q50_dequantize(_p(t.data), t.data[(n + 1) // 2:].ctypes.data_as(C.c_void_p), _p(t.scales), n, _p(out))
     elif t.scheme == Q4_K:
         L.or_q4k_dequantize(_p(t.data), n, _p(out))
     elif t.scheme == Q6_K:

@@ -62,13 +62,17 @@ struct DeviceGuard {
   }
 };
 
-bool valid_scheme(int s) { return s == SM_F32 || s == SM_Q8_0 || s == SM_Q4_0 || s == SM_Q4_K || s == SM_Q6_K; }
+bool valid_scheme(int s) {
+  return s == SM_F32 || s == SM_Q8_0 || s == SM_Q4_0 || s == SM_Q4_1 || s == SM_Q5_0 || s == SM_Q4_K || s == SM_Q6_K;
+}
 
 size_t packed_bytes(int scheme, int64_t n) {
   switch (scheme) {
     case SM_F32: return (size_t)n * 4;
     case SM_Q8_0: return (size_t)n;
     case SM_Q4_0: return (size_t)(n + 1) / 2;
+    case SM_Q4_1: return (size_t)(n + 1) / 2;                          // nibbles
+    case SM_Q5_0: return (size_t)(n + 1) / 2 + 4 * (size_t)((n + 31) / 32);  // low nibbles, then 32 high bits per block
     case SM_Q4_K: return (size_t)(n / 256) * Q4K_BLOCK_BYTES;
     case SM_Q6_K: return (size_t)(n / 256) * Q6K_BLOCK_BYTES;
   }
@@ -106,6 +110,14 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
   if ((scheme == SM_Q4_K || scheme == SM_Q6_K) && layout == SM_LAYOUT_REFERENCE && rows % 256)
     return fail(SM_ERR_SHAPE, "weight_upload: reference-layout K-quant needs K (rows) divisible by 256");
   if (nbytes != packed_bytes(scheme, n)) return fail(SM_ERR_SHAPE, "weight_upload: data length does not match shape");
+  const bool q41_q50 = scheme == SM_Q4_1 || scheme == SM_Q5_0;
+  if (q41_q50) {
+    // block size fixed at 32 (Q4_1Tensor.cs:14, Q5_0Tensor.cs:14); Q4_1 scales = block scales then block mins
+    const size_t nb = (size_t)((n + 31) / 32);
+    if (bs != 32 && bs != 0) return fail(SM_ERR_INVALID_ARG, "weight_upload: Q4_1 / Q5_0 block size is 32");
+    if (!scales || nscales != (scheme == SM_Q4_1 ? 2 * nb : nb))
+      return fail(SM_ERR_SHAPE, "weight_upload: scales length does not match block count");
+  }
   const bool has_scales = scheme == SM_Q8_0 || scheme == SM_Q4_0;
   if (has_scales) {
     if (bs <= 0) return fail(SM_ERR_INVALID_ARG, "weight_upload: block size must be positive");
@@ -121,7 +133,7 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
   d.layout = layout;
   d.rows = rows;
   d.cols = cols;
-  d.block_size = has_scales ? bs : 256;
+  d.block_size = has_scales ? bs : (q41_q50 ? 32 : 256);
   d.n = n;
   const cudaMemcpyKind kind = from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   cudaStream_t st = ctx->stream;
@@ -152,6 +164,32 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
                                  d.aux_stride, st);
     cudaFreeAsync(staging, st);
     if (rc) return cleanup(rc);
+  } else if (q41_q50) {
+    // nibbles in data; the scales and the second per-block array (mins / high bits) in aux
+    const int64_t nb = (n + 31) / 32;
+    d.data_bytes = (size_t)(n + 1) / 2;
+    if (cudaMalloc(&d.data, d.data_bytes) != cudaSuccess)
+      return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+    cudaMemcpyAsync(d.data, data, d.data_bytes, kind, st);
+    const void* second = scheme == SM_Q4_1 ? (const void*)(scales + nb) : (const void*)((const uint8_t*)data + d.data_bytes);
+    if (layout == SM_LAYOUT_INTENDED && cols % 32 == 0) {  // [scales | second] rows, padded to 16 bytes
+      d.aux_bpr = cols / 32;
+      d.aux_stride = (2 * d.aux_bpr * 4 + 15) / 16 * 4;
+      d.aux_bytes = (size_t)rows * d.aux_stride * 4;
+      if (cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
+        return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+      cudaMemsetAsync(d.aux, 0, d.aux_bytes, st);
+      cudaMemcpy2DAsync(d.aux, (size_t)d.aux_stride * 4, scales, (size_t)d.aux_bpr * 4, (size_t)d.aux_bpr * 4, rows,
+                        kind, st);
+      cudaMemcpy2DAsync((float*)d.aux + d.aux_bpr, (size_t)d.aux_stride * 4, second, (size_t)d.aux_bpr * 4,
+                        (size_t)d.aux_bpr * 4, rows, kind, st);
+    } else {
+      d.aux_bytes = (size_t)nb * 8;
+      if (cudaMalloc(&d.aux, d.aux_bytes) != cudaSuccess)
+        return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));
+      cudaMemcpyAsync(d.aux, scales, (size_t)nb * 4, kind, st);
+      cudaMemcpyAsync((float*)d.aux + nb, second, (size_t)nb * 4, kind, st);
+    }
   } else {
     d.data_bytes = nbytes;
     if (cudaMalloc(&d.data, nbytes) != cudaSuccess) return cleanup(fail(SM_ERR_OOM, "weight_upload: out of device memory"));

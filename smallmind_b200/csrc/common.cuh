@@ -59,6 +59,29 @@ __host__ __device__ __forceinline__ int64_t aux_idx(int64_t b, int bpr, int stri
   return stride ? (b / bpr) * stride + (b % bpr) : b;
 }
 
+// Q4_1 / Q5_0 (block 32): the aux array holds the block scales and, beside them,
+// a second value per block (Q4_1: the min; Q5_0: the 32 high bits as a uint32).
+// Row-padded aux (aux_stride > 0): a row is [scales (bpr) | second (bpr) | pad];
+// plain aux: [scales (all blocks) | second (all blocks)].
+__host__ __device__ __forceinline__ int64_t aux_second_idx(int64_t b, int bpr, int stride, int64_t nblocks) {
+  return stride ? (b / bpr) * stride + bpr + (b % bpr) : nblocks + b;
+}
+
+// w of element li of a Q4_1 / Q5_0 weight (Q4_1Tensor.cs:153-156: q * scale + min;
+// Q5_0Tensor.cs:157-172: (low | high << 4) - 16, times scale)
+__device__ __forceinline__ float q41_q50_weight(int scheme, const void* data, const void* aux, int bpr, int stride,
+                                                int64_t nblocks, int64_t li) {
+  const int64_t b = li >> 5;
+  const uint8_t p = ((const uint8_t*)data)[li >> 1];
+  const int lo4 = (li & 1) ? (p >> 4) : (p & 0xF);
+  const float* af = (const float*)aux;
+  const float sc = af[aux_idx(b, bpr, stride)];
+  if (scheme == 4 /* SM_Q4_1 */) return __fadd_rn(__fmul_rn((float)lo4, sc), af[aux_second_idx(b, bpr, stride, nblocks)]);
+  const uint32_t hb = ((const uint32_t*)aux)[aux_second_idx(b, bpr, stride, nblocks)];
+  const int q = (lo4 | (int)(((hb >> (li & 31)) & 1u) << 4)) - 16;
+  return __fmul_rn((float)q, sc);
+}
+
 constexpr int Q4K_BLOCK_BYTES = 144;
 constexpr int Q6K_BLOCK_BYTES = 210;
 constexpr int Q6K_BODY_BYTES = 208;

@@ -71,6 +71,37 @@ struct Decoder<SM_Q4_0> {
   }
 };
 
+// Q4_1 / Q5_0 (block 32 = one unit): Q4_1Tensor.cs:153-156 (q * scale + min),
+// Q5_0Tensor.cs:157-172 ((low | high << 4) - 16, times scale); nibbles by global index.
+template <int FMT>
+struct Decoder41_50 {
+  __device__ __forceinline__ static void decode(const DevWeight& W, int row, int u, int K, bool, int, UnitW& o) {
+    const int64_t e0 = (int64_t)row * K + 32 * u;
+    const int64_t b = e0 >> 5, nb = (W.n + 31) / 32;
+    const int4 a = __ldg((const int4*)((const uint8_t*)W.data + e0 / 2));
+    const float* af = (const float*)W.aux;
+    const float sc = af[aux_idx(b, W.aux_bpr, W.aux_stride)];
+    const int64_t i2 = aux_second_idx(b, W.aux_bpr, W.aux_stride, nb);
+    const int v[4] = {a.x, a.y, a.z, a.w};
+    if (FMT == SM_Q4_1) {
+      const float mn = af[i2];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o.w[e] = __fadd_rn(__fmul_rn((float)((v[e >> 3] >> (4 * (e & 7))) & 0xF), sc), mn);
+    } else {
+      const uint32_t hb = ((const uint32_t*)W.aux)[i2];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int q = (((v[e >> 3] >> (4 * (e & 7))) & 0xF) | (int)(((hb >> e) & 1u) << 4)) - 16;
+        o.w[e] = __fmul_rn((float)q, sc);
+      }
+    }
+  }
+};
+template <>
+struct Decoder<SM_Q4_1> : Decoder41_50<SM_Q4_1> {};
+template <>
+struct Decoder<SM_Q5_0> : Decoder41_50<SM_Q5_0> {};
+
 __device__ __forceinline__ int64_t kq_block(int row, int kb, int K, int N, bool literal) {
   return literal ? (int64_t)kb * N + row : (int64_t)row * (K / 256) + kb;
 }
@@ -210,6 +241,9 @@ __device__ __forceinline__ float elem_weight(const DevWeight& W, int64_t li) {
       const int nib = (li & 1) ? (p >> 4) : (p & 0xF);
       return __fmul_rn((float)(nib < 8 ? nib : nib - 16), ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)]);
     }
+    case SM_Q4_1:
+    case SM_Q5_0:
+      return q41_q50_weight(W.scheme, W.data, W.aux, W.aux_bpr, W.aux_stride, (W.n + 31) / 32, li);
     default:
       return ((const float*)W.data)[li];
   }
@@ -236,6 +270,10 @@ __global__ void matmul_literal_linear_kernel(DevWeight W, const float* __restric
       const int nib = (li & 1) ? (p >> 4) : (p & 0xF);
       q = (float)(nib < 8 ? nib : nib - 16);
       sc = ((const float*)W.aux)[aux_idx(li / W.block_size, W.aux_bpr, W.aux_stride)];
+    } else if (W.scheme == SM_Q4_1 || W.scheme == SM_Q5_0) {
+      // FusedQ4_1MatMul.cs:380-383 / FusedQ5_0MatMul.cs:421-424: C += aik * bkj, bkj dequantized
+      acc = __fadd_rn(acc, __fmul_rn(a, elem_weight(W, li)));
+      continue;
     } else {
       q = ((const float*)W.data)[li];
       sc = 1.f;
@@ -365,6 +403,8 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
   switch (W.scheme) {
     case SM_Q8_0: return launch_rows<SM_Q8_0>(W, x, y, M, ldy, accumulate, st, n_launch);
     case SM_Q4_0: return launch_rows<SM_Q4_0>(W, x, y, M, ldy, accumulate, st, n_launch);
+    case SM_Q4_1: return launch_rows<SM_Q4_1>(W, x, y, M, ldy, accumulate, st, n_launch);
+    case SM_Q5_0: return launch_rows<SM_Q5_0>(W, x, y, M, ldy, accumulate, st, n_launch);
     case SM_Q4_K: return launch_rows<SM_Q4_K>(W, x, y, M, ldy, accumulate, st, n_launch);
     case SM_Q6_K: return launch_rows<SM_Q6_K>(W, x, y, M, ldy, accumulate, st, n_launch);
     case SM_F32: return launch_rows<SM_F32>(W, x, y, M, ldy, accumulate, st, n_launch);

@@ -278,8 +278,18 @@ inline int grid_for(int64_t n, int threads) {
 
 }  // namespace
 
+__global__ void dequant_q41_q50_kernel(DevWeight w, float* __restrict__ out) {
+  const int64_t nb = (w.n + 31) / 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < w.n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = q41_q50_weight(w.scheme, w.data, w.aux, w.aux_bpr, w.aux_stride, nb, i);
+}
+
 int launch_dequant(const DevWeight& w, float* out, cudaStream_t st) {
   switch (w.scheme) {
+    case SM_Q4_1:
+    case SM_Q5_0:
+      dequant_q41_q50_kernel<<<grid_for(w.n, 256), 256, 0, st>>>(w, out);
+      break;
     case SM_Q8_0:
       dequant_q8_kernel<<<grid_for(w.n, 256), 256, 0, st>>>((const int8_t*)w.data, (const float*)w.aux, w.n,
                                                              w.block_size, w.aux_bpr, w.aux_stride, out);

@@ -13,7 +13,7 @@ entries: data = the tensor's blocks in the reference byte layout (144 / 210
 bytes per 256 elements, Q4KTensor.cs:84-94, Q6KTensor.cs:86-95), no aux.
 
 GGUF (versions 2 and 3, as GgufReader.cs:39-120 reads them) holds ggml-layout
-blocks.  Q8_0 / Q4_0 / Q4_K / Q6_K blocks are converted to the reference byte
+blocks.  Q8_0 / Q4_0 / Q4_1 / Q5_0 / Q4_K / Q6_K blocks are converted to the reference byte
 layouts without any requantization (the conversion only moves bits: every
 weight decodes to the same value), then uploaded with ``sm_weight_upload``.
 F32 / F16 tensors (norms, embeddings) are read as fp32.
@@ -81,6 +81,10 @@ def _smq_data_aux_len(t: HostTensor) -> tuple[int, int]:
         return n, 4 * ((n + t.block_size - 1) // t.block_size)
     if s == QuantScheme.Q4_0:
         return (n + 1) // 2, 4 * ((n + t.block_size - 1) // t.block_size)
+    if s == QuantScheme.Q4_1:  # nibbles; aux = fp32 scales then fp32 mins
+        return (n + 1) // 2, 8 * ((n + 31) // 32)
+    if s == QuantScheme.Q5_0:  # low nibbles then a 32-bit high-bit word per block; aux = fp32 scales
+        return (n + 1) // 2 + 4 * ((n + 31) // 32), 4 * ((n + 31) // 32)
     if s in KQ_BLOCK_BYTES:
         if n % 256:
             raise ValueError(f"{t.name}: K-quant tensors need a multiple of 256 elements")
@@ -174,8 +178,9 @@ def smq_read(path_or_bytes) -> SmqFile:
 # ---------------------------------------------------------------- GGUF
 
 GGUF_MAGIC = b"GGUF"
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 0, 1, 2, 8, 12, 14
-GGML_BLOCK = {GGML_Q4_0: (32, 18), GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144), GGML_Q6_K: (256, 210)}
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 0, 1, 2, 3, 6, 8, 12, 14
+GGML_BLOCK = {GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q5_0: (32, 22), GGML_Q8_0: (32, 34),
+              GGML_Q4_K: (256, 144), GGML_Q6_K: (256, 210)}
 # value types (GgufValueType.cs): fixed-size scalars -> struct code
 _GGUF_SCALAR = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
 GGUF_STRING, GGUF_ARRAY = 8, 9
@@ -294,6 +299,33 @@ def ggml_q4_0_to_ref(raw: np.ndarray, n: int) -> tuple[np.ndarray, np.ndarray]:
     return packed[: (n + 1) // 2], _f16(np.ascontiguousarray(b[:, :2])).reshape(-1)
 
 
+def _ggml_nibbles_by_index(qs: np.ndarray) -> np.ndarray:
+    """ggml's 16 code bytes per block (element i low nibble of byte i, element
+    i + 16 high nibble) -> nibbles packed by global index, even element in the
+    low nibble (Q4_1Tensor.cs / Q5_0Tensor.cs element order)."""
+    v = np.concatenate([qs & 0xF, qs >> 4], axis=1).reshape(-1)
+    return (v[0::2] | (v[1::2] << 4)).astype(np.uint8)
+
+
+def ggml_q4_1_to_ref(raw: np.ndarray, n: int) -> tuple[np.ndarray, np.ndarray]:
+    """ggml Q4_1 (fp16 d, fp16 m, 16 code bytes; value q d + m) -> Q4_1Tensor
+    nibbles by global index + [fp32 scales | fp32 mins], block size 32."""
+    b = raw.reshape(-1, 20)
+    d = _f16(np.ascontiguousarray(b[:, 0:2])).reshape(-1)
+    m = _f16(np.ascontiguousarray(b[:, 2:4])).reshape(-1)
+    return _ggml_nibbles_by_index(b[:, 4:])[: (n + 1) // 2], np.concatenate([d, m])
+
+
+def ggml_q5_0_to_ref(raw: np.ndarray, n: int) -> tuple[np.ndarray, np.ndarray]:
+    """ggml Q5_0 (fp16 d, 32-bit qh with bit i = element i's fifth bit, 16 code
+    bytes; value ((lo | hi << 4) - 16) d) -> Q5_0Tensor low nibbles by global
+    index followed by the per-block high words, + fp32 scales, block size 32."""
+    b = raw.reshape(-1, 22)
+    d = _f16(np.ascontiguousarray(b[:, 0:2])).reshape(-1)
+    hi = np.ascontiguousarray(b[:, 2:6]).reshape(-1)
+    return np.concatenate([_ggml_nibbles_by_index(b[:, 6:])[: (n + 1) // 2], hi]), d
+
+
 def _ggml_q4k_scale_min(sc: np.ndarray):
     """The 8 six-bit scales and mins of ggml's 12-byte Q4_K field, per block."""
     s = np.empty((sc.shape[0], 8), np.uint8)
@@ -371,6 +403,12 @@ def gguf_tensor_to_host(g: GgufFile, t: GgufTensorInfo) -> HostTensor:
     if t.type == GGML_Q4_0:
         d, s = ggml_q4_0_to_ref(raw, n)
         return HostTensor(t.name, QuantScheme.Q4_0, dims, d, s, 32)
+    if t.type == GGML_Q4_1:
+        d, s = ggml_q4_1_to_ref(raw, n)
+        return HostTensor(t.name, QuantScheme.Q4_1, dims, d, s, 32)
+    if t.type == GGML_Q5_0:
+        d, s = ggml_q5_0_to_ref(raw, n)
+        return HostTensor(t.name, QuantScheme.Q5_0, dims, d, s, 32)
     if t.type == GGML_Q4_K:
         return HostTensor(t.name, QuantScheme.Q4_K, dims, ggml_q4_k_to_ref(raw))
     if t.type == GGML_Q6_K:
@@ -410,6 +448,17 @@ def config_from_metadata(meta: dict, tensors: dict, max_context: int | None = No
 
 def _rows(t: HostTensor, r0: int, r1: int) -> HostTensor:
     """Rows [r0, r1) of a weight whose rows are whole blocks (a merged Q|K|V split)."""
+    if t.scheme in (QuantScheme.Q4_1, QuantScheme.Q5_0):
+        if t.cols % 32:
+            raise ValueError(f"{t.name}: rows are not whole blocks")
+        nb, bpr, lo = t.rows * t.cols // 32, t.cols // 32, t.rows * t.cols // 2
+        data = t.data[r0 * t.cols // 2:r1 * t.cols // 2]
+        if t.scheme == QuantScheme.Q5_0:
+            sc = t.scales[r0 * bpr:r1 * bpr]
+            data = np.concatenate([data, t.data[lo + 4 * r0 * bpr:lo + 4 * r1 * bpr]])
+        else:
+            sc = np.concatenate([t.scales[r0 * bpr:r1 * bpr], t.scales[nb + r0 * bpr:nb + r1 * bpr]])
+        return HostTensor(t.name, t.scheme, [r1 - r0, t.cols], data, sc, 32)
     per = t.data.nbytes // t.rows
     if per * t.rows != t.data.nbytes:
         raise ValueError(f"{t.name}: rows are not whole blocks")

@@ -6,8 +6,8 @@ import struct
 
 import numpy as np
 
-F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
-BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+F32, F16, Q4_0, Q4_1, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 3, 6, 8, 12, 14
+BLOCK = {Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 
 
 def _s(x: str) -> bytes:
@@ -59,8 +59,11 @@ def random_blocks(ttype: int, n: int, rs: np.random.RandomState, scale: float = 
     nb = n // be
     b = rs.randint(0, 256, (nb, bb)).astype(np.uint8)
     h = lambda a: np.asarray(a, np.float16).view(np.uint8).reshape(nb, -1)
-    if ttype in (Q4_0, Q8_0):
+    if ttype in (Q4_0, Q8_0, Q5_0):
         b[:, 0:2] = h(rs.randn(nb) * scale * 10)
+    elif ttype == Q4_1:
+        b[:, 0:2] = h(np.abs(rs.randn(nb)) * scale * 10)
+        b[:, 2:4] = h(rs.randn(nb) * scale * 50)
     elif ttype == Q4_K:
         b[:, 0:2] = h(np.abs(rs.randn(nb)) * scale)
         b[:, 2:4] = h(np.abs(rs.randn(nb)) * scale)
@@ -75,7 +78,7 @@ def _f16(b):
 
 
 def ggml_dequant(ttype: int, raw: np.ndarray) -> np.ndarray:
-    """fp32 values of ggml blocks (the published Q8_0 / Q4_0 / Q4_K / Q6_K formulas)."""
+    """fp32 values of ggml blocks (the published Q8_0 / Q4_0 / Q4_1 / Q5_0 / Q4_K / Q6_K formulas)."""
     f = np.float32
     if ttype == Q8_0:
         b = raw.reshape(-1, 34)
@@ -84,6 +87,16 @@ def ggml_dequant(ttype: int, raw: np.ndarray) -> np.ndarray:
         b = raw.reshape(-1, 18)
         q = np.concatenate([b[:, 2:] & 0xF, b[:, 2:] >> 4], axis=1).astype(np.int32) - 8
         return (q.astype(f) * _f16(b[:, :2])).reshape(-1)
+    if ttype == Q4_1:
+        b = raw.reshape(-1, 20)
+        q = np.concatenate([b[:, 4:] & 0xF, b[:, 4:] >> 4], axis=1).astype(f)
+        return ((q * _f16(b[:, 0:2])).astype(f) + _f16(b[:, 2:4])).reshape(-1)
+    if ttype == Q5_0:
+        b = raw.reshape(-1, 22)
+        qh = np.ascontiguousarray(b[:, 2:6]).view(np.uint32).astype(np.int64)
+        lo = np.concatenate([b[:, 6:] & 0xF, b[:, 6:] >> 4], axis=1).astype(np.int64)
+        hi = (qh >> np.arange(32)) & 1
+        return (((lo | (hi << 4)) - 16).astype(f) * _f16(b[:, 0:2])).reshape(-1)
     if ttype == Q4_K:
         b = raw.reshape(-1, 144)
         d, dmin = _f16(b[:, 0:2]), _f16(b[:, 2:4])

@@ -28,11 +28,12 @@ def _tensors(O):
     rs = np.random.RandomState(0)
     out = [L.HostTensor("norm.weight", L.QuantScheme.F32, [64], rs.randn(64).astype(np.float32).view(np.uint8))]
     for name, sch, rows, cols, bs in [("q8.weight", O.Q8_0, 8, 128, 64), ("q4.weight", O.Q4_0, 6, 96, 32),
+                                      ("q41.weight", O.Q4_1, 5, 64, 32), ("q50.weight", O.Q5_0, 3, 96, 32),
                                       ("q4k.weight", O.Q4_K, 4, 512, 256), ("q6k.weight", O.Q6_K, 3, 256, 256)]:
         t = O.quantize(rs.randn(rows * cols).astype(np.float32), sch, rows, cols, bs)
         sc = None if t.scales is None else np.asarray(t.scales, np.float32)
         out.append(L.HostTensor(name, sch, [rows, cols], np.asarray(t.data).view(np.uint8).copy(), sc,
-                                bs if sch in (O.Q8_0, O.Q4_0) else 256))
+                                bs if sch in (O.Q8_0, O.Q4_0, O.Q4_1, O.Q5_0) else 256))
     return out
 
 
@@ -97,7 +98,8 @@ def test_smq_rejects_malformed(O, tmp_path):
         L.smq_read(bytes(bad))
 
 
-@pytest.mark.parametrize("ttype,scheme", [(G.Q8_0, "Q8_0"), (G.Q4_0, "Q4_0"), (G.Q4_K, "Q4_K"), (G.Q6_K, "Q6_K")])
+@pytest.mark.parametrize("ttype,scheme", [(G.Q8_0, "Q8_0"), (G.Q4_0, "Q4_0"), (G.Q4_1, "Q4_1"), (G.Q5_0, "Q5_0"),
+                                          (G.Q4_K, "Q4_K"), (G.Q6_K, "Q6_K")])
 def test_ggml_blocks_convert_bit_exact(O, ttype, scheme):
     """Every weight decodes to the same fp32 value after the layout conversion."""
     L = _ld()
@@ -111,6 +113,23 @@ def test_ggml_blocks_convert_bit_exact(O, ttype, scheme):
     want = G.ggml_dequant(ttype, raw)
     assert got.dtype == np.float32
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("ttype", [G.Q4_1, G.Q5_0])
+def test_rows_split_of_block32_pairs(O, ttype):
+    """A merged Q|K|V of Q4_1 / Q5_0 splits by rows into tensors that decode to
+    the same rows (their second per-block field travels with the rows)."""
+    L = _ld()
+    rs = np.random.RandomState(3)
+    rows, cols = 12, 96
+    raw = G.random_blocks(ttype, rows * cols, rs)
+    g = L.GgufFile(3, {}, [], 0, bytes(raw))
+    t = L.gguf_tensor_to_host(g, L.GgufTensorInfo("w", [cols, rows], ttype, 0))
+    full = O.dequantize(O.QTensor(int(t.scheme), rows, cols, t.data, t.scales, 32))
+    for r0, r1 in [(0, 5), (5, 9), (9, 12)]:
+        p = L._rows(t, r0, r1)
+        got = O.dequantize(O.QTensor(int(p.scheme), r1 - r0, cols, p.data, p.scales, 32))
+        assert np.array_equal(got.view(np.uint32), full[r0:r1].view(np.uint32))
 
 
 def test_gguf_read_and_import_to_smq(O, tmp_path):

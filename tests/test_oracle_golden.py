@@ -241,3 +241,46 @@ def test_kv_step_twin_matches_full_recompute(O):
         lg = dec.step(toks[t:t + 1])
         ref = O.model_forward(host, toks[:t + 1], 1)[0]
         assert rel_err(lg, ref) < 1e-5
+
+
+# ---------------------------------------------------------------- Q4_1 / Q5_0
+@pytest.mark.parametrize("scheme,m,k,n,lo,tol", [("Q4_1", 4, 64, 32, 2.0, 5.0), ("Q5_0", 4, 64, 32, 3.0, 3.0),
+                                                 ("Q4_1", 1, 64, 64, 1.0, 5.0), ("Q5_0", 1, 64, 64, 1.0, 3.0)])
+def test_reference_fused_q41_q50_matches_dequantized(O, scheme, m, k, n, lo, tol):
+    # ExpandedQuantizationTests.cs:229-300: Random(42), a ~ U(-1, 1), B ~ U(-lo, lo) quantized K x N;
+    # the fused kernel against matmul over the dequantized B, percent tolerance per element
+    r = O.dotnet_random(42)
+    a = O.dotnet_random_floats(r, m * k, -1.0, 1.0)
+    b = O.dotnet_random_floats(r, k * n, -lo, lo)
+    t = O.quantize(b, getattr(O, scheme), k, n, 32)
+    expected = _matmul_float(a, O.dequantize(t).reshape(-1), m, k, n)
+    got = O.matmul(t, a, m, k, n, mode=0).reshape(-1)
+    _assert_arrays_close(expected, got, tol)
+
+
+@pytest.mark.parametrize("scheme", ["Q4_1", "Q5_0"])
+@pytest.mark.parametrize("rows,cols", [(4, 64), (3, 50), (1, 7)])
+def test_q41_q50_sizes_and_determinism(O, scheme, rows, cols):
+    # ExpandedQuantizationTests.cs:95-193: block size fixed at 32; data (n+1)/2 bytes, one scale (and min)
+    # per block, 4 high-bit bytes per block (Q5_0); the same input quantizes to the same bytes
+    n, nb = rows * cols, (rows * cols + 31) // 32
+    x = O.fill_normal(n, 11, 1.0)
+    t1, t2 = O.quantize(x, getattr(O, scheme), rows, cols, 32), O.quantize(x.copy(), getattr(O, scheme), rows, cols, 32)
+    assert t1.block_size == 32
+    if scheme == "Q4_1":
+        assert t1.data.size == (n + 1) // 2 and t1.scales.size == 2 * nb
+    else:
+        assert t1.data.size == (n + 1) // 2 + 4 * nb and t1.scales.size == nb
+    assert np.array_equal(t1.data, t2.data) and np.array_equal(t1.scales, t2.scales)
+    # the element formulas (Q4_1Tensor.cs:153-156, Q5_0Tensor.cs:157-172) from the packed fields
+    d = O.dequantize(t1).reshape(-1)
+    i = np.arange(n)
+    nib = np.where(i & 1, t1.data[i >> 1] >> 4, t1.data[i >> 1] & 0xF).astype(np.int64)
+    sc = t1.scales[i >> 5]
+    if scheme == "Q4_1":
+        want = (nib.astype(np.float32) * sc).astype(np.float32) + t1.scales[nb + (i >> 5)]
+    else:
+        hw = t1.data[(n + 1) // 2:].view(np.uint32).astype(np.int64)
+        q = (nib | (((hw[i >> 5] >> (i & 31)) & 1) << 4)) - 16
+        want = q.astype(np.float32) * sc
+    assert np.array_equal(d.view(np.uint32), want.astype(np.float32).view(np.uint32))
