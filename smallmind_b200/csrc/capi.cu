@@ -697,6 +697,15 @@ bool m1_supported(const sm_model* m) {
       if (!gemv1_supports(*L.w[r], c.hidden)) return false;
     if (!gemv1_supports(*L.w[SM_ROLE_WO], m->qd()) || !gemv1_supports(*L.w[SM_ROLE_W_DOWN], c.ffn_hidden))
       return false;
+    // one launch per Q|K|V and per gate|up: their formats must share a kernel
+    const int fq = L.w[SM_ROLE_WQ]->scheme, fk = L.w[SM_ROLE_WK]->scheme, fv = L.w[SM_ROLE_WV]->scheme;
+    int fa = fq, fb = fq;
+    for (int f : {fk, fv}) {
+      if (f == fa || f == fb) continue;
+      if (fb != fa) return false;
+      fb = f;
+    }
+    if (!gemv1_mix_ok(fa, fb) || L.w[SM_ROLE_W_GATE]->scheme != L.w[SM_ROLE_W_UP]->scheme) return false;
   }
   return gemv1_supports(*m->output, c.hidden);
 }

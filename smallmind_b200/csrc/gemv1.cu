@@ -186,6 +186,7 @@ bool gemv1_supports(const DevWeight& w, int K) {
   switch (w.scheme) {
     case SM_Q4_K: case SM_Q6_K: return (K & 255) == 0;
     case SM_Q8_0: case SM_Q4_0: return w.block_size % 32 == 0;
+    case SM_Q4_1: case SM_Q5_0: return w.aux_stride > 0;  // row-padded [scales | second] aux
     default: return false;
   }
 }
@@ -231,6 +232,8 @@ void* pick_kernel(int fa, int fb) {
       case SM_Q6_K: return (void*)gemv1_kernel<SM_Q6_K, SM_Q6_K, R>;
       case SM_Q8_0: return (void*)gemv1_kernel<SM_Q8_0, SM_Q8_0, R>;
       case SM_Q4_0: return (void*)gemv1_kernel<SM_Q4_0, SM_Q4_0, R>;
+      case SM_Q4_1: return (void*)gemv1_kernel<SM_Q4_1, SM_Q4_1, R>;
+      case SM_Q5_0: return (void*)gemv1_kernel<SM_Q5_0, SM_Q5_0, R>;
     }
   } else if (fa == SM_Q4_K && fb == SM_Q6_K) {
     return (void*)gemv1_kernel<SM_Q4_K, SM_Q6_K, R>;
@@ -238,6 +241,11 @@ void* pick_kernel(int fa, int fb) {
   return nullptr;
 }
 }  // namespace
+
+bool gemv1_mix_ok(int fa, int fb) {
+  if (fb == SM_Q4_K && fa == SM_Q6_K) std::swap(fa, fb);
+  return pick_kernel<4>(fa, fb) != nullptr;
+}
 
 int launch_gemv1(const GemvArgs& args, cudaStream_t st, int* n_launch) {
   GemvArgs a = args;

@@ -48,6 +48,8 @@ struct StreamArgs {
 int launch_gemv_stream(const GemvArgs& g, int* status, cudaStream_t st, int* n_launch);
 
 bool gemv1_supports(const DevWeight& w, int K);
+// true when one gemv1 launch can mix segments of formats fa and fb (fa == fb, or Q4_K with Q6_K)
+bool gemv1_mix_ok(int fa, int fb);
 int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y, int mode);
 int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch);
 // y[M][N] (+)= x[M][K] W^T on tcgen05 (INTENDED layout, M >= 16, K % 64 == 0)

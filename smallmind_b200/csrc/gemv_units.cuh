@@ -184,6 +184,73 @@ struct Unit<SM_Q4_0> {
   }
 };
 
+// Q4_1 / Q5_0: 32 nibbles (global-index order: even low) + fp32 scale and a
+// second per-block word in the row-padded aux (Q4_1: the min; Q5_0: the 32
+// fifth bits).  Q4_1: sum((sc u + mn) x) = 16 sc sum(f x) + (mn - 16 sc) sum(x),
+// f = 1 + u/16 (Q4_1Tensor.cs:153-156).  Q5_0: the fifth bit joins the nibble
+// in the byte, f = 1 + u5/32, sum(sc (u5 - 16) x) = sc (32 sum(f x) - 48 sum(x))
+// (Q5_0Tensor.cs:157-172).
+template <int FMT>
+struct Unit4150 {
+  struct Raw {
+    int4 q;
+    float sc;
+    uint32_t second;
+  };
+  __device__ __forceinline__ static void load(const GemvSeg& s, int row, int u, int K, Raw& r) {
+    const int64_t e0 = (int64_t)row * K + 32 * u, b = e0 >> 5;
+    r.q = __ldg((const int4*)(s.data + (e0 >> 1)));
+    r.sc = __ldg((const float*)s.aux + aux_idx(b, s.aux_bpr, s.aux_stride));
+    r.second = __ldg((const uint32_t*)s.aux + aux_second_idx(b, s.aux_bpr, s.aux_stride, 0));
+  }
+  __device__ __forceinline__ static void load_row(const GemvSeg& s, const uint8_t* rowp, int row, int u, int K,
+                                                  bool up, Raw& r) {
+    const int64_t b = ((int64_t)row * K >> 5) + u;
+    const void* aux = up ? s.aux2 : s.aux;
+    r.q = *(const int4*)(rowp + 16 * u);
+    r.sc = __ldg((const float*)aux + aux_idx(b, s.aux_bpr, s.aux_stride));
+    r.second = __ldg((const uint32_t*)aux + aux_second_idx(b, s.aux_bpr, s.aux_stride, 0));
+  }
+  // bits 0, 2, 4, 6 of h -> bit 6 of bytes 0..3
+  __device__ __forceinline__ static uint32_t spread_even(uint32_t h) {
+    uint32_t t = h & 0x55u;
+    t = (t | (t << 12)) & 0x00050005u;
+    t = (t | (t << 6)) & 0x01010101u;
+    return t << 6;
+  }
+  __device__ __forceinline__ static float dot(const Raw& r, int, const float* x, float x16a, float x16b) {
+    const uint32_t w[4] = {(uint32_t)r.q.x, (uint32_t)r.q.y, (uint32_t)r.q.z, (uint32_t)r.q.w};
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t tl, th;
+      if (FMT == SM_Q4_1) {
+        tl = ((w[i] << 3) & 0x78787878u) | 0x80808080u;
+        th = ((w[i] >> 1) & 0x78787878u) | 0x80808080u;
+      } else {
+        const uint32_t h = r.second >> (8 * i);
+        tl = ((w[i] << 2) & 0x3C3C3C3Cu) | spread_even(h) | 0x80808080u;
+        th = ((w[i] >> 2) & 0x3C3C3C3Cu) | spread_even(h >> 1) | 0x80808080u;
+      }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        a0 = fmaf(fbyte(tl, b), x[8 * i + 2 * b], a0);
+        a1 = fmaf(fbyte(th, b), x[8 * i + 2 * b + 1], a1);
+      }
+    }
+    const float sx = x16a + x16b;
+    if (FMT == SM_Q4_1) {
+      const float s16 = 16.f * r.sc;
+      return s16 * (a0 + a1) + (__uint_as_float(r.second) - s16) * sx;
+    }
+    return r.sc * (32.f * (a0 + a1) - 48.f * sx);
+  }
+};
+template <>
+struct Unit<SM_Q4_1> : Unit4150<SM_Q4_1> {};
+template <>
+struct Unit<SM_Q5_0> : Unit4150<SM_Q5_0> {};
+
 // Rows of group lg handled by this segment (GLU: R/2 gate rows then the same R/2 up rows).
 template <int R>
 __device__ __forceinline__ int group_row(const GemvSeg& s, int lg, int r) {

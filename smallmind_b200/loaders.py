@@ -472,8 +472,8 @@ def _rows(t: HostTensor, r0: int, r1: int) -> HostTensor:
 
 
 def _upload(ctx: CudaContext, t: HostTensor) -> CudaWeightTensor:
-    if t.scheme == QuantScheme.F32:
-        raise ValueError(f"{t.name}: F32 linear weights are not on the device path")
+    if t.scheme == QuantScheme.F32:  # F32 / F16 linear weights as fp32 rows (GgufImporter converts F16 to F32)
+        return CudaWeightTensor(ctx, QuantScheme.F32, t.rows, t.cols, t.data, None, 1)
     return CudaWeightTensor(ctx, t.scheme, t.rows, t.cols, t.data, t.scales, t.block_size or 32)
 
 

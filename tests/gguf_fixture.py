@@ -134,9 +134,14 @@ def ggml_dequant(ttype: int, raw: np.ndarray) -> np.ndarray:
     raise ValueError(ttype)
 
 
-def tiny_llama_gguf(path, cfg: dict, seed: int = 5):
-    """A LLaMA-shaped GGUF: Q4_K q/k/o/gate/up, Q6_K v/down/output, F32 norms,
-    F16 embedding.  Returns {name: (ggml type, raw bytes, ggml dims)}."""
+DEFAULT_TYPES = dict(q=Q4_K, k=Q4_K, v=Q6_K, o=Q4_K, gate=Q4_K, up=Q4_K, down=Q6_K, output=Q6_K)
+
+
+def tiny_llama_gguf(path, cfg: dict, seed: int = 5, types: dict | None = None):
+    """A LLaMA-shaped GGUF: by default Q4_K q/k/o/gate/up, Q6_K v/down/output
+    (``types`` overrides per role), F32 norms, F16 embedding.  Returns
+    {name: (ggml type, raw bytes, ggml dims)}."""
+    ty = dict(DEFAULT_TYPES, **(types or {}))
     rs = np.random.RandomState(seed)
     H, F, V = cfg["hidden"], cfg["ffn_hidden"], cfg["vocab_size"]
     qd, kd = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
@@ -151,8 +156,9 @@ def tiny_llama_gguf(path, cfg: dict, seed: int = 5):
     def add(name, ttype, rows, cols):
         if ttype == F32:
             raw = (1.0 + 0.05 * rs.randn(rows * cols)).astype(np.float32).view(np.uint8)
-        elif ttype == F16:
-            raw = (0.5 * rs.randn(rows * cols)).astype(np.float16).view(np.uint8)
+        elif ttype == F16:  # the embedding at 0.5, linear weights at 0.02
+            sd = 0.5 if name == "token_embd.weight" else 0.02
+            raw = (sd * rs.randn(rows * cols)).astype(np.float16).view(np.uint8)
         else:
             raw = random_blocks(ttype, rows * cols, rs)
         ts[name] = (ttype, raw, [cols] if rows == 1 else [cols, rows])
@@ -161,15 +167,15 @@ def tiny_llama_gguf(path, cfg: dict, seed: int = 5):
     for l in range(cfg["n_layers"]):
         p = f"blk.{l}."
         add(p + "attn_norm.weight", F32, 1, H)
-        add(p + "attn_q.weight", Q4_K, qd, H)
-        add(p + "attn_k.weight", Q4_K, kd, H)
-        add(p + "attn_v.weight", Q6_K, kd, H)
-        add(p + "attn_output.weight", Q4_K, H, qd)
+        add(p + "attn_q.weight", ty["q"], qd, H)
+        add(p + "attn_k.weight", ty["k"], kd, H)
+        add(p + "attn_v.weight", ty["v"], kd, H)
+        add(p + "attn_output.weight", ty["o"], H, qd)
         add(p + "ffn_norm.weight", F32, 1, H)
-        add(p + "ffn_gate.weight", Q4_K, F, H)
-        add(p + "ffn_up.weight", Q4_K, F, H)
-        add(p + "ffn_down.weight", Q6_K, H, F)
+        add(p + "ffn_gate.weight", ty["gate"], F, H)
+        add(p + "ffn_up.weight", ty["up"], F, H)
+        add(p + "ffn_down.weight", ty["down"], H, F)
     add("output_norm.weight", F32, 1, H)
-    add("output.weight", Q6_K, V, H)
+    add("output.weight", ty["output"], V, H)
     write_gguf(path, meta, [(n, dims, t, raw) for n, (t, raw, dims) in ts.items()])
     return ts

@@ -36,12 +36,19 @@ def _oracle_model(O, L, tensors, cfg):
                        q(tensors["output.weight"]), layers)
 
 
-@pytest.mark.parametrize("via", ["gguf", "smq"])
-def test_file_model_greedy_matches_oracle(ctx, O, tmp_path, via):
+TYPES = {"kquant": None,
+         "q4_1": dict(q=G.Q4_1, k=G.Q4_1, v=G.Q4_1, o=G.Q4_1, gate=G.Q4_1, up=G.Q4_1, down=G.Q4_1, output=G.Q4_1),
+         "q5_0": dict(q=G.Q5_0, k=G.Q5_0, v=G.Q5_0, o=G.Q5_0, gate=G.Q5_0, up=G.Q5_0, down=G.Q5_0, output=G.Q5_0),
+         "mixed": dict(q=G.Q5_0, k=G.Q5_0, v=G.Q8_0, o=G.F16, gate=G.Q4_1, up=G.Q4_1, down=G.Q5_0, output=G.Q4_0)}
+
+
+@pytest.mark.parametrize("via,types", [("gguf", "kquant"), ("smq", "kquant"), ("gguf", "q4_1"), ("smq", "q5_0"),
+                                       ("gguf", "mixed"), ("smq", "mixed")])
+def test_file_model_greedy_matches_oracle(ctx, O, tmp_path, via, types):
     import smallmind_b200 as sm
     from smallmind_b200 import loaders as L
     gp = tmp_path / "tiny.gguf"
-    G.tiny_llama_gguf(gp, CFG)
+    G.tiny_llama_gguf(gp, CFG, types=TYPES[types])
     g = L.gguf_read(gp)
     tensors = {t.name: L.gguf_tensor_to_host(g, t) for t in g.tensors}
     if via == "gguf":
