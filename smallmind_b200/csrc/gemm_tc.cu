@@ -113,6 +113,37 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Packed bytes of one unit, loaded ahead of their decode (register prefetch).
+// Q4_K: a = block header, b = the unit's 16 code bytes.  Q6_K: a = ql, b.xy =
+// high plane words, b.z = the two int8 scales, b.w = d bits.  Q8_0: a, b = 32
+// codes, s = scale.  Q4_0: a = 16 code bytes, s = scale.  Q4_1 / Q5_0: a = 16
+// code bytes, s = scale, b.x = the block's min (Q4_1) or high-bit word (Q5_0).
+struct RawUnit {
+  uint4 a, b;
+  float s;
+};
+
+__device__ __forceinline__ void load_raw41_50(const DevWeight& W, int n, int k0, int K, RawUnit& r) {
+  const int64_t i0 = (int64_t)n * K + k0, b = i0 >> 5;
+  r.a = __ldg((const uint4*)((const uint8_t*)W.data + (i0 >> 1)));
+  r.s = __ldg((const float*)W.aux + aux_idx(b, W.aux_bpr, W.aux_stride));
+  r.b.x = __ldg((const uint32_t*)W.aux + aux_second_idx(b, W.aux_bpr, W.aux_stride, (W.n + 31) / 32));
+}
+
+// Q4_1Tensor.cs:153-156 (q * scale + min) and Q5_0Tensor.cs:157-172 ((low | high << 4) - 16, times scale)
+__device__ __forceinline__ void decode_raw41_50(int scheme, const RawUnit& r, float (&w)[32]) {
+  const uint32_t qw[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const uint32_t b = (qw[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+    const int nib = (e & 1) ? (int)(b >> 4) : (int)(b & 0xF);
+    if (scheme == SM_Q4_1)
+      w[e] = __fadd_rn(__fmul_rn((float)nib, r.s), __uint_as_float(r.b.x));
+    else
+      w[e] = __fmul_rn((float)((nib | (int)(((r.b.x >> e) & 1u) << 4)) - 16), r.s);
+  }
+}
+
 // ---------------------------------------------------------------- weight unit -> 32 fp32 values
 // Elements k0 .. k0 + 31 (k0 % 32 == 0) of weight row n, exactly as the
 // reference element formulas produce them.
@@ -191,6 +222,13 @@ __device__ __forceinline__ void weight_unit(const DevWeight& W, int n, int k0, i
       }
       break;
     }
+    case SM_Q4_1:
+    case SM_Q5_0: {
+      RawUnit r;
+      load_raw41_50(W, n, k0, K, r);
+      decode_raw41_50(W.scheme, r, w);
+      break;
+    }
     default: {  // F32
       const float4* src = (const float4*)((const float*)W.data + (int64_t)n * K + k0);
 #pragma unroll
@@ -205,17 +243,8 @@ __device__ __forceinline__ void weight_unit(const DevWeight& W, int n, int k0, i
   }
 }
 
-// Packed bytes of one unit, loaded ahead of their decode (register prefetch).
-// Q4_K: a = block header, b = the unit's 16 code bytes.  Q6_K: a = ql, b.xy =
-// high plane words, b.z = the two int8 scales, b.w = d bits.  Q8_0: a, b = 32
-// codes, s = scale.  Q4_0: a = 16 code bytes, s = scale.
-struct RawUnit {
-  uint4 a, b;
-  float s;
-};
-
 __device__ __forceinline__ bool raw_prefetchable(const DevWeight& W) {
-  return W.scheme == SM_Q4_K || W.scheme == SM_Q6_K ||
+  return W.scheme == SM_Q4_K || W.scheme == SM_Q6_K || W.scheme == SM_Q4_1 || W.scheme == SM_Q5_0 ||
          ((W.scheme == SM_Q8_0 || W.scheme == SM_Q4_0) && W.block_size % 32 == 0);
 }
 
@@ -247,6 +276,10 @@ __device__ __forceinline__ void load_raw(const DevWeight& W, int n, int k0, int 
       r.s = __ldg((const float*)W.aux + aux_idx(i0 / W.block_size, W.aux_bpr, W.aux_stride));
       break;
     }
+    case SM_Q4_1:
+    case SM_Q5_0:
+      load_raw41_50(W, n, k0, K, r);
+      break;
     default: {  // Q4_0
       const int64_t i0 = (int64_t)n * K + k0;
       r.a = __ldg((const uint4*)((const uint8_t*)W.data + (i0 >> 1)));
@@ -299,6 +332,10 @@ __device__ __forceinline__ void decode_raw(int scheme, int k0, const RawUnit& r,
       for (int e = 0; e < 32; ++e) w[e] = __fmul_rn((float)(int8_t)((vw[e >> 2] >> (8 * (e & 3))) & 0xFF), r.s);
       break;
     }
+    case SM_Q4_1:
+    case SM_Q5_0:
+      decode_raw41_50(scheme, r, w);
+      break;
     default: {  // Q4_0
       const uint32_t qw[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
 #pragma unroll
@@ -624,6 +661,8 @@ bool gemm_tc_supports(const DevWeight& W, int M) {
     case SM_Q8_0:
     case SM_Q4_0:
       return W.block_size > 0;
+    case SM_Q4_1:
+    case SM_Q5_0:
     case SM_F32:
       return true;
   }

@@ -29,7 +29,7 @@ def test_dequant_bit_exact(ctx, O, scheme, rows, cols):
 
 
 @pytest.mark.parametrize("scheme", ["Q4_1", "Q5_0"])
-@pytest.mark.parametrize("m", [1, 2, 5, 16, 33])
+@pytest.mark.parametrize("m", [1, 2, 5, 16, 33, 160])
 @pytest.mark.parametrize("rows,cols", [(200, 1024), (37, 96), (19, 40)])
 def test_matmul_intended_vs_oracle(ctx, O, scheme, m, rows, cols):
     import smallmind_b200 as sm
