@@ -219,6 +219,19 @@ SM_API int sm_kv_destroy(sm_kv* kv);
 /* InferenceSession.ResetKVCache (InferenceSession.cs:485-526): length of seq -> 0. */
 SM_API int sm_kv_reset(sm_kv* kv, int seq_id);
 SM_API int sm_kv_length(sm_kv* kv, int seq_id, int* len);
+/* Keep the first len tokens of seq_id (0 <= len <= current length): the cached
+ * prefix that a new prompt shares (ChatSession.cs:282-300 reuses the cache when
+ * the longest common prefix covers it; this also keeps a partial prefix). */
+SM_API int sm_kv_truncate(sm_kv* kv, int seq_id, int len);
+/* KvCacheEntry.Slide (KvCacheEntry.cs:203-229): keep the last `window` tokens,
+ * moved to positions 0 .. window-1 of every layer; no-op when window >= length;
+ * window < 0 is an error.  Cached keys keep the rotation of their old positions,
+ * as in the reference. */
+SM_API int sm_kv_slide(sm_kv* kv, int seq_id, int window);
+/* KvCacheEntry.GetKeys / GetValues (KvCacheEntry.cs:155-189): tokens [start,
+ * start + count) of one layer, into host arrays laid out [token][kv_head][head_dim]
+ * (either may be NULL); the range must lie inside the cached tokens. */
+SM_API int sm_kv_read(sm_kv* kv, int layer, int seq_id, int start, int count, float* keys, float* values);
 
 /* Prefill: TransformerModel.Forward(idx[1,T], positionOffset = current length)
  * (TransformerModel.cs:272-344) appending T tokens to seq_id's cache; writes the

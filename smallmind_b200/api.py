@@ -264,6 +264,22 @@ class KVCache:
         L.check(L.lib().sm_kv_length(self.handle, seq, C.byref(v)), "sm_kv_length")
         return v.value
 
+    def truncate(self, seq: int, length: int):
+        """Keep the first ``length`` cached tokens of ``seq``."""
+        L.check(L.lib().sm_kv_truncate(self.handle, seq, length), "sm_kv_truncate")
+
+    def slide(self, seq: int, window: int):
+        """KvCacheEntry.Slide: keep the last ``window`` tokens, moved to the front."""
+        L.check(L.lib().sm_kv_slide(self.handle, seq, window), "sm_kv_slide")
+
+    def read(self, layer: int, seq: int, start: int, count: int):
+        """KvCacheEntry.GetKeys / GetValues: (keys, values), each [count, n_kv_heads * head_dim]."""
+        width = self.model.cfg["n_kv_heads"] * self.model.cfg["head_dim"]
+        k = np.empty((count, width), np.float32)
+        v = np.empty((count, width), np.float32)
+        L.check(L.lib().sm_kv_read(self.handle, layer, seq, start, count, _p(k), _p(v)), "sm_kv_read")
+        return k, v
+
     def prefill(self, seq: int, tokens, want_logits: bool = True):
         toks = np.ascontiguousarray(tokens, np.int32)
         logits = np.empty(self.model.cfg["vocab_size"], np.float32) if want_logits else None
@@ -306,6 +322,61 @@ class InferenceSession:
         out, all_logits = [nxt], [logits] if return_logits else []
         for _ in range(max_new_tokens - 1):
             t, lg = self.kv.decode([self.seq], [out[-1]], want_logits=return_logits)
+            out.append(int(t[0]))
+            if return_logits:
+                all_logits.append(lg[0])
+        return (out, all_logits) if return_logits else out
+
+
+def longest_common_prefix(previous, current) -> int:
+    """ChatSession.CalculateLongestCommonPrefix (ChatSession.cs:1368-1383)."""
+    n = 0
+    for a, b in zip(previous, current):
+        if a != b:
+            break
+        n += 1
+    return n
+
+
+class ChatSession:
+    """Multi-turn greedy generation over one KV slot with prefix reuse.
+
+    The reference (ChatSession.cs:270-312, 398-403) keeps a session's KV cache
+    between turns and, when the new prompt's longest common prefix with the
+    cached tokens covers the whole cache, prefills only the new tokens;
+    otherwise it resets and prefills everything.  Here the cached tokens are
+    tracked exactly (the prompt plus every generated token fed back), and a
+    partial match keeps the shared prefix (``sm_kv_truncate``) instead of
+    resetting.  At least one prompt token is always prefilled, so the last
+    position's logits exist.  Counters mirror the reference's cache statistics.
+    """
+
+    def __init__(self, kv: KVCache, seq: int = 0, reuse: bool = True):
+        self.kv, self.seq, self.reuse = kv, seq, reuse
+        self.cached: list[int] = []
+        self.kv_cache_hits = 0
+        self.kv_cache_misses = 0
+        self.tokens_from_cache = 0
+        kv.reset(seq)
+
+    def generate(self, prompt_ids, max_new_tokens: int, return_logits: bool = False):
+        prompt = [int(t) for t in prompt_ids]
+        keep = 0
+        if self.reuse and self.cached:
+            keep = min(longest_common_prefix(self.cached, prompt), len(prompt) - 1)
+        if keep > 0:
+            self.kv_cache_hits += 1
+            self.tokens_from_cache += keep
+            self.kv.truncate(self.seq, keep)
+        else:
+            self.kv_cache_misses += 1
+            self.kv.reset(self.seq)
+        nxt, logits = self.kv.prefill(self.seq, np.asarray(prompt[keep:], np.int32), want_logits=return_logits)
+        self.cached = prompt[:]
+        out, all_logits = [nxt], [logits] if return_logits else []
+        for _ in range(max_new_tokens - 1):
+            t, lg = self.kv.decode([self.seq], [out[-1]], want_logits=return_logits)
+            self.cached.append(out[-1])
             out.append(int(t[0]))
             if return_logits:
                 all_logits.append(lg[0])

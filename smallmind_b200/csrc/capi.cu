@@ -1194,6 +1194,96 @@ SM_API int sm_kv_reset(sm_kv* kv, int seq) {
   return SM_OK;
 }
 
+// KvCacheEntry.Slide (KvCacheEntry.cs:203-229): positions [start, start + keep)
+// move to [0, keep) in every layer and KV head, K and V.  One CTA per (head,
+// K|V, layer) walks the run front to back in chunks of at most `start` tokens,
+// so a chunk's source never overlaps its destination or a later chunk's source.
+__global__ void kv_slide_kernel(float* k, float* v, size_t layer_stride, int seq, int n_kv, int max_tokens, int hd,
+                                int start, int keep) {
+  float* base = (blockIdx.y ? v : k) + layer_stride * blockIdx.z + ((size_t)seq * n_kv + blockIdx.x) * max_tokens * hd;
+  const int step = min(start, 64);
+  for (int t0 = 0; t0 < keep; t0 += step) {
+    const int n = min(step, keep - t0) * hd / 4;
+    const float4* src = (const float4*)(base + (size_t)(t0 + start) * hd);
+    float4* dst = (float4*)(base + (size_t)t0 * hd);
+    float4 tmp[4];
+    for (int i0 = 0; i0 < n; i0 += 4 * blockDim.x) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * blockDim.x + threadIdx.x;
+        if (i < n) tmp[j] = src[i];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * blockDim.x + threadIdx.x;
+        if (i < n) dst[i] = tmp[j];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+static int kv_set_length(sm_kv* kv, int seq, int len) {
+  kv->len_host[seq] = len;
+  SM_CUDA_TRY(cudaMemcpyAsync(kv->len_dev + seq, &len, sizeof(int), cudaMemcpyHostToDevice, kv->m->ctx->stream));
+  SM_CUDA_TRY(cudaStreamSynchronize(kv->m->ctx->stream));
+  return SM_OK;
+}
+
+SM_API int sm_kv_truncate(sm_kv* kv, int seq, int len) {
+  if (!kv) return fail(SM_ERR_INVALID_ARG, "null kv");
+  if (seq < 0 || seq >= kv->max_seqs) return fail(SM_ERR_INVALID_ARG, "kv_truncate: bad sequence id");
+  DeviceGuard g(kv->m->ctx->device);
+  SM_TRY(kv_sync_host(kv));
+  if (len < 0 || len > kv->len_host[seq]) return fail(SM_ERR_SHAPE, "kv_truncate: length outside [0, current length]");
+  return kv_set_length(kv, seq, len);
+}
+
+SM_API int sm_kv_slide(sm_kv* kv, int seq, int window) {
+  if (!kv) return fail(SM_ERR_INVALID_ARG, "null kv");
+  if (seq < 0 || seq >= kv->max_seqs) return fail(SM_ERR_INVALID_ARG, "kv_slide: bad sequence id");
+  // KvCacheEntry.cs:205-206
+  if (window < 0) return fail(SM_ERR_INVALID_ARG, "kv_slide: window must be non-negative");
+  DeviceGuard g(kv->m->ctx->device);
+  SM_TRY(kv_sync_host(kv));
+  const int cur = kv->len_host[seq];
+  if (window >= cur) return SM_OK;  // nothing to slide (KvCacheEntry.cs:208-209)
+  const auto& c = kv->m->cfg;
+  if (window > 0) {
+    if (c.head_dim % 4) return fail(SM_ERR_UNSUPPORTED, "kv_slide: head_dim must be a multiple of 4");
+    dim3 grid(c.n_kv_heads, 2, c.n_layers);
+    kv_slide_kernel<<<grid, 256, 0, kv->m->ctx->stream>>>(kv->k, kv->v, kv->layer_stride(), seq, c.n_kv_heads,
+                                                         kv->max_tokens, c.head_dim, cur - window, window);
+    SM_CUDA_TRY(cudaGetLastError());
+  }
+  return kv_set_length(kv, seq, window);
+}
+
+SM_API int sm_kv_read(sm_kv* kv, int layer, int seq, int start, int count, float* keys, float* values) {
+  if (!kv || (!keys && !values)) return fail(SM_ERR_INVALID_ARG, "kv_read: null argument");
+  const auto& c = kv->m->cfg;
+  if (layer < 0 || layer >= c.n_layers) return fail(SM_ERR_INVALID_ARG, "kv_read: bad layer");
+  if (seq < 0 || seq >= kv->max_seqs) return fail(SM_ERR_INVALID_ARG, "kv_read: bad sequence id");
+  DeviceGuard g(kv->m->ctx->device);
+  SM_TRY(kv_sync_host(kv));
+  // KvCacheEntry.GetKeys / GetValues (KvCacheEntry.cs:155-189): the range must lie inside the cached tokens
+  if (start < 0 || count < 0 || start + count > kv->len_host[seq]) return fail(SM_ERR_SHAPE, "kv_read: range outside the cached tokens");
+  if (count == 0) return SM_OK;
+  cudaStream_t st = kv->m->ctx->stream;
+  const size_t hd = c.head_dim, row = hd * sizeof(float);
+  for (int which = 0; which < 2; ++which) {
+    float* out = which ? values : keys;
+    if (!out) continue;
+    const float* base = (which ? kv->v : kv->k) + kv->layer_stride() * layer;
+    for (int h = 0; h < c.n_kv_heads; ++h) {
+      const float* src = base + (((size_t)seq * c.n_kv_heads + h) * kv->max_tokens + start) * hd;
+      SM_CUDA_TRY(cudaMemcpy2DAsync(out + h * hd, row * c.n_kv_heads, src, row, row, count, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  SM_CUDA_TRY(cudaStreamSynchronize(st));
+  return SM_OK;
+}
+
 SM_API int sm_kv_length(sm_kv* kv, int seq, int* len) {
   if (!kv || !len) return fail(SM_ERR_INVALID_ARG, "null argument");
   if (seq < 0 || seq >= kv->max_seqs) return fail(SM_ERR_INVALID_ARG, "kv_length: bad sequence id");
