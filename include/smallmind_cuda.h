@@ -247,6 +247,40 @@ SM_API int sm_prefill(sm_model* m, sm_kv* kv, int seq_id, const int* tokens, int
 SM_API int sm_decode(sm_model* m, sm_kv* kv, const int* seq_ids, const int* tokens, int n, float* logits,
                      int* next_tokens, int flags);
 
+/* Sampling options of InferenceSession's pipeline (InferenceSession.cs:565-606).
+ * Disabled values: temperature 1, top_k <= 0, top_p >= 1, min_p <= 0,
+ * repetition_penalty 1, presence / frequency penalty 0.  repetition_window 0
+ * means min(context length, 256) (:780-783). */
+typedef struct sm_sampling_params {
+  double temperature;
+  int top_k;
+  double top_p;
+  double min_p;
+  float repetition_penalty;
+  float presence_penalty;
+  float frequency_penalty;
+  int repetition_window;
+} sm_sampling_params;
+
+#define SM_SAMPLE_MAX_VOCAB 53248
+
+/* One token per logits row through the reference sampling pipeline, on the
+ * device (replaces InferenceSession.SampleNextToken's host stages: penalties
+ * :769-850, temperature :741-763, top-k :635-670, softmax :672-712, top-p
+ * :862-907, min-p :913-935, SampleFromProbs :714-734).
+ * logits [n_rows][vocab] (vocab <= SM_SAMPLE_MAX_VOCAB); targets[n_rows] are the
+ * uniform draws in [0, 1) that SampleFromProbs compares the cumulative sum with
+ * (the reference takes them from DeterministicRng.NextDouble); context
+ * [n_rows][context_stride] with context_lens[n_rows] are each row's token history
+ * for the penalties (NULL when no penalty is set; ids outside [0, vocab) are
+ * skipped).  tokens[n_rows] receives the samples; probs (may be NULL)
+ * [n_rows][vocab] the final distribution.  flags: SM_PTR_HOST (all arrays host,
+ * synchronous) or SM_PTR_DEVICE (all arrays device; stream-ordered, no
+ * allocation). */
+SM_API int sm_sample(sm_ctx* ctx, const float* logits, int n_rows, int vocab, const sm_sampling_params* params,
+                     const int* context, const int* context_lens, int context_stride, const double* targets,
+                     int* tokens, float* probs, int flags);
+
 /* Number of kernels the library launched on this context so far (evidence
  * counter for benchmarks). */
 SM_API int sm_ctx_launch_count(sm_ctx* ctx, int64_t* out);

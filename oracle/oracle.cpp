@@ -847,6 +847,130 @@ static inline uint64_t splitmix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
+// ---------------------------------------------------------------- sampling
+// NormalizeProbabilities (InferenceSession.cs:982-1031): Vector<float> lane sums
+// (8 lanes), horizontal sum, remainder, then multiply by 1 / sum.
+static void or_normalize(float* p, int V) {
+  float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int i = 0;
+  for (; i + 8 <= V; i += 8)
+    for (int j = 0; j < 8; ++j) lanes[j] += p[i + j];
+  float sum = 0.f;
+  for (int j = 0; j < 8; ++j) sum += lanes[j];
+  for (; i < V; ++i) sum += p[i];
+  if (sum > 0.f) {
+    const float inv = 1.0f / sum;
+    for (int k = 0; k < V; ++k) p[k] *= inv;
+  }
+}
+
+int or_sample(float* L, int V, double temperature, int top_k, double top_p, double min_p, float rep_penalty,
+              float presence_penalty, float frequency_penalty, int rep_window, const int* context, int ctx_len,
+              double target, float* probs_out) {
+  // 1. penalties (InferenceSession.cs:769-850): distinct tokens of the window, first-seen order, with counts
+  if (!(rep_penalty == 1.0f && presence_penalty == 0.0f && frequency_penalty == 0.0f)) {
+    const int win = rep_window > 0 ? rep_window : std::min(ctx_len, 256);
+    const int start = std::max(0, ctx_len - win);
+    std::vector<int> ids, counts;
+    for (int i = start; i < ctx_len; ++i) {
+      const int t = context[i];
+      int f = -1;
+      for (size_t j = 0; j < ids.size(); ++j)
+        if (ids[j] == t) { f = (int)j; break; }
+      if (f >= 0) ++counts[f];
+      else { ids.push_back(t); counts.push_back(1); }
+    }
+    for (size_t j = 0; j < ids.size(); ++j) {
+      float& x = L[ids[j]];
+      if (rep_penalty != 1.0f) x = x > 0 ? x / rep_penalty : x * rep_penalty;
+      if (presence_penalty != 0.0f) x -= presence_penalty;
+      if (frequency_penalty != 0.0f) x -= (float)counts[j] * frequency_penalty;
+    }
+  }
+  // 2. temperature (:741-763)
+  if (temperature != 1.0) {
+    const float inv = 1.0f / (float)temperature;
+    for (int i = 0; i < V; ++i) L[i] *= inv;
+  }
+  // 3. top-k (:635-670): the k-th largest value of a descending sort; values below it -> -inf
+  if (top_k > 0 && top_k < V) {
+    std::vector<float> s(L, L + V);
+    std::sort(s.begin(), s.end(), [](float a, float b) { return a > b; });
+    const float kth = s[std::min(top_k - 1, V - 1)];
+    for (int i = 0; i < V; ++i)
+      if (!(L[i] >= kth)) L[i] = -INFINITY;
+  }
+  // 4. softmax (:672-712)
+  std::vector<float> p(V);
+  float mx = -INFINITY;
+  for (int i = 0; i < V; ++i)
+    if (L[i] != -INFINITY) mx = std::max(mx, L[i]);
+  float sum = 0.f;
+  for (int i = 0; i < V; ++i) {
+    if (L[i] != -INFINITY) {
+      p[i] = std::exp(L[i] - mx);
+      sum += p[i];
+    } else {
+      p[i] = 0.f;
+    }
+  }
+  if (sum > 0)
+    for (int i = 0; i < V; ++i) p[i] /= sum;
+  // 5. top-p (:862-907): descending order (ties by index here; the reference's sort leaves them unspecified)
+  if (top_p < 1.0) {
+    std::vector<int> idx(V);
+    for (int i = 0; i < V; ++i) idx[i] = i;
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return p[a] > p[b]; });
+    float cum = 0.f;
+    int cut = V;
+    for (int i = 0; i < V; ++i) {
+      cum += p[idx[i]];
+      if ((double)cum >= top_p) { cut = i + 1; break; }
+    }
+    for (int i = cut; i < V; ++i) p[idx[i]] = 0.f;
+    or_normalize(p.data(), V);
+  }
+  // 6. min-p (:913-935)
+  if (min_p > 0.0) {
+    float mp = -INFINITY;
+    for (int i = 0; i < V; ++i) mp = std::max(mp, p[i]);
+    const float thr = mp * (float)min_p;
+    for (int i = 0; i < V; ++i)
+      if (p[i] < thr) p[i] = 0.f;
+    or_normalize(p.data(), V);
+  }
+  if (probs_out) std::memcpy(probs_out, p.data(), sizeof(float) * V);
+  // 7. SampleFromProbs (:714-734)
+  double cum = 0.0;
+  for (int i = 0; i < V; ++i) {
+    cum += p[i];
+    if (cum >= target) return i;
+  }
+  return V - 1;
+}
+
+// DeterministicRng.cs: SplitMix64 seeding, xoroshiro128+ (rotations 24 / 16 / 37), 53-bit doubles
+void or_deterministic_rng_doubles(int32_t seed, int n, double* out) {
+  uint64_t s = (uint64_t)(int64_t)seed;
+  auto splitmix = [&]() {
+    s += 0x9e3779b97f4a7c15ULL;
+    uint64_t z = s;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+  };
+  uint64_t s0 = splitmix(), s1 = splitmix();
+  if (s0 == 0 && s1 == 0) s0 = s1 = 1;
+  auto rotl = [](uint64_t x, int k) { return (x << k) | (x >> (64 - k)); };
+  for (int i = 0; i < n; ++i) {
+    const uint64_t r = s0 + s1;
+    s1 ^= s0;
+    s0 = rotl(s0, 24) ^ s1 ^ (s1 << 16);
+    s1 = rotl(s1, 37);
+    out[i] = (double)(r & ((1ULL << 53) - 1)) * (1.0 / (double)(1ULL << 53));
+  }
+}
+
 void or_fill_normal(float* out, int64_t n, uint64_t seed, float std_dev, int n_threads) {
   int chunks = std::max(1, n_threads);
   parallel_for(chunks, chunks, [&](int c) {

@@ -131,6 +131,22 @@ int or_model_forward(const or_model* m, const int* tokens, int T, int n_last, fl
  * for past positions so each new token costs one row.  kv: [layers][2][max_ctx][n_kv*hd]. */
 int or_model_step(const or_model* m, float* kv, int pos, const int* tokens, int T, float* last_logits, int n_threads);
 
+/* One token from one logits row through the reference sampling pipeline
+ * (InferenceSession.cs:565-606): repetition / presence / frequency penalties
+ * over the context window (:769-850), temperature (:741-763), top-k (:635-670),
+ * softmax (:672-712), top-p (:862-907), min-p (:913-935), then the first index
+ * whose double cumulative probability reaches `target` (:714-734), `target`
+ * being the caller's uniform draw.  logits is modified in place; probs_out
+ * (may be NULL) receives the final distribution.  Disabled values:
+ * temperature 1, top_k <= 0, top_p >= 1, min_p <= 0, penalties 1 / 0 / 0. */
+int or_sample(float* logits, int V, double temperature, int top_k, double top_p, double min_p, float rep_penalty,
+              float presence_penalty, float frequency_penalty, int rep_window, const int* context, int ctx_len,
+              double target, float* probs_out);
+
+/* DeterministicRng (src/SmallMind.Core/Rng/DeterministicRng.cs): SplitMix64-seeded
+ * xoroshiro128+; writes n NextDouble() draws. */
+void or_deterministic_rng_doubles(int32_t seed, int n, double* out);
+
 /* synthetic weights: N(0, std) from a counter-based generator (SplitMix64 + Box-Muller) */
 void or_fill_normal(float* out, int64_t n, uint64_t seed, float std_dev, int n_threads);
 

@@ -97,6 +97,8 @@ def _declare(L):
         "or_model_forward": (i, [C.POINTER(Model), vp, i, i, vp, i]),
         "or_model_step": (i, [C.POINTER(Model), vp, i, vp, i, vp, i]),
         "or_fill_normal": (None, [vp, i64, C.c_uint64, f, i]),
+        "or_sample": (i, [vp, i, C.c_double, i, C.c_double, C.c_double, f, f, f, i, vp, i, C.c_double, vp]),
+        "or_deterministic_rng_doubles": (None, [C.c_int32, i, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -362,3 +364,23 @@ class KVDecoder:
             raise ValueError(f"or_model_step rc={rc}")
         self.pos += toks.size
         return out
+
+
+# ---------------------------------------------------------------- sampling
+def sample(logits: np.ndarray, target: float, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+           min_p: float = 0.0, repetition_penalty: float = 1.0, presence_penalty: float = 0.0,
+           frequency_penalty: float = 0.0, repetition_window: int = 0, context=()):
+    """(token, probs) of one row through the reference sampling pipeline (or_sample)."""
+    lg = np.array(logits, np.float32).reshape(-1)
+    ctx = np.ascontiguousarray(np.asarray(context, np.int32).reshape(-1))
+    probs = np.empty_like(lg)
+    t = lib().or_sample(_p(lg), lg.size, temperature, top_k, top_p, min_p, repetition_penalty, presence_penalty,
+                        frequency_penalty, repetition_window, _p(ctx) if ctx.size else None, ctx.size, target,
+                        _p(probs))
+    return t, probs
+
+
+def deterministic_rng_doubles(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float64)
+    lib().or_deterministic_rng_doubles(seed, n, _p(out))
+    return out

@@ -6,11 +6,11 @@ compute path.
 """
 from ._lib import (LAYOUT_INTENDED, LAYOUT_REFERENCE, PTR_DEVICE, PTR_HOST, ShapeError, SmallMindCudaError,
                    last_error, lib)
-from .api import (ChatSession, CudaContext, CudaModel, CudaWeightTensor, InferenceSession, KVCache, QuantScheme,
-                  attention, longest_common_prefix, rmsnorm, rope, silu_mul)
+from .api import (ChatSession, CudaContext, CudaModel, CudaWeightTensor, DeterministicRng, InferenceSession, KVCache,
+                  QuantScheme, SamplingOptions, attention, longest_common_prefix, rmsnorm, rope, sample, silu_mul)
 
 __all__ = [
-    "ChatSession", "longest_common_prefix", "CudaContext", "CudaModel", "CudaWeightTensor", "InferenceSession", "KVCache", "QuantScheme", "attention",
+    "ChatSession", "longest_common_prefix", "DeterministicRng", "SamplingOptions", "sample", "CudaContext", "CudaModel", "CudaWeightTensor", "InferenceSession", "KVCache", "QuantScheme", "attention",
     "rmsnorm", "rope", "silu_mul", "LAYOUT_INTENDED", "LAYOUT_REFERENCE", "PTR_HOST", "PTR_DEVICE", "ShapeError",
     "SmallMindCudaError", "last_error", "lib",
 ]

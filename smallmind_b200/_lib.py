@@ -30,6 +30,16 @@ class ModelConfig(C.Structure):
     ]
 
 
+class SamplingParams(C.Structure):
+    """sm_sampling_params (include/smallmind_cuda.h)."""
+    _fields_ = [("temperature", C.c_double), ("top_k", C.c_int), ("top_p", C.c_double), ("min_p", C.c_double),
+                ("repetition_penalty", C.c_float), ("presence_penalty", C.c_float),
+                ("frequency_penalty", C.c_float), ("repetition_window", C.c_int)]
+
+
+SAMPLE_MAX_VOCAB = 53248
+
+
 # name -> (restype, argtypes); every symbol declared in include/smallmind_cuda.h
 vp, i, i64, f, sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 PP = C.POINTER(C.c_void_p)
@@ -43,6 +53,7 @@ SIGNATURES = {
     "sm_stream_sync": (i, [vp]),
     "sm_ctx_device_status": (i, [vp]),
     "sm_ctx_launch_count": (i, [vp, C.POINTER(C.c_int64)]),
+    "sm_sample": (i, [vp, vp, i, i, C.POINTER(SamplingParams), vp, vp, i, vp, vp, vp, i]),
     "sm_weight_upload": (i, [vp, i, i, i, i, vp, sz, vp, sz, i, PP]),
     "sm_weight_upload_device": (i, [vp, i, i, i, i, vp, sz, vp, sz, i, PP]),
     "sm_weight_destroy": (i, [vp]),

@@ -13,6 +13,7 @@ Everything runs in libsmallmind_cuda.so; there is no CPU path.
 from __future__ import annotations
 
 import ctypes as C
+from dataclasses import dataclass
 from enum import IntEnum
 
 import numpy as np
@@ -310,11 +311,115 @@ class KVCache:
             self.handle = None
 
 
+@dataclass
+class SamplingOptions:
+    """The sampling fields of the reference's ProductionInferenceOptions as
+    InferenceSession.SampleNextToken reads them (InferenceSession.cs:565-606).
+    ``seed`` set: targets come from DeterministicRng(seed) (:104-105)."""
+    temperature: float = 1.0
+    top_k: int = 0
+    top_p: float = 1.0
+    min_p: float = 0.0
+    repetition_penalty: float = 1.0
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repetition_window: int = 0
+    seed: int | None = None
+
+    def params(self) -> L.SamplingParams:
+        return L.SamplingParams(self.temperature, self.top_k, self.top_p, self.min_p, self.repetition_penalty,
+                                self.presence_penalty, self.frequency_penalty, self.repetition_window)
+
+    @property
+    def penalized(self) -> bool:
+        return not (self.repetition_penalty == 1.0 and self.presence_penalty == 0.0 and self.frequency_penalty == 0.0)
+
+
+class DeterministicRng:
+    """DeterministicRng (src/SmallMind.Core/Rng/DeterministicRng.cs): SplitMix64
+    seeding of a xoroshiro128+ generator; NextDouble keeps 53 bits."""
+    _M = (1 << 64) - 1
+
+    def __init__(self, seed: int):
+        s = seed & self._M  # (ulong)seed of an int: sign-extended
+
+        def splitmix():
+            nonlocal s
+            s = (s + 0x9E3779B97F4A7C15) & self._M
+            z = s
+            z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & self._M
+            z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & self._M
+            return z ^ (z >> 31)
+
+        self.s0, self.s1 = splitmix(), splitmix()
+        if self.s0 == 0 and self.s1 == 0:
+            self.s0 = self.s1 = 1
+
+    def next_ulong(self) -> int:
+        s0, s1 = self.s0, self.s1
+        r = (s0 + s1) & self._M
+        s1 ^= s0
+        self.s0 = (((s0 << 24) | (s0 >> 40)) & self._M) ^ s1 ^ ((s1 << 16) & self._M)
+        self.s1 = ((s1 << 37) | (s1 >> 27)) & self._M
+        return r
+
+    def next_double(self) -> float:
+        return (self.next_ulong() & ((1 << 53) - 1)) * (1.0 / (1 << 53))
+
+
+def sample(ctx: CudaContext, logits: np.ndarray, options: SamplingOptions, targets, context=None,
+           want_probs: bool = False):
+    """sm_sample over host arrays: logits [rows, vocab], targets [rows] uniform draws,
+    context: per-row token histories (for the penalties).  Returns tokens (and probs)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    if lg.ndim == 1:
+        lg = lg[None]
+    rows, vocab = lg.shape
+    tg = np.ascontiguousarray(np.asarray(targets, np.float64).reshape(-1))
+    if tg.size != rows:
+        raise ValueError("one target per row")
+    ctx_arr = lens = None
+    stride = 0
+    if context is not None and options.penalized:
+        hist = [np.asarray(c, np.int32).reshape(-1) for c in context]
+        stride = max(1, max(h.size for h in hist))
+        ctx_arr = np.zeros((rows, stride), np.int32)
+        lens = np.zeros(rows, np.int32)
+        for r, h in enumerate(hist):
+            ctx_arr[r, :h.size] = h
+            lens[r] = h.size
+    toks = np.zeros(rows, np.int32)
+    probs = np.empty((rows, vocab), np.float32) if want_probs else None
+    prm = options.params()
+    L.check(L.lib().sm_sample(ctx.handle, _p(lg), rows, vocab, C.byref(prm),
+                              _p(ctx_arr) if ctx_arr is not None else None, _p(lens) if lens is not None else None,
+                              stride, _p(tg), _p(toks), _p(probs) if want_probs else None, L.PTR_HOST), "sm_sample")
+    return (toks, probs) if want_probs else toks
+
+
 class InferenceSession:
     """Greedy generation loop (InferenceSession.GenerateNextTokenAsync, TopK = 1) over one sequence slot."""
 
     def __init__(self, kv: KVCache, seq: int = 0):
         self.kv, self.seq = kv, seq
+
+    def generate_sampled(self, prompt_ids, max_new_tokens: int, options: SamplingOptions):
+        """GenerateNextTokenAsync with the full sampling pipeline on the device
+        (sm_sample); the context for the penalties is prompt + generated tokens."""
+        rng = DeterministicRng(options.seed if options.seed is not None else 0)
+        ctx = self.kv.model.ctx
+        self.kv.reset(self.seq)
+        context = [int(t) for t in prompt_ids]
+        _, logits = self.kv.prefill(self.seq, prompt_ids, want_logits=True)
+        out = []
+        while True:
+            t = int(sample(ctx, logits, options, [rng.next_double()], [context])[0])
+            out.append(t)
+            context.append(t)
+            if len(out) == max_new_tokens:
+                return out
+            _, lg = self.kv.decode([self.seq], [t], want_logits=True)
+            logits = lg[0]
 
     def generate(self, prompt_ids, max_new_tokens: int, return_logits: bool = False):
         self.kv.reset(self.seq)

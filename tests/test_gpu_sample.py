@@ -1,0 +1,166 @@
+"""Device sampling (sm_sample) against the oracle's restatement of the reference
+pipeline (InferenceSession.cs:565-734).
+
+Tolerance: the final distribution within 1e-4 relative (plus 1e-9 absolute) of
+the oracle's.  The reference normalises by a sequential fp32 sum over the whole
+vocabulary (Softmax, :672-712), whose rounding error reaches ~3e-5 relative at
+32K entries; the device sums as a tree.  The token is therefore checked two
+ways: exactly against the device's own distribution (the first index whose
+float64 cumulative sum reaches the target, :714-734), and against the oracle's
+distribution up to the measured difference of the two cumulative sums (the
+target lies in the token's cumulative interval widened by that difference).
+Top-p cuts where the reference's running fp32 sum over the sorted
+probabilities (:889-897) reaches top_p; over a nucleus of thousands of tokens
+that sum drifts from the exact one, so the device's cut (exact, in float64) may
+sit a few tokens away: any cut between the fp32-sequential and the exact
+position is accepted, and the renormalised distribution on it is compared."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    dict(),
+    dict(temperature=0.7),
+    dict(top_k=1),
+    dict(top_k=40, temperature=0.8),
+    dict(top_p=0.9),
+    dict(top_k=50, top_p=0.95, temperature=0.9),
+    dict(min_p=0.05),
+    dict(top_p=0.5, min_p=0.1, temperature=1.3),
+    dict(repetition_penalty=1.3, presence_penalty=0.2, frequency_penalty=0.1, top_k=64),
+    dict(repetition_penalty=0.8, repetition_window=16, top_p=0.8),
+]
+
+
+def _opts(sm, d):
+    return sm.SamplingOptions(**d)
+
+
+def _check_token(t, p_dev, p_ref, target):
+    c_dev = np.cumsum(p_dev.astype(np.float64))
+    hit = np.nonzero(c_dev >= target)[0]
+    assert t == (int(hit[0]) if hit.size else p_dev.size - 1)
+    c_ref = np.cumsum(p_ref.astype(np.float64))
+    delta = float(np.max(np.abs(c_dev - c_ref))) + 1e-12
+    lo = c_ref[t - 1] if t > 0 else 0.0
+    assert lo < target + delta and (c_ref[t] >= target - delta or t == p_ref.size - 1)
+
+
+def _check_top_p_cut(O, logits, target, case, context, p_dev):
+    """The device kept a descending prefix of the pre-top-p distribution whose length
+    lies between the fp32-sequential and the exact cut, renormalised."""
+    pre = dict(case, top_p=1.0)
+    _, q = O.sample(logits, target, context=context, **pre)
+    order = np.argsort(-q, kind="stable")
+    qs = q[order]
+    c32 = np.cumsum(qs, dtype=np.float32)
+    c64 = np.cumsum(qs.astype(np.float64))
+    cut = lambda c: int(np.argmax(c >= case["top_p"])) + 1 if np.any(c >= case["top_p"]) else q.size
+    lo, hi = sorted((cut(c32), cut(c64)))
+    kept = np.nonzero(p_dev > 0)[0]
+    n = kept.size
+    assert lo - 1 <= n <= hi + 1, (lo, hi, n)
+    assert set(kept) == set(order[:n])
+    want = np.zeros_like(q)
+    want[order[:n]] = qs[:n] / qs[:n].sum(dtype=np.float64)
+    assert np.allclose(p_dev, want, rtol=1e-4, atol=1e-9)
+
+
+@pytest.mark.parametrize("vocab", [384, 32000, 49152])
+@pytest.mark.parametrize("ci", range(len(CASES)))
+def test_sample_matches_oracle(ctx, O, vocab, ci):
+    import smallmind_b200 as sm
+    case = CASES[ci]
+    rs = np.random.RandomState(vocab + ci)
+    rows = 4
+    logits = (rs.randn(rows, vocab) * 3).astype(np.float32)
+    targets = O.deterministic_rng_doubles(ci + 1, rows)
+    hist = [rs.randint(0, vocab, n) for n in (0, 7, 300, 40)]
+    toks, probs = sm.sample(ctx, logits, _opts(sm, case), targets, context=hist, want_probs=True)
+    for r in range(rows):
+        t, p = O.sample(logits[r], targets[r], context=hist[r], **case)
+        if case.get("top_p", 1.0) < 1.0 and "min_p" not in case and not np.allclose(probs[r], p, rtol=1e-4, atol=1e-9):
+            _check_top_p_cut(O, logits[r], targets[r], case, hist[r], probs[r])
+            _check_token(int(toks[r]), probs[r], probs[r], targets[r])
+            continue
+        assert np.allclose(probs[r], p, rtol=1e-4, atol=1e-9), (r, float(np.max(np.abs(probs[r] - p))))
+        _check_token(int(toks[r]), probs[r], p, targets[r])
+
+
+def test_sample_ties_and_edges(ctx, O):
+    import smallmind_b200 as sm
+    from smallmind_b200 import _lib as L
+    rs = np.random.RandomState(3)
+    V = 1000
+    logits = rs.randint(-3, 4, (3, V)).astype(np.float32)  # many equal values: the k-th value has ties
+    targets = np.array([0.25, 0.5, 0.999], np.float64)
+    for case in (dict(top_k=5), dict(top_k=300), dict(top_k=999), dict(top_k=V + 5)):
+        toks, probs = sm.sample(ctx, logits, _opts(sm, case), targets, want_probs=True)
+        for r in range(3):
+            t, p = O.sample(logits[r], targets[r], **case)
+            assert np.allclose(probs[r], p, rtol=1e-4, atol=1e-9)
+            _check_token(int(toks[r]), probs[r], p, targets[r])
+    # -inf logits are never sampled; a target past the total picks the last index (:733)
+    lg = np.full(64, -np.inf, np.float32)
+    lg[10] = 1.0
+    assert sm.sample(ctx, lg, _opts(sm, {}), [0.7])[0] == 10
+    assert sm.sample(ctx, np.zeros(16, np.float32), _opts(sm, {}), [1.0])[0] == 15
+    with pytest.raises(Exception):
+        sm.sample(ctx, np.zeros(L.SAMPLE_MAX_VOCAB + 1, np.float32), _opts(sm, {}), [0.5])
+    with pytest.raises(Exception):
+        sm.sample(ctx, np.zeros(8, np.float32), _opts(sm, dict(temperature=0.0)), [0.5])
+
+
+def test_sample_device_pointers_match_host(ctx, O):
+    """SM_PTR_DEVICE (the stream-ordered, allocation-free form) gives the host form's tokens."""
+    import ctypes as C
+
+    import torch
+
+    import smallmind_b200 as sm
+    from smallmind_b200 import _lib as L
+    rs = np.random.RandomState(8)
+    rows, V = 8, 32000
+    logits = (rs.randn(rows, V) * 2).astype(np.float32)
+    targets = O.deterministic_rng_doubles(5, rows)
+    opts = sm.SamplingOptions(temperature=0.9, top_k=100, top_p=0.9)
+    want = sm.sample(ctx, logits, opts, targets)
+    dl = torch.from_numpy(logits).cuda()
+    dt = torch.from_numpy(targets).cuda()
+    out = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    prm = opts.params()
+    assert L.lib().sm_sample(ctx.handle, dl.data_ptr(), rows, V, C.byref(prm), None, None, 0, dt.data_ptr(),
+                             out.data_ptr(), None, L.PTR_DEVICE) == 0
+    ctx.sync()
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+def test_generate_sampled_matches_oracle(ctx, O):
+    """Seeded sampling end to end: each step's token is the oracle pipeline's
+    sample of the oracle model's logits for the same history and draw, up to
+    the 1e-4 distribution tolerance at the cumulative boundary."""
+    import smallmind_b200 as sm
+    cfg = dict(vocab_size=384, hidden=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, ffn_hidden=512,
+               max_context=48, norm_eps=1e-5, rope_theta=10000.0)
+    schemes = dict(wq=O.Q4_K, wk=O.Q4_K, wv=O.Q6_K, wo=O.Q4_K, w_gate=O.Q4_K, w_up=O.Q4_K, w_down=O.Q6_K,
+                   output=O.Q6_K)
+    host = O.make_model(cfg, schemes, seed=3)
+    model = sm.CudaModel.from_host(ctx, host)
+    kv = sm.KVCache(model, 1, 48)
+    opts = sm.SamplingOptions(temperature=0.8, top_k=40, top_p=0.95, repetition_penalty=1.1, seed=1234)
+    prompt = np.random.RandomState(2).randint(0, cfg["vocab_size"], 7).astype(np.int32)
+    toks = sm.InferenceSession(kv).generate_sampled(prompt, 8, opts)
+    draws = O.deterministic_rng_doubles(1234, len(toks))
+    hist = list(prompt)
+    for step, t in enumerate(toks):
+        lg = O.model_forward(host, np.array(hist, np.int32), 1)[0]
+        want, p = O.sample(lg, draws[step], temperature=0.8, top_k=40, top_p=0.95, repetition_penalty=1.1,
+                           context=hist)
+        if t != want:
+            c = np.cumsum(p.astype(np.float64))
+            assert abs(c[min(t, want)] - draws[step]) < 1e-4, step
+        hist.append(t)
+    kv.close()
+    model.close()
