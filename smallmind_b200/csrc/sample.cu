@@ -7,12 +7,14 @@
 // (vocab <= SM_SAMPLE_MAX_VOCAB) and every stage works there:
 //   penalties   one thread per distinct token of the window (first occurrence)
 //   temperature x * (1 / T)
-//   top-k       exact k-th largest value by a 4-pass radix select (8-bit digits
-//               of the order-preserving key, warp-aggregated shared histograms)
+//   top-k       exact k-th largest value: the row turned into order-preserving
+//               keys, the largest key x with count(key >= x) >= k found bit by
+//               bit (key_search: one barrier per block step; the last bits on a
+//               compacted bucket in one warp)
 //   softmax     block max, expf, block sum, division
-//   top-p       the cut value by a bitwise search over the probability's bits
-//               (31 block reductions of sum(p >= candidate) in double), ties at
-//               the cut kept in index order
+//   top-p       the cut value by the same search over the probability's bits
+//               (fp32 per thread, float64 across threads); ties at the cut kept
+//               in index order
 //   min-p       block max, threshold, renormalise (multiply by 1 / sum)
 //   sample      per-thread contiguous chunks, block scan of the chunk sums in
 //               double, first index whose cumulative sum reaches the target.
@@ -131,13 +133,114 @@ __device__ __forceinline__ void normalize(float* P, int V, float* redf) {
   __syncthreads();
 }
 
+// Bitwise search for the largest key x with  W(key >= x) >= need,  W = element
+// count (top-k) or the sum of the probabilities (top-p; keys are then the bits of
+// p >= 0).  Block-wide steps (one barrier each, double-buffered partials) narrow
+// the bucket of keys sharing x's decided bits; once it holds <= LIST_MAX
+// elements they are compacted into `list` and warp 0 decides the remaining bits
+// alone.  Returns x, the weight strictly above x and the number of keys equal to x.
+constexpr int LIST_MAX = 1024;
+struct Found {
+  uint32_t x;
+  double above;
+  int eq;
+};
+
+template <bool SUM>
+__device__ Found key_search(const uint32_t* K, int V, double need, int top_bit, uint32_t* list, double* redw,
+                            int* redc, int* list_n, Found* out) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t x = 0, mask = 0;
+  double above = 0.0;
+  int pop = V, bit = top_bit, ph = 0;
+  for (; bit >= 0 && pop > LIST_MAX; --bit) {
+    const uint32_t b = 1u << bit;
+    float sw = 0.f;
+    int sc = 0;
+    for (int i = threadIdx.x; i < V; i += ST) {
+      const uint32_t k = K[i];
+      if ((k & mask) == x && (k & b)) {
+        if (SUM) sw += __uint_as_float(k);
+        ++sc;
+      }
+    }
+    const double dw = warp_sum(SUM ? (double)sw : 0.0);
+    sc = warp_sum(sc);
+    if (lane == 0) {
+      redw[ph * 32 + w] = dw;
+      redc[ph * 32 + w] = sc;
+    }
+    __syncthreads();
+    const double tw = SUM ? warp_sum(lane < SW ? redw[ph * 32 + lane] : 0.0) : 0.0;
+    const int tc = warp_sum(lane < SW ? redc[ph * 32 + lane] : 0);
+    ph ^= 1;
+    const double t = SUM ? tw : (double)tc;
+    if (above + t >= need) {
+      x |= b;
+      pop = tc;
+    } else {
+      above += t;
+      pop -= tc;
+    }
+    mask |= b;
+  }
+  if (bit >= 0) {
+    // compact the bucket (pop <= LIST_MAX keys) and finish in warp 0
+    if (threadIdx.x == 0) *list_n = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < V; i0 += ST) {
+      const int i = i0 + threadIdx.x;
+      const uint32_t k = i < V ? K[i] : 0u;
+      const bool in = i < V && (k & mask) == x;
+      const unsigned bal = __ballot_sync(0xffffffffu, in);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(list_n, __popc(bal));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (in) list[base + __popc(bal & ((1u << lane) - 1u))] = k;
+    }
+    __syncthreads();
+    if (w == 0) {
+      const int n = *list_n;
+      for (; bit >= 0; --bit) {
+        const uint32_t b = 1u << bit;
+        float sw = 0.f;
+        int sc = 0;
+        for (int j = lane; j < n; j += 32) {
+          const uint32_t k = list[j];
+          if ((k & mask) == x && (k & b)) {
+            if (SUM) sw += __uint_as_float(k);
+            ++sc;
+          }
+        }
+        const double t = SUM ? warp_sum((double)sw) : (double)warp_sum(sc);
+        const int tc = warp_sum(sc);
+        if (above + t >= need) {
+          x |= b;
+          pop = tc;
+        } else {
+          above += t;
+          pop -= tc;
+        }
+        mask |= b;
+      }
+      if (lane == 0) *out = Found{x, above, pop};
+    }
+    __syncthreads();
+    return *out;
+  }
+  return Found{x, above, pop};
+}
+
 __global__ void __launch_bounds__(ST, 1) sample_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ float P[];  // the row: logits, then probabilities
   __shared__ float redf[32];
   __shared__ double redd[32];
   __shared__ int redi[32];
-  __shared__ unsigned hist[256];
-  __shared__ uint32_t sel[2];
+  __shared__ double sredw[64];
+  __shared__ int sredc[64];
+  __shared__ uint32_t slist[LIST_MAX];
+  __shared__ int slist_n;
+  __shared__ Found sfound;
   const int V = a.vocab, row = blockIdx.x, tid = threadIdx.x;
   const sm_sampling_params& p = a.p;
   const float* src = a.logits + (size_t)row * V;
@@ -171,40 +274,19 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const __grid_constant__ S
     for (int i = tid; i < V; i += ST) P[i] = __fmul_rn(P[i], inv);
     __syncthreads();
   }
-  // 3. top-k (:635-670): exact k-th largest (descending-sort position k-1), values below -> -inf
+  // 3. top-k (:635-670): exact k-th largest (descending-sort position k-1), values below -> -inf.
+  // The row becomes order-preserving keys; the k-th largest key is the largest x with
+  // count(key >= x) >= k.
   if (p.top_k > 0 && p.top_k < V) {
-    uint32_t prefix = 0, pmask = 0;
-    int kk = p.top_k;  // rank still to find, counted from the top inside the current prefix
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int i = tid; i < 256; i += ST) hist[i] = 0;
-      __syncthreads();
-      for (int i0 = 0; i0 < V; i0 += ST) {
-        const int i = i0 + tid;
-        const bool in = i < V && (fkey(P[min(i, V - 1)]) & pmask) == prefix;
-        const unsigned d = in ? (fkey(P[i]) >> shift) & 0xFF : 256u + (tid & 31);  // out: unique dummy
-        const unsigned grp = __match_any_sync(0xffffffffu, d);
-        if (in && (__ffs(grp) - 1) == (tid & 31)) atomicAdd(&hist[d], (unsigned)__popc(grp));
-      }
-      __syncthreads();
-      if (tid == 0) {
-        int cum = 0, b = 255;
-        for (; b > 0; --b) {
-          if (cum + (int)hist[b] >= kk) break;
-          cum += hist[b];
-        }
-        sel[0] = (uint32_t)b;
-        sel[1] = (uint32_t)(kk - cum);
-      }
-      __syncthreads();
-      prefix |= sel[0] << shift;
-      pmask |= 0xFFu << shift;
-      kk = (int)sel[1];
-      __syncthreads();
+    uint32_t* K = reinterpret_cast<uint32_t*>(P);
+    for (int i = tid; i < V; i += ST) K[i] = fkey(P[i]);
+    __syncthreads();
+    const uint32_t x = key_search<false>(K, V, (double)p.top_k, 31, slist, sredw, sredc, &slist_n, &sfound).x;
+    for (int i = tid; i < V; i += ST) {
+      const uint32_t k = K[i];
+      const float v = __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+      P[i] = k >= x ? v : -INFINITY;
     }
-    const uint32_t u = (prefix & 0x80000000u) ? (prefix & 0x7FFFFFFFu) : ~prefix;
-    const float kth = __uint_as_float(u);
-    for (int i = tid; i < V; i += ST)
-      if (!(P[i] >= kth)) P[i] = -INFINITY;
     __syncthreads();
   }
   // 4. softmax (:672-712)
@@ -231,30 +313,14 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const __grid_constant__ S
   const int c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
   // 5. top-p (:862-907): the cut value tau = the largest p with sum(p >= tau) >= top_p
   if (p.top_p < 1.0) {
-    uint32_t x = 0;
-    for (int bit = 30; bit >= 0; --bit) {
-      const uint32_t cand = x | (1u << bit);
-      double s = 0.0;
-      for (int i = tid; i < V; i += ST)
-        if (__float_as_uint(P[i]) >= cand) s += (double)P[i];
-      s = block_sum(s, redd);
-      if (s >= p.top_p) x = cand;
-    }
-    const float tau = __uint_as_float(x);
-    // sum above the cut and the ties at it; keep the first m ties (index order)
-    double above = 0.0;
-    int neq = 0;
-    for (int i = tid; i < V; i += ST) {
-      if (P[i] > tau) above += (double)P[i];
-      neq += P[i] == tau;
-    }
-    above = block_sum(above, redd);
-    neq = block_sum(neq, redi);
+    const Found f = key_search<true>(reinterpret_cast<const uint32_t*>(P), V, p.top_p, 30, slist, sredw, sredc,
+                                     &slist_n, &sfound);
+    const float tau = __uint_as_float(f.x);
+    const double above = f.above;
+    const int neq = f.eq;
+    // keep the first m ties at the cut (index order)
     int m = neq;
-    if (tau > 0.f && above < p.top_p) {
-      const double need = (p.top_p - above) / (double)tau;
-      m = min(neq, max(1, (int)ceil(need)));
-    }
+    if (tau > 0.f && above < p.top_p) m = min(neq, max(1, (int)ceil((p.top_p - above) / (double)tau)));
     int mine = 0;
     for (int i = c0; i < c1; ++i) mine += P[i] == tau;
     int before = (int)block_exclusive_scan((double)mine, redd);
