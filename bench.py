@@ -500,6 +500,44 @@ def run_ours(args):
     bs64_tps = bs * n64 / (e0.elapsed_time(e1) / 1000.0)
     kv3.close()
 
+    # serving, 256 sequences (256 / world on each rank) of a 512-token prompt
+    # and 128 greedy tokens; wall clock over prefill + decode through the public API, max over ranks
+    serving = None
+    if not args.no_serving:
+        n_seq, p_len, n_new = max(1, 256 // world), 512, 128
+        kv5 = sm.KVCache(model, n_seq, p_len + n_new)
+        prompts = [rs.randint(0, cfg["vocab_size"], p_len).astype(np.int32) for _ in range(n_seq)]
+        seqs5 = torch.arange(n_seq, dtype=torch.int32, device="cuda")
+        kv5.prefill(0, prompts[0], want_logits=False)  # warm the prefill and bs-n_seq decode paths
+        kv5.reset(0)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        first = np.empty(n_seq, np.int32)
+        per = []
+        for s_, pr in enumerate(prompts):
+            ta = time.perf_counter()
+            first[s_], _ = kv5.prefill(s_, pr, want_logits=False)
+            per.append(time.perf_counter() - ta)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        toks5 = torch.from_numpy(first).cuda()
+        for _ in range(n_new - 1):
+            kv5.decode_device(seqs5.data_ptr(), toks5.data_ptr(), n_seq, None, toks5.data_ptr())
+        _ = toks5.cpu()
+        t2 = time.perf_counter()
+        pre_s = sharding.max_over_ranks(t1 - t0, device="cuda")
+        tot_s = sharding.max_over_ranks(t2 - t0, device="cuda")
+        kv5.close()
+        serving = {"sequences": n_seq * world, "prompt": p_len, "new_tokens": n_new,
+                   "generated_tok_s": round(world * n_seq * n_new / tot_s, 1),
+                   "total_tok_s": round(world * n_seq * (p_len + n_new) / tot_s, 1),
+                   "prefill_s": round(pre_s, 3), "decode_s": round(tot_s - pre_s, 3),
+                   "prefill_ms_median": round(1e3 * float(np.median(per)), 2),
+                   "prefill_ms_max": round(1e3 * float(np.max(per)), 2),
+                   "decode_tok_s": round(world * n_seq * (n_new - 1) / max(1e-9, tot_s - pre_s), 1)}
+
     # SmolLM-135M-shaped Q8_0, 128-token prompt, 128 greedy bs1 decode steps
     smol = dict(SMOLLM)
     model_s, _ = build_gpu_model(sm, ctx, smol, seed=77, schemes={k: "Q8_0" for k in SCHEMES}, block_size=64)
@@ -554,6 +592,7 @@ def run_ours(args):
                      "q6k_gbs": round(d_bytes / (d_ms * 1e-3) / 1e9, 1)},
             "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
             "bs64_decode_tok_s": round(bs64_tps, 1),
+            "serving_256x512p128": serving,
             "smollm_q8_bs1_decode_tok_s": round(smol_tps, 1),
             "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
             "gpu_launches": int(launches_timed),
@@ -572,6 +611,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-serving", action="store_true", help="skip the 256-sequence serving run (config 5)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
     ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
     ap.add_argument("--gemm-sweep", action="store_true",

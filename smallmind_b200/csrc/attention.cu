@@ -329,10 +329,10 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
   const int G = nH / nKv;
   extern __shared__ float sm_[];
   float* qs = sm_;                        // [CMAXG][HD]
-  float* sc = qs + CMAXG * HD;            // [CMAXG][chunk_cap]
+  float* sc = qs + CMAXG * HD;            // [chunk_cap][CMAXG]: a key's scores of the group's heads side by side
   float* pacc = sc + CMAXG * chunk_cap;   // [CMAXG][HD]  this CTA's e.V
   float* stat = pacc + CMAXG * HD;        // [CMAXG] slice max, [CMAXG] slice sum
-  float* part = stat + 2 * CMAXG;         // [CT/HD][CMAXG][HD]
+  float* part = stat + 2 * CMAXG;         // [CT/32][CMAXG][HD]
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int len = lens[b];
   const int per = (len + CL - 1) / CL;
@@ -353,32 +353,49 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
 #pragma unroll
   for (int h = 0; h < CMAXG; ++h) lmax[h] = -FLT_MAX;
   const int passes = (n + 31) / 32;
+  // the next pass's key slice is loaded before this pass's dot products (two passes in flight)
+  float kn[DPL];
+  auto load_k = [&](int pp, float (&dst)[DPL]) {
+    const int j = pp * 32 + slot;
+    if (j < n) {
+      const float4* kp = (const float4*)(kb + (int64_t)(j0 + j) * row_stride + sub * DPL);
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) {
+        const float4 t = __ldg(kp + i);
+        dst[4 * i] = t.x; dst[4 * i + 1] = t.y; dst[4 * i + 2] = t.z; dst[4 * i + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[i] = 0.f;
+    }
+  };
+  if (passes > 0) load_k(0, kn);
   for (int p = 0; p < passes; ++p) {
     const int jj = p * 32 + slot;
     const bool valid = jj < n;
     float kv[DPL];
-    if (valid) {
-      const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * row_stride + sub * DPL);
 #pragma unroll
-      for (int i = 0; i < DPL / 4; ++i) {
-        const float4 t = __ldg(kp + i);
-        kv[4 * i] = t.x; kv[4 * i + 1] = t.y; kv[4 * i + 2] = t.z; kv[4 * i + 3] = t.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) kv[i] = 0.f;
-    }
+    for (int i = 0; i < DPL; ++i) kv[i] = kn[i];
+    if (p + 1 < passes) load_k(p + 1, kn);
 #pragma unroll
     for (int h = 0; h < CMAXG; ++h) {
       if (h >= G) break;
+      const float4 qa = *(const float4*)&qs[h * HD + sub * DPL];
+      const float4 qb = *(const float4*)&qs[h * HD + sub * DPL + 4];
       float s = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) s = fmaf(qs[h * HD + sub * DPL + i], kv[i], s);
+      s = fmaf(qa.x, kv[0], s);
+      s = fmaf(qa.y, kv[1], s);
+      s = fmaf(qa.z, kv[2], s);
+      s = fmaf(qa.w, kv[3], s);
+      s = fmaf(qb.x, kv[4], s);
+      s = fmaf(qb.y, kv[5], s);
+      s = fmaf(qb.z, kv[6], s);
+      s = fmaf(qb.w, kv[7], s);
       s += __shfl_xor_sync(0xffffffffu, s, 1);
       s += __shfl_xor_sync(0xffffffffu, s, 2);
       s += __shfl_xor_sync(0xffffffffu, s, 4);
       if (valid) {
-        if (sub == 0) sc[h * chunk_cap + jj] = s;
+        if (sub == 0) sc[jj * CMAXG + h] = s;
         lmax[h] = fmaxf(lmax[h], __fmul_rn(s, scale));
       }
     }
@@ -407,27 +424,56 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
     gmax[threadIdx.x] = m;
   }
   __syncthreads();
-  // e = FastExp(s*scale - max) in place, then e.V
-  for (int t = threadIdx.x; t < G * n; t += CT) {
-    const int h = t / n, jj = t - h * n;
-    sc[h * chunk_cap + jj] = pade_exp(__fsub_rn(__fmul_rn(sc[h * chunk_cap + jj], scale), gmax[h]));
+  // e = FastExp(s*scale - max) in place (each thread keeps one head: CT is a multiple of CMAXG),
+  // with this thread's share of the slice sum of its head
+  float esum = 0.f;
+  {
+    const int h = threadIdx.x & (CMAXG - 1);
+    if (h < G) {
+      const float gm = gmax[h];
+      for (int t = threadIdx.x; t < CMAXG * n; t += CT) {
+        const float e = pade_exp(__fsub_rn(__fmul_rn(sc[t], scale), gm));
+        sc[t] = e;
+        esum += e;
+      }
+    }
   }
   __syncthreads();
-  constexpr int PH = CT / HD;
-  const int d = threadIdx.x % HD, ph = threadIdx.x / HD;
-  float acc[CMAXG];
+  // e.V: 16 lanes per value row (4 dims each, one 16-byte load), 16 rows per pass;
+  // lanes l and l + 16 of a warp hold the same dims and are merged by a shuffle
+  constexpr int PH = CT / 32;
+  static_assert(HD == 64, "e.V lane layout assumes head_dim 64");
+  const int d4 = threadIdx.x & 15, pr = threadIdx.x >> 4;
+  float4 acc[CMAXG];
 #pragma unroll
-  for (int h = 0; h < CMAXG; ++h) acc[h] = 0.f;
+  for (int h = 0; h < CMAXG; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-  for (int jj = ph; jj < n; jj += PH) {
-    const float v = __ldg(vb + (int64_t)(j0 + jj) * row_stride + d);
+  for (int jj = pr; jj < n; jj += CT / 16) {
+    const float4 v = __ldg((const float4*)(vb + (int64_t)(j0 + jj) * row_stride) + d4);
+    const float4 ea = *(const float4*)&sc[jj * CMAXG], eb = *(const float4*)&sc[jj * CMAXG + 4];
+    const float ev[CMAXG] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w};
 #pragma unroll
     for (int h = 0; h < CMAXG; ++h)
-      if (h < G) acc[h] = fmaf(sc[h * chunk_cap + jj], v, acc[h]);
+      if (h < G) {
+        const float e = ev[h];
+        acc[h].x = fmaf(e, v.x, acc[h].x);
+        acc[h].y = fmaf(e, v.y, acc[h].y);
+        acc[h].z = fmaf(e, v.z, acc[h].z);
+        acc[h].w = fmaf(e, v.w, acc[h].w);
+      }
   }
+  {
+    const int ph = threadIdx.x >> 5;
 #pragma unroll
-  for (int h = 0; h < CMAXG; ++h)
-    if (h < G) part[(ph * CMAXG + h) * HD + d] = acc[h];
+    for (int h = 0; h < CMAXG; ++h)
+      if (h < G) {
+        acc[h].x += __shfl_xor_sync(0xffffffffu, acc[h].x, 16);
+        acc[h].y += __shfl_xor_sync(0xffffffffu, acc[h].y, 16);
+        acc[h].z += __shfl_xor_sync(0xffffffffu, acc[h].z, 16);
+        acc[h].w += __shfl_xor_sync(0xffffffffu, acc[h].w, 16);
+        if ((threadIdx.x & 31) < 16) *(float4*)&part[(ph * CMAXG + h) * HD + 4 * d4] = acc[h];
+      }
+  }
   __syncthreads();
   for (int t = threadIdx.x; t < G * HD; t += CT) {
     const int h = t / HD, dd = t - h * HD;
@@ -436,13 +482,17 @@ __global__ void __launch_bounds__(CT) decode_cluster_kernel(
     pacc[h * HD + dd] = s;
   }
   {
-    // slice sum of each head: warp h over the slice, then a warp sum
+    // slice sum of each head: lanes of one head (lane & 7) merged by shuffles, then the warps
+    esum += __shfl_xor_sync(0xffffffffu, esum, 8);
+    esum += __shfl_xor_sync(0xffffffffu, esum, 16);
+    __syncthreads();  // every thread is done reading part (the e.V partials)
     const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
-    for (int h = w; h < G; h += CT / 32) {
+    if (ln < CMAXG) part[w * CMAXG + ln] = esum;
+    __syncthreads();
+    if (threadIdx.x < G) {
       float s = 0.f;
-      for (int jj = ln; jj < n; jj += 32) s += sc[h * chunk_cap + jj];
-      s = warp_sum(s);
-      if (ln == 0) stat[CMAXG + h] = s;
+      for (int ww = 0; ww < CT / 32; ++ww) s += part[ww * CMAXG + threadIdx.x];
+      stat[CMAXG + threadIdx.x] = s;
     }
   }
   cluster.sync();
@@ -503,7 +553,7 @@ int launch_decode_cluster_cl(const float* q, int q_stride, const float* kc, cons
                              const int* lens, const int* seq_map, int B, int nH, int nKv, int hd, cudaStream_t st,
                              int* n_launch) {
   const int chunk_cap = (max_ctx + CL - 1) / CL;
-  const size_t smem = sizeof(float) * (CMAXG * 64 * 2 + CMAXG * (size_t)chunk_cap + 2 * CMAXG + (CT / 64) * CMAXG * 64);
+  const size_t smem = sizeof(float) * (CMAXG * 64 * 2 + CMAXG * (size_t)chunk_cap + 2 * CMAXG + (CT / 32) * CMAXG * 64);
   if (smem > 200 * 1024 / 4) return SM_ERR_UNSUPPORTED;
   auto kern = decode_cluster_kernel<64, CL>;
   static bool attr_set[64] = {};
@@ -567,6 +617,11 @@ int launch_attention_decode_cluster(const float* q, int q_stride, const float* k
                                     float* out, int out_stride, const int* lens, const int* seq_map, int B, int nH,
                                     int nKv, int hd, cudaStream_t st, int* n_launch) {
   if (hd != 64 || nH % nKv || nH / nKv > CMAXG) return SM_ERR_UNSUPPORTED;
+  {
+    // SMALLMIND_ATTN_CLUSTER=0 selects the three-kernel split-context path
+    const char* e = std::getenv("SMALLMIND_ATTN_CLUSTER");
+    if (e && e[0] == '0') return SM_ERR_UNSUPPORTED;
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -574,7 +629,7 @@ int launch_attention_decode_cluster(const float* q, int q_stride, const float* k
   while (cl > 1 && (int64_t)cl * nKv * B > 2 * sms) cl >>= 1;
   auto fits = [&](int c) {
     const int64_t cap = (max_ctx + c - 1) / c;
-    return sizeof(float) * (CMAXG * 64 * 2 + CMAXG * cap + 2 * CMAXG + (CT / 64) * CMAXG * 64) <= 200 * 1024 / 4;
+    return sizeof(float) * (CMAXG * 64 * 2 + CMAXG * cap + 2 * CMAXG + (CT / 32) * CMAXG * 64) <= 200 * 1024 / 4;
   };
   while (cl < 16 && !fits(cl)) cl <<= 1;
   switch (cl) {

@@ -262,6 +262,17 @@ SM_API int sm_ctx_create(int device, sm_ctx** out) {
     return fail(SM_ERR_OOM, "ctx_create: allocation failed");
   }
   cudaMemset(c->dev_status, 0, sizeof(int));
+  {
+    // the library's per-call temporaries come from this process's default stream-ordered
+    // pool; keep freed blocks in it (the default threshold of 0 hands them back to the
+    // driver at every synchronising call, and the next call maps them again)
+    cudaMemPool_t pool = nullptr;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
+  }
   *out = c;
   return SM_OK;
 }
@@ -327,6 +338,7 @@ SM_API int sm_weight_destroy(sm_weight* w) {
   if (!w) return SM_OK;
   DeviceGuard g(w->ctx->device);
   cudaStreamSynchronize(w->ctx->stream);
+  gemm_tc_release_weight(w->w.data);
   if (w->w.data) cudaFree(w->w.data);
   if (w->w.aux) cudaFree(w->w.aux);
   delete w;

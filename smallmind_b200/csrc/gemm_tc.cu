@@ -25,6 +25,9 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "mbar.cuh"
@@ -648,7 +651,86 @@ int make_plane_map(CUtensorMap* map, void* base, int M, int K) {
   return r == CUDA_SUCCESS ? SM_OK : fail(SM_ERR_CUDA, "gemm: tensor map encoding failed");
 }
 
+// Resident fp16 planes of weight groups.  A GEMM with more than one 128-row tile
+// of x reads the weights as fp16 hi / lo planes; splitting them costs a pass over
+// every weight per call (~11 us per TinyLlama weight).  The first such call for
+// a weight group (outside stream capture, when free HBM stays above an eighth of
+// the device after the allocation) keeps the planes, 4 bytes per weight, until
+// one of the group's weights is destroyed.  SMALLMIND_WEIGHT_PLANES=0 disables it.
+struct PlaneEntry {
+  std::vector<const void*> keys;
+  int dev;
+  __half* hi;
+  __half* lo;
+};
+std::mutex g_plane_mu;
+std::vector<PlaneEntry> g_planes;
+
+bool planes_enabled() {
+  const char* e = std::getenv("SMALLMIND_WEIGHT_PLANES");
+  return !(e && e[0] == '0');
+}
+
+// the group's planes (nullptr when not resident); creates them when allowed
+int resident_planes(const DevWeight* const* Ws, int nw, int N, int K, int dev, cudaStream_t st, __half** hi,
+                    __half** lo, int* n_launch) {
+  *hi = *lo = nullptr;
+  std::vector<const void*> keys(nw);
+  for (int i = 0; i < nw; ++i) keys[i] = Ws[i]->data;
+  std::lock_guard<std::mutex> g(g_plane_mu);
+  for (const auto& e : g_planes)
+    if (e.dev == dev && e.keys == keys) {
+      *hi = e.hi;
+      *lo = e.lo;
+      return SM_OK;
+    }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return SM_OK;
+  const size_t bytes = (size_t)N * K * 4;
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || free_b < bytes + total_b / 8) return SM_OK;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return SM_OK;
+  }
+  __half* whi = (__half*)p;
+  __half* wlo = whi + (size_t)N * K;
+  int64_t row0 = 0;
+  for (int i = 0; i < nw; ++i) {
+    const int Ni = Ws[i]->N();
+    const int64_t units = (int64_t)Ni * K / 32;
+    weight_split_kernel<<<(int)std::min<int64_t>((units + 255) / 256, 148 * 16), 256, 0, st>>>(
+        *Ws[i], Ni, K, (uint4*)(whi + row0 * K), (uint4*)(wlo + row0 * K));
+    if (n_launch) ++*n_launch;
+    row0 += Ni;
+  }
+  SM_CUDA_TRY(cudaGetLastError());
+  SM_CUDA_TRY(cudaStreamSynchronize(st));  // complete before any other stream can find the entry
+  g_planes.push_back(PlaneEntry{keys, dev, whi, wlo});
+  *hi = whi;
+  *lo = wlo;
+  return SM_OK;
+}
+
 }  // namespace
+
+void gemm_tc_release_weight(const void* data) {
+  std::lock_guard<std::mutex> g(g_plane_mu);
+  for (size_t i = 0; i < g_planes.size();) {
+    const auto& k = g_planes[i].keys;
+    if (std::find(k.begin(), k.end(), data) != k.end()) {
+      int prev = -1;
+      cudaGetDevice(&prev);
+      if (prev != g_planes[i].dev) cudaSetDevice(g_planes[i].dev);
+      cudaFree(g_planes[i].hi);
+      if (prev >= 0 && prev != g_planes[i].dev) cudaSetDevice(prev);
+      g_planes.erase(g_planes.begin() + i);
+    } else {
+      ++i;
+    }
+  }
+}
 
 bool gemm_tc_supports(const DevWeight& W, int M) {
   if (W.layout != SM_LAYOUT_INTENDED || M < 16) return false;
@@ -697,20 +779,23 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
   // more than one 128-row tile of x: dequantize W once into fp16 planes and feed
   // both operands by TMA; otherwise dequantize each weight tile in the kernel
   const bool wt = M > BM;
-  const int64_t n = (int64_t)M * K, nw_el = wt ? (int64_t)N * K : 0;
+  __half *rhi = nullptr, *rlo = nullptr;
+  if (wt && planes_enabled()) SM_TRY(resident_planes(Ws, nw, N, K, dev, st, &rhi, &rlo, n_launch));
+  const bool resident = rhi != nullptr;
+  const int64_t n = (int64_t)M * K, nw_el = wt && !resident ? (int64_t)N * K : 0;
   void* planes = nullptr;
   SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)(n + nw_el) * 4, st));
   __half* hi = (__half*)planes;
   __half* lo = hi + n;
-  __half* whi = lo + n;
-  __half* wlo = whi + nw_el;
+  __half* whi = resident ? rhi : lo + n;
+  __half* wlo = resident ? rlo : whi + nw_el;
   int rc = SM_OK;
   {
     const int64_t n4 = n / 4;
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
     gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
     if (n_launch) ++*n_launch;
-    if (wt) {
+    if (wt && !resident) {
       int64_t row0 = 0;
       for (int i = 0; i < nw; ++i) {
         const int Ni = Ws[i]->N();

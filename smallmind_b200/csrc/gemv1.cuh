@@ -59,6 +59,9 @@ int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy,
 // up to 3 weights with the same K stacked along N, each with its own output (ys[i], row stride ldys[i]);
 // every weight but the last must have N % 128 == 0
 bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M);
+// Drops the resident fp16 planes of every weight group that contains this weight
+// (called before the weight's memory is freed).
+void gemm_tc_release_weight(const void* data);
 int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
                          int accumulate, int* status, cudaStream_t st, int* n_launch);
 // Q4_K (INTENDED) y[m] (+)= W x[m] for M rows of x (stride K), y rows of stride ldy
