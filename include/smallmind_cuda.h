@@ -239,6 +239,16 @@ SM_API int sm_kv_read(sm_kv* kv, int layer, int seq_id, int start, int count, fl
  * a host array; last_logits / next_token are host pointers (either may be NULL). */
 SM_API int sm_prefill(sm_model* m, sm_kv* kv, int seq_id, const int* tokens, int n_tokens, float* last_logits,
                       int* next_token);
+/* Several prompts in one pass (batched prefill, the multi-sequence form of
+ * sm_prefill; BatchedInferenceEngine.cs:226-233 leaves batching unimplemented):
+ * prompt i appends n_tokens[i] tokens to seq_ids[i]'s cache at its current
+ * length.  tokens holds the prompts back to back.  The linear layers run once
+ * over all the rows; attention runs per prompt over its own slot.  last_logits
+ * [n][vocab] and/or next_tokens[n] (greedy) are host pointers (either may be
+ * NULL).  Each sequence id appears at most once. */
+SM_API int sm_prefill_batch(sm_model* m, sm_kv* kv, const int* seq_ids, const int* tokens, const int* n_tokens,
+                            int n, float* last_logits, int* next_tokens);
+
 /* One decode step for n sequences (InferenceSession.GenerateNextTokenAsync decode
  * branch, InferenceSession.cs:527-563, batched): token[i] is appended to
  * seq_ids[i]; logits [n][vocab] and/or greedy argmax next_tokens[n] (TopK = 1,

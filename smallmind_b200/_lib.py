@@ -79,6 +79,7 @@ SIGNATURES = {
     "sm_kv_reset": (i, [vp, i]),
     "sm_kv_length": (i, [vp, i, C.POINTER(C.c_int)]),
     "sm_kv_truncate": (i, [vp, i, i]),
+    "sm_prefill_batch": (i, [vp, vp, vp, vp, vp, i, vp, vp]),
     "sm_kv_slide": (i, [vp, i, i]),
     "sm_kv_read": (i, [vp, i, i, i, i, vp, vp]),
     "sm_prefill": (i, [vp, vp, i, vp, i, vp, vp]),

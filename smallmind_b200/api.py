@@ -289,6 +289,19 @@ class KVCache:
                                    _p(logits) if want_logits else None, _p(nxt)), "sm_prefill")
         return int(nxt[0]), logits
 
+    def prefill_batch(self, seq_ids, prompts, want_logits: bool = True):
+        """Several prompts in one pass (sm_prefill_batch): returns (next tokens [n], logits [n, vocab])."""
+        s = np.ascontiguousarray(seq_ids, np.int32)
+        ps = [np.asarray(p, np.int32).reshape(-1) for p in prompts]
+        lens = np.array([p.size for p in ps], np.int32)
+        toks = np.ascontiguousarray(np.concatenate(ps))
+        n = s.size
+        logits = np.empty((n, self.model.cfg["vocab_size"]), np.float32) if want_logits else None
+        nxt = np.zeros(n, np.int32)
+        L.check(L.lib().sm_prefill_batch(self.model.handle, self.handle, _p(s), _p(toks), _p(lens), n,
+                                         _p(logits) if want_logits else None, _p(nxt)), "sm_prefill_batch")
+        return nxt, logits
+
     def decode(self, seq_ids, tokens, want_logits: bool = True):
         s = np.ascontiguousarray(seq_ids, np.int32)
         t = np.ascontiguousarray(tokens, np.int32)

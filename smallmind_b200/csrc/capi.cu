@@ -809,8 +809,8 @@ int head_m1(sm_model* m, const float* x_row, int& nl) {
 }
 
 // The transformer stack over `rows` token rows whose tok/seq/pos/lens are in
-// work.ints.  prefill: all rows belong to one sequence (prefill_seq) at
-// positions pos0..pos0+rows-1; otherwise one row per sequence (decode).
+// work.ints.  prefill: the rows are one or more prompts (PrefillSeg), each at
+// positions pos0..pos0+T-1 of its slot; otherwise one row per sequence (decode).
 // Projections that share their input (Q|K|V, gate|up): one tensor-core GEMM over
 // the stacked weights when it applies, else one launch per weight.
 int matmul_multi(const DevWeight* const* ws, float* const* ys, const int* ld, int nw, const float* x, int rows,
@@ -822,7 +822,15 @@ int matmul_multi(const DevWeight* const* ws, float* const* ys, const int* ld, in
   return SM_OK;
 }
 
-int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int pos0, int& nl) {
+// One prompt of a prefill: its rows [r0, r0 + T) of the step, its slot and its first position.
+struct PrefillSeg {
+  int seq, pos0, r0, T;
+};
+
+// rows: the step's token rows.  Prefill: segs[0..nsegs) cover the rows (one or more prompts,
+// each attending causally to its own slot); decode: segs is null (one row per sequence).
+int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs, int& nl) {
+  const bool prefill = segs != nullptr;
   const auto& c = m->cfg;
   Work& w = m->work;
   cudaStream_t st = m->ctx->stream;
@@ -854,9 +862,12 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
                                  kc, vc, mt, st));
     ++nl;
     if (prefill) {
-      SM_TRY(launch_attention_prefill(w.qkv, QS, kc + seq_stride * prefill_seq, vc + seq_stride * prefill_seq, hd,
-                                      head_stride, w.att, qd, rows, pos0 + rows, c.n_heads, c.n_kv_heads, hd, st,
-                                      &nl));
+      for (int i = 0; i < nsegs; ++i) {
+        const PrefillSeg& sg = segs[i];
+        SM_TRY(launch_attention_prefill(w.qkv + (size_t)sg.r0 * QS, QS, kc + seq_stride * sg.seq,
+                                        vc + seq_stride * sg.seq, hd, head_stride, w.att + (size_t)sg.r0 * qd, qd,
+                                        sg.T, sg.pos0 + sg.T, c.n_heads, c.n_kv_heads, hd, st, &nl));
+      }
     } else {
       int arc = launch_attention_decode_cluster(w.qkv, QS, kc, vc, seq_stride, hd, head_stride, mt, w.att, qd,
                                                 w.lens(), w.seq(), rows, c.n_heads, c.n_kv_heads, hd, st, &nl);
@@ -880,12 +891,21 @@ int forward(sm_model* m, sm_kv* kv, int rows, bool prefill, int prefill_seq, int
     ++nl;
     SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.x, rows, H, 1, st, &nl));  // + residual (:184)
   }
-  // final norm + LM head: last row only for prefill (what the loop reads), every row for decode
-  const int first = prefill ? rows - 1 : 0;
-  const int nrows = prefill ? 1 : rows;
-  if (m1 && nrows == 1) return head_m1(m, w.x + (size_t)first * H, nl);
-  SM_TRY(launch_rmsnorm(w.x + (size_t)first * H, m->out_norm, w.h, nrows, H, c.norm_eps, st));
-  ++nl;
+  // final norm + LM head: each prompt's last row only for prefill (what the loop reads), every
+  // row for decode
+  const int nrows = prefill ? nsegs : rows;
+  if (prefill && nsegs == 1 && m1) return head_m1(m, w.x + (size_t)(segs[0].r0 + segs[0].T - 1) * H, nl);
+  if (!prefill && m1 && rows == 1) return head_m1(m, w.x, nl);
+  if (prefill) {
+    for (int i = 0; i < nsegs; ++i) {
+      SM_TRY(launch_rmsnorm(w.x + (size_t)(segs[i].r0 + segs[i].T - 1) * H, m->out_norm, w.h + (size_t)i * H, 1, H,
+                            c.norm_eps, st));
+      ++nl;
+    }
+  } else {
+    SM_TRY(launch_rmsnorm(w.x, m->out_norm, w.h, nrows, H, c.norm_eps, st));
+    ++nl;
+  }
   SM_TRY(launch_matmul(*m->output, w.h, w.logits, nrows, c.vocab_size, 0, st, &nl));
   SM_TRY(launch_argmax(w.logits, nrows, c.vocab_size, w.amax(), st));
   ++nl;
@@ -1334,7 +1354,8 @@ SM_API int sm_prefill(sm_model* m, sm_kv* kv, int seq, const int* tokens, int T,
   SM_CUDA_TRY(cudaMemcpyAsync(w.pos(), staging.data() + 2 * T, sizeof(int) * T, cudaMemcpyHostToDevice, st));
   SM_CUDA_TRY(cudaMemcpyAsync(w.lens(), staging.data() + 3 * T, sizeof(int) * T, cudaMemcpyHostToDevice, st));
   int nl = 0;
-  SM_TRY(forward(m, kv, T, true, seq, pos0, nl));
+  const PrefillSeg seg{seq, pos0, 0, T};
+  SM_TRY(forward(m, kv, T, &seg, 1, nl));
   m->ctx->launches += nl;
   const int newlen = pos0 + T;
   SM_CUDA_TRY(cudaMemcpyAsync(kv->len_dev + seq, &newlen, sizeof(int), cudaMemcpyHostToDevice, st));
@@ -1343,6 +1364,65 @@ SM_API int sm_prefill(sm_model* m, sm_kv* kv, int seq, const int* tokens, int T,
   if (next_token) SM_CUDA_TRY(cudaMemcpyAsync(next_token, w.amax(), sizeof(int), cudaMemcpyDeviceToHost, st));
   SM_CUDA_TRY(cudaStreamSynchronize(st));
   kv->len_host[seq] = newlen;
+  return SM_OK;
+}
+
+SM_API int sm_prefill_batch(sm_model* m, sm_kv* kv, const int* seq_ids, const int* tokens, const int* n_tokens,
+                            int n, float* last_logits, int* next_tokens) {
+  if (!m || !kv || !seq_ids || !tokens || !n_tokens) return fail(SM_ERR_INVALID_ARG, "prefill_batch: null argument");
+  if (!m->finalized) return fail(SM_ERR_STATE, "prefill_batch: model not finalized");
+  if (kv->m != m) return fail(SM_ERR_INVALID_ARG, "prefill_batch: cache belongs to another model");
+  if (n <= 0 || n > kv->max_seqs) return fail(SM_ERR_SHAPE, "prefill_batch: prompt count out of range");
+  DeviceGuard g(m->ctx->device);
+  SM_TRY(kv_sync_host(kv));
+  std::vector<PrefillSeg> segs(n);
+  std::vector<char> seen(kv->max_seqs, 0);
+  int rows = 0;
+  for (int i = 0; i < n; ++i) {
+    const int s = seq_ids[i], T = n_tokens[i];
+    if (s < 0 || s >= kv->max_seqs) return fail(SM_ERR_INVALID_ARG, "prefill_batch: bad sequence id");
+    if (seen[s]) return fail(SM_ERR_INVALID_ARG, "prefill_batch: a sequence appears twice");
+    seen[s] = 1;
+    if (T <= 0) return fail(SM_ERR_SHAPE, "prefill_batch: need at least one token per prompt");
+    // TransformerModel.cs:280-283, per prompt
+    if (kv->len_host[s] + T > kv->max_tokens)
+      return fail(SM_ERR_SHAPE, "prefill_batch: Sequence length + offset exceeds block size");
+    segs[i] = PrefillSeg{s, kv->len_host[s], rows, T};
+    rows += T;
+  }
+  for (int r = 0; r < rows; ++r)
+    if (tokens[r] < 0 || tokens[r] >= m->cfg.vocab_size)
+      return fail(SM_ERR_INVALID_ARG, "prefill_batch: token id out of range");
+  SM_TRY(work_reserve(m, rows, n, 1, kv->max_tokens));
+  cudaStream_t st = m->ctx->stream;
+  Work& w = m->work;
+  std::vector<int> staging((size_t)4 * rows);
+  for (const auto& sg : segs)
+    for (int i = 0; i < sg.T; ++i) {
+      const int r = sg.r0 + i;
+      staging[r] = tokens[r];
+      staging[rows + r] = sg.seq;
+      staging[2 * rows + r] = sg.pos0 + i;
+      staging[3 * rows + r] = sg.pos0 + i + 1;
+    }
+  SM_CUDA_TRY(cudaMemcpyAsync(w.tok(), staging.data(), sizeof(int) * rows, cudaMemcpyHostToDevice, st));
+  SM_CUDA_TRY(cudaMemcpyAsync(w.seq(), staging.data() + rows, sizeof(int) * rows, cudaMemcpyHostToDevice, st));
+  SM_CUDA_TRY(cudaMemcpyAsync(w.pos(), staging.data() + 2 * rows, sizeof(int) * rows, cudaMemcpyHostToDevice, st));
+  SM_CUDA_TRY(cudaMemcpyAsync(w.lens(), staging.data() + 3 * rows, sizeof(int) * rows, cudaMemcpyHostToDevice, st));
+  int nl = 0;
+  SM_TRY(forward(m, kv, rows, segs.data(), n, nl));
+  m->ctx->launches += nl;
+  std::vector<int> newlen(n);
+  for (int i = 0; i < n; ++i) {
+    newlen[i] = segs[i].pos0 + segs[i].T;
+    SM_CUDA_TRY(cudaMemcpyAsync(kv->len_dev + segs[i].seq, &newlen[i], sizeof(int), cudaMemcpyHostToDevice, st));
+  }
+  if (last_logits)
+    SM_CUDA_TRY(cudaMemcpyAsync(last_logits, w.logits, sizeof(float) * (size_t)n * m->cfg.vocab_size,
+                                cudaMemcpyDeviceToHost, st));
+  if (next_tokens) SM_CUDA_TRY(cudaMemcpyAsync(next_tokens, w.amax(), sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+  SM_CUDA_TRY(cudaStreamSynchronize(st));
+  for (int i = 0; i < n; ++i) kv->len_host[segs[i].seq] = newlen[i];
   return SM_OK;
 }
 
@@ -1392,7 +1472,7 @@ SM_API int sm_decode(sm_model* m, sm_kv* kv, const int* seq_ids, const int* toke
     decode_prep_kernel<<<ceil_div(n, 128), 128, 0, st>>>(w.seq(), w.pos(), w.lens(), kv->len_dev, n, kv->max_tokens,
                                                           m->ctx->dev_status);
     ++nl;
-    SM_TRY(forward(m, kv, n, false, 0, 0, nl));
+    SM_TRY(forward(m, kv, n, nullptr, 0, nl));
     decode_commit_kernel<<<ceil_div(n, 128), 128, 0, st>>>(w.seq(), kv->len_dev, n, kv->max_tokens);
     ++nl;
     SM_CUDA_TRY(cudaGetLastError());

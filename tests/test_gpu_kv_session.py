@@ -109,3 +109,42 @@ def test_kv_read_slide_truncate(ctx, O):
     assert kv.length(2) == 0
     kv.close()
     model.close()
+
+
+def test_prefill_batch_matches_oracle(ctx, O):
+    """Several prompts in one pass (sm_prefill_batch), ragged lengths, slots in any
+    order, one slot already holding context: each prompt's last-position logits
+    and the greedy decode that follows match the oracle's full recompute."""
+    import smallmind_b200 as sm
+    host, model = _model(ctx, O)
+    kv = sm.KVCache(model, 5, 96)
+    rs = np.random.RandomState(12)
+    V = CFG["vocab_size"]
+    pre = list(rs.randint(0, V, 6))
+    kv.prefill(3, np.array(pre, np.int32), want_logits=False)
+    seqs = [4, 0, 3, 2]
+    prompts = [list(rs.randint(0, V, n)) for n in (9, 1, 5, 17)]
+    nxt, logits = kv.prefill_batch(seqs, prompts)
+    hist = {}
+    for i, s in enumerate(seqs):
+        h = (pre if s == 3 else []) + prompts[i]
+        ref = O.model_forward(host, np.array(h, np.int32), 1)[0]
+        assert cosine(logits[i], ref) >= 0.9999, s
+        assert nxt[i] == int(np.argmax(ref)), s
+        hist[s] = h + [int(nxt[i])]
+        assert kv.length(s) == len(h)
+    # decode all four together from there
+    toks = [hist[s][-1] for s in seqs]
+    for step in range(3):
+        t, lg = kv.decode(seqs, toks)
+        for i, s in enumerate(seqs):
+            ref = O.model_forward(host, np.array(hist[s], np.int32), 1)[0]
+            assert cosine(lg[i], ref) >= 0.9999 and t[i] == int(np.argmax(ref)), (step, s)
+            hist[s].append(int(t[i]))
+        toks = [int(x) for x in t]
+    with pytest.raises(Exception):
+        kv.prefill_batch([1, 1], [[1, 2], [3]])  # a slot twice
+    with pytest.raises(Exception):
+        kv.prefill_batch([1], [list(range(100))])  # past the slot's capacity
+    kv.close()
+    model.close()
