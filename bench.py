@@ -202,6 +202,42 @@ def time_gemv(sm, ctx, ws, torch, reps=5):
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle)
+def time_attention_decode(sm, ctx, torch, stream):
+    """op-level decode attention (32 q / 4 kv heads, hd 64, fp32 K/V N(0,1)).
+    Device time per call (CUDA events, 20 calls after 3 warm-up) and the K/V bytes it reads."""
+    nH, nKv, hd = 32, 4, 64
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(4)
+    cases = [(f"b1_ctx{c}", [c]) for c in (512, 1024, 2048)]
+    rs = np.random.RandomState(16)
+    cases.append(("b16_ragged_256_2048", list(rs.randint(256, 2049, 16))))
+    for name, lens in cases:
+        B, mc = len(lens), int(max(lens))
+        kc = torch.randn(B, nKv, mc, hd, device="cuda", generator=g)
+        vc = torch.randn(B, nKv, mc, hd, device="cuda", generator=g)
+        q = torch.randn(B, nH * hd, device="cuda", generator=g)
+        o = torch.empty_like(q)
+        ln = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+
+        def call():
+            rc = sm.lib().sm_attention_decode(ctx.handle, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(),
+                                              ln.data_ptr(), B, mc, nH, nKv, hd)
+            assert rc == 0, sm.last_error()
+        for _ in range(3):
+            call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(20):
+            call()
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / 20 * 1e3
+        byts = sum(lens) * nKv * hd * 4 * 2
+        out[name] = {"us": round(us, 2), "gbs": round(byts / (us * 1e-6) / 1e9, 1)}
+    return out
+
+
 def cpu_decode_sample(cfg, ctx_len, steps, threads):
     from oracle import oracle as O
     schemes = {k: getattr(O, v) for k, v in SCHEMES.items()}
@@ -481,6 +517,8 @@ def run_ours(args):
     except Exception:
         pass
 
+    attn = time_attention_decode(sm, ctx, torch, stream)
+
     # bs64 decode (short context) and per-token bytes
     bs = 64
     kv3 = sm.KVCache(model, bs, 64)
@@ -597,6 +635,7 @@ def run_ours(args):
             "decode_hbm_frac": round(wbytes / (ms_per_step * 1e-3) / 1e9 / hbm, 4),
             "bs64_decode_tok_s": round(bs64_tps, 1),
             "serving_256x512p128": serving,
+            "attention_decode": attn,
             "smollm_q8_bs1_decode_tok_s": round(smol_tps, 1),
             "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
             "gpu_launches": int(launches_timed),
