@@ -313,14 +313,17 @@ __global__ void __launch_bounds__(ST, 1) sample_kernel(const __grid_constant__ S
   const int c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
   // 5. top-p (:862-907): the cut value tau = the largest p with sum(p >= tau) >= top_p
   if (p.top_p < 1.0) {
-    const Found f = key_search<true>(reinterpret_cast<const uint32_t*>(P), V, p.top_p, 30, slist, sredw, sredc,
+    // top_p <= 0: the reference's first sorted token already reaches it (:891-896), so only the top
+    // probability is kept; a tiny positive target gives that cut
+    const double need = p.top_p > 0.0 ? p.top_p : 1e-300;
+    const Found f = key_search<true>(reinterpret_cast<const uint32_t*>(P), V, need, 30, slist, sredw, sredc,
                                      &slist_n, &sfound);
     const float tau = __uint_as_float(f.x);
     const double above = f.above;
     const int neq = f.eq;
     // keep the first m ties at the cut (index order)
     int m = neq;
-    if (tau > 0.f && above < p.top_p) m = min(neq, max(1, (int)ceil((p.top_p - above) / (double)tau)));
+    if (tau > 0.f && above < need) m = min(neq, max(1, (int)ceil((need - above) / (double)tau)));
     int mine = 0;
     for (int i = c0; i < c1; ++i) mine += P[i] == tau;
     int before = (int)block_exclusive_scan((double)mine, redd);

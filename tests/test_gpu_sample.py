@@ -95,7 +95,8 @@ def test_sample_ties_and_edges(ctx, O):
     V = 1000
     logits = rs.randint(-3, 4, (3, V)).astype(np.float32)  # many equal values: the k-th value has ties
     targets = np.array([0.25, 0.5, 0.999], np.float64)
-    for case in (dict(top_k=5), dict(top_k=300), dict(top_k=999), dict(top_k=V + 5)):
+    for case in (dict(top_k=5), dict(top_k=300), dict(top_k=999), dict(top_k=V + 5), dict(top_p=0.0),
+                 dict(top_p=1e-9, top_k=3)):
         toks, probs = sm.sample(ctx, logits, _opts(sm, case), targets, want_probs=True)
         for r in range(3):
             t, p = O.sample(logits[r], targets[r], **case)
