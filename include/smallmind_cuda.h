@@ -281,9 +281,9 @@ typedef struct sm_sampling_params {
  * logits [n_rows][vocab] (vocab <= SM_SAMPLE_MAX_VOCAB); targets[n_rows] are the
  * uniform draws in [0, 1) that SampleFromProbs compares the cumulative sum with
  * (the reference takes them from DeterministicRng.NextDouble); context
- * [n_rows][context_stride] with context_lens[n_rows] are each row's token history
- * for the penalties (NULL when no penalty is set; ids outside [0, vocab) are
- * skipped).  tokens[n_rows] receives the samples; probs (may be NULL)
+ * [n_rows][context_stride] with context_lens[n_rows] (each <= context_stride) are
+ * each row's token history for the penalties (NULL when no penalty is set; ids
+ * outside [0, vocab) are skipped).  tokens[n_rows] receives the samples; probs (may be NULL)
  * [n_rows][vocab] the final distribution.  flags: SM_PTR_HOST (all arrays host,
  * synchronous) or SM_PTR_DEVICE (all arrays device; stream-ordered, no
  * allocation). */

@@ -13,6 +13,7 @@ Everything runs in libsmallmind_cuda.so; there is no CPU path.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 from enum import IntEnum
 
@@ -419,7 +420,9 @@ class InferenceSession:
     def generate_sampled(self, prompt_ids, max_new_tokens: int, options: SamplingOptions):
         """GenerateNextTokenAsync with the full sampling pipeline on the device
         (sm_sample); the context for the penalties is prompt + generated tokens."""
-        rng = DeterministicRng(options.seed if options.seed is not None else 0)
+        # seed unset: the reference falls back to an unseeded System.Random (InferenceSession.cs:109)
+        seed = options.seed if options.seed is not None else int.from_bytes(os.urandom(4), "little", signed=True)
+        rng = DeterministicRng(seed)
         ctx = self.kv.model.ctx
         self.kv.reset(self.seq)
         context = [int(t) for t in prompt_ids]
