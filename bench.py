@@ -238,6 +238,39 @@ def time_attention_decode(sm, ctx, torch, stream):
     return out
 
 
+def time_sample(sm, ctx, torch, stream):
+    """Device sampling (sm_sample, SM_PTR_DEVICE) per option set at vocab 32000 / 49152:
+    device time per call (CUDA events, 20 calls after 3 warm-up), one row."""
+    import ctypes as C
+
+    from smallmind_b200 import _lib as L
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for V in (32000, 49152):
+        lg = torch.randn(1, V, device="cuda", generator=g) * 3
+        tg = torch.rand(1, dtype=torch.float64, device="cuda", generator=g)
+        tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for name, o in [("plain", {}), ("top_k40", dict(top_k=40, temperature=0.8)), ("top_p0.9", dict(top_p=0.9)),
+                        ("k40_p0.95", dict(top_k=40, top_p=0.95, temperature=0.8))]:
+            prm = sm.SamplingOptions(**o).params()
+            torch.cuda.synchronize()
+
+            def call():
+                rc = L.lib().sm_sample(ctx.handle, lg.data_ptr(), 1, V, C.byref(prm), None, None, 0, tg.data_ptr(),
+                                       tok.data_ptr(), None, L.PTR_DEVICE)
+                assert rc == 0, sm.last_error()
+            for _ in range(3):
+                call()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(20):
+                call()
+            e1.record(stream)
+            e1.synchronize()
+            out[f"V{V}_{name}"] = round(e0.elapsed_time(e1) / 20 * 1e3, 2)
+    return out
+
+
 def cpu_decode_sample(cfg, ctx_len, steps, threads):
     from oracle import oracle as O
     schemes = {k: getattr(O, v) for k, v in SCHEMES.items()}
@@ -412,6 +445,13 @@ def run_ours(args):
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     torch.cuda.set_stream(stream)
+    if args.attn_only or args.sample_only:
+        r = time_attention_decode(sm, ctx, torch, stream) if args.attn_only else time_sample(sm, ctx, torch, stream)
+        if rank == 0:
+            print(json.dumps({"attention_decode" if args.attn_only else "sample_us": r}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     model, weights = build_gpu_model(sm, ctx, cfg)
     max_tok = args.prompt + args.warmup + args.steps + 8
@@ -655,6 +695,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-serving", action="store_true", help="skip the 256-sequence serving run (config 5)")
+    ap.add_argument("--attn-only", action="store_true", help="time the config-4 decode attention cases and exit")
+    ap.add_argument("--sample-only", action="store_true", help="time device sampling (sm_sample) and exit")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length before the timed decode steps")
     ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
     ap.add_argument("--gemm-sweep", action="store_true",
