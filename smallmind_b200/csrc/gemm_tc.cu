@@ -776,12 +776,14 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     attr_set[dev] = true;
   }
-  // more than one 128-row tile of x: dequantize W once into fp16 planes and feed
-  // both operands by TMA; otherwise dequantize each weight tile in the kernel
-  const bool wt = M > BM;
+  // More than one 128-row tile of x: the weights come as fp16 planes (resident, or split for this
+  // call).  One tile (M <= 128): resident planes when they exist or can be made, since reading
+  // 4 B per weight by TMA (~1.6 T weights/s) beats dequantizing in the loader warps (~0.5 T/s);
+  // otherwise the loaders dequantize.
   __half *rhi = nullptr, *rlo = nullptr;
-  if (wt && planes_enabled()) SM_TRY(resident_planes(Ws, nw, N, K, dev, st, &rhi, &rlo, n_launch));
+  if (planes_enabled()) SM_TRY(resident_planes(Ws, nw, N, K, dev, st, &rhi, &rlo, n_launch));
   const bool resident = rhi != nullptr;
+  const bool wt = M > BM || resident;
   const int64_t n = (int64_t)M * K, nw_el = wt && !resident ? (int64_t)N * K : 0;
   void* planes = nullptr;
   SM_CUDA_TRY(cudaMallocAsync(&planes, (size_t)(n + nw_el) * 4, st));

@@ -66,3 +66,16 @@ def test_gemm_tc_long_k_many_slices(ctx, O):
     # (the accumulating form, y += x W^T, runs in the model prefill tests)
     out, ref = _run(ctx, O, "Q6_K", 32, 2048, 256, seed=11)
     assert rel_err(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("planes", ["0", "1"])
+@pytest.mark.parametrize("scheme", ["Q4_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0"])
+@pytest.mark.parametrize("m,k,n", [(16, 512, 256), (64, 1024, 384), (128, 768, 200)])
+def test_gemm_tc_one_tile_both_weight_paths(ctx, O, monkeypatch, planes, scheme, m, k, n):
+    """M <= 128: with resident fp16 weight planes (SMALLMIND_WEIGHT_PLANES unset / 1) the
+    weights come by TMA from the planes; with SMALLMIND_WEIGHT_PLANES=0 the loader warps
+    dequantize each weight tile.  Both within 1e-4 of the oracle."""
+    monkeypatch.setenv("SMALLMIND_WEIGHT_PLANES", planes)
+    out, ref = _run(ctx, O, scheme, m, k, n, seed=m + k)
+    assert np.isfinite(out).all()
+    assert rel_err(out, ref) <= TOL
