@@ -43,6 +43,14 @@ METRIC = "decode tok/s (bs1, bs64) + Q4_K GEMV HBM GB/s vs peak; prefill tok/s"
 BYTES = {"Q4_K": 144 / 256, "Q6_K": 210 / 256, "Q8_0": 1.0 + 4 / 32, "Q4_0": 0.5 + 4 / 32}
 
 
+def bench_config(world):
+    """The `config` object of both arms' JSON lines (the same workload either way)."""
+    return {"workload": "TinyLlama-1.1B-shaped Q4_K_M decode, bs1 per GPU, ctx 2048",
+            "model": "TinyLlama-1.1B-shaped (H2048 L22 32q/4kv FFN5632 V32000)", "global_batch": world,
+            "seq_len": PROMPT, "parallelism": f"replica x{world} (sequence sharding)",
+            "l2": "no flush: 667 MB of weights per step > 126 MB L2"}
+
+
 def linear_shapes(c):
     H, F, V = c["hidden"], c["ffn_hidden"], c["vocab_size"]
     qd, kd = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
@@ -77,49 +85,57 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    def __init__(self, out_path):
-        self.out_path = out_path
-        self.proc = None
+    """SM clock, power and throttle reasons sampled every `interval_s` through NVML on a
+    background thread while the timed region runs (read-only queries; nothing is set)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
+
+    def __init__(self, device, interval_s=0.002):
+        self.device, self.interval_s = device, interval_s
+        self.rows = []
+        self.err = None
+        self._stop = None
+
+    def _run(self):
+        import pynvml as N
+        try:
+            h = N.nvmlDeviceGetHandleByIndex(self.device)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                mhz = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                rs = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((mhz, rs))
+                self._stop.wait(self.interval_s)
+        except Exception as e:  # no NVML: the line carries the error instead of clocks
+            self.err = repr(e)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
+        self.max_mhz = None
         try:
-            self.f = open(self.out_path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml as N
+            N.nvmlInit()
+        except Exception as e:
+            self.err = repr(e)
+            return self
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.f.close()
+        if self._stop is not None:
+            self._stop.set()
+            self._t.join(timeout=5)
 
-    def summary(self, device):
-        try:
-            rows = [l.split(",") for l in open(self.out_path).read().strip().splitlines()]
-        except Exception:
-            return None
-        rows = [[x.strip() for x in r] for r in rows if len(r) >= 9 and r[0].strip() == str(device)]
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(rows)}
+    def summary(self):
+        if not self.rows:
+            return {"error": self.err or "no samples"}
+        mhz = [r[0] for r in self.rows]
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(r[1] & bit for r in self.rows))
+        return {"sm_mhz": float(np.median(mhz)), "sm_min_mhz": float(min(mhz)), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 2 ms interval, timed region"}
 
 
 # ---------------------------------------------------------------- model build on the GPU
@@ -271,24 +287,34 @@ def time_sample(sm, ctx, torch, stream):
     return out
 
 
-def cpu_decode_sample(cfg, ctx_len, steps, threads):
+def cpu_decode_sample(cfg, ctx_len, steps, threads, warmup=1, linear_threads=0, host=None):
+    """Greedy bs1 decode steps of the oracle's KV-cached forward at context ctx_len (a synthetic
+    cache), after `warmup` untimed steps.  linear_threads 0 splits the quantized linears' rows
+    over `threads`; 1 runs them single-threaded as the reference does."""
     from oracle import oracle as O
     schemes = {k: getattr(O, v) for k, v in SCHEMES.items()}
     t0 = time.time()
-    host = O.make_model(cfg, schemes, seed=1234, threads=threads)
+    if host is None:
+        host = O.make_model(cfg, schemes, seed=1234, threads=threads)
     build_s = time.time() - t0
     dec = O.KVDecoder(host, threads=threads)
     rs = np.random.RandomState(0)
     dec.kv[:] = rs.standard_normal(dec.kv.size).astype(np.float32)  # synthetic cache of ctx_len positions
-    dec.pos = ctx_len
-    tok = 1
-    dec.step([tok])  # warm
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        lg = dec.step([tok])
-        tok = int(np.argmax(lg))
-    dt = time.perf_counter() - t0
-    return steps / dt, dt, build_s
+    O.set_linear_threads(linear_threads)
+    try:
+        tok = 1
+        for _ in range(max(1, warmup)):
+            dec.pos = ctx_len
+            dec.step([tok])
+        dec.pos = ctx_len
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            lg = dec.step([tok])
+            tok = int(np.argmax(lg))
+        dt = time.perf_counter() - t0
+    finally:
+        O.set_linear_threads(0)
+    return steps / dt, dt, build_s, host
 
 
 def make_weights(sm, ctx, torch, scheme, rows, cols, count, seed=7):
@@ -318,21 +344,26 @@ def make_weights(sm, ctx, torch, scheme, rows, cols, count, seed=7):
     return out
 
 
-def run_gemv_sweep(args):
-    """Op-sweep (BASELINE config 2) GEMV at M = 1: device time per launch from a CUDA graph over
-    enough distinct weights to exceed L2."""
-    import torch
+SWEEP_SHAPES = ((2048, 2048), (2048, 5632), (5632, 2048), (4096, 11008))
+SWEEP_SCHEMES = ("Q4_K", "Q6_K", "Q8_0", "Q4_0")
 
-    import smallmind_b200 as sm
-    ctx = sm.CudaContext(0)
-    stream = torch.cuda.Stream()
-    ctx.set_stream(stream.cuda_stream)
-    torch.cuda.set_stream(stream)
+
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def gemv_sweep(sm, ctx, torch, only=None):
+    """Op-sweep (BASELINE config 2) GEMV at M = 1: device time per launch from a CUDA graph over
+    enough distinct weights to exceed L2; HBM GB/s of packed weights + x + y."""
     hbm, _ = peaks()
     res = {}
-    for scheme in ("Q4_K", "Q6_K", "Q8_0", "Q4_0"):
-        for (K, N) in ((2048, 2048), (2048, 5632), (5632, 2048), (4096, 11008)):
-            if args.gemv_only and args.gemv_only != f"{scheme} {K}x{N}":
+    for scheme in SWEEP_SCHEMES:
+        for (K, N) in SWEEP_SHAPES:
+            if only and only != f"{scheme} {K}x{N}":
                 continue
             nb = N * K * BYTES[scheme]
             count = max(2, int(300e6 // nb) + 1)
@@ -342,36 +373,24 @@ def run_gemv_sweep(args):
                                        "frac": round(alg / (ms * 1e-3) / 1e9 / hbm, 3)}
             for w in ws:
                 w.close()
-    print(json.dumps({"gemv_sweep_m1": res, "peak_gbs": hbm}), flush=True)
+    return res
 
 
-def run_gemm_sweep(args):
+def gemm_sweep(sm, ctx, torch, stream, only=None, ms_list=(8, 64, 512, 2048)):
     """Op-sweep at M = 8, 64 (decode batches, HBM-bound: GB/s of packed weights +
     activations) and M = 512, 2048 (prefill, tensor-bound: algorithmic 2*M*K*N FLOP/s against the
-    measured dense bf16 peak).  Device time per call (fp16 split of x + tcgen05 GEMM for M >= 16) from
-    a CUDA graph over rotating weights."""
-    import torch
-
-    import smallmind_b200 as sm
-    ctx = sm.CudaContext(0)
-    stream = torch.cuda.Stream()
-    ctx.set_stream(stream.cuda_stream)
-    torch.cuda.set_stream(stream)
+    measured dense bf16 peak).  Device time per call from a CUDA graph over rotating weights."""
     hbm, _ = peaks()
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            tflops = float(json.load(f)["bf16_tflops"])
-    except Exception:
-        tflops = 1590.0
+    tflops, _ = tensor_peak()
     res = {}
-    for scheme in ("Q4_K", "Q6_K", "Q8_0", "Q4_0"):
-        for (K, N) in ((2048, 2048), (2048, 5632), (5632, 2048), (4096, 11008)):
-            if args.gemv_only and not args.gemv_only.startswith(f"{scheme} {K}x{N}"):
+    for scheme in SWEEP_SCHEMES:
+        for (K, N) in SWEEP_SHAPES:
+            if only and not only.startswith(f"{scheme} {K}x{N}"):
                 continue
             nb = N * K * BYTES[scheme]
             ws = make_weights(sm, ctx, torch, scheme, N, K, max(2, int(300e6 // nb) + 1))
-            for M in (8, 64, 512, 2048):
-                if args.gemv_only and args.gemv_only.count(" ") == 2 and args.gemv_only.split()[2] != f"M{M}":
+            for M in ms_list:
+                if only and only.count(" ") == 2 and only.split()[2] != f"M{M}":
                     continue
                 x = torch.randn(M, K, device="cuda")
                 y = torch.empty(M, N, device="cuda")
@@ -399,30 +418,64 @@ def run_gemm_sweep(args):
                                 "frac_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm, 3)}
                 else:
                     fl = 2.0 * M * K * N / (ms * 1e-3) / 1e12
-                    res[key] = {"us": round(ms * 1000, 1), "TFLOPs": round(fl, 1), "frac_tensor": round(fl / tflops, 3)}
+                    res[key] = {"us": round(ms * 1000, 1), "TFLOPs": round(fl, 1),
+                                "frac_tensor": round(fl / tflops, 3)}
                 del g, x, y
             for w in ws:
                 w.close()
-    print(json.dumps({"gemm_sweep": res, "peak_gbs": hbm, "peak_tflops": tflops}), flush=True)
+    return res
+
+
+def _sweep_ctx():
+    import torch
+
+    import smallmind_b200 as sm
+    ctx = sm.CudaContext(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    torch.cuda.set_stream(stream)
+    return sm, ctx, torch, stream
+
+
+def run_gemv_sweep(args):
+    sm, ctx, torch, stream = _sweep_ctx()
+    print(json.dumps({"gemv_sweep_m1": gemv_sweep(sm, ctx, torch, args.gemv_only), "peak_gbs": peaks()[0]}),
+          flush=True)
+
+
+def run_gemm_sweep(args):
+    sm, ctx, torch, stream = _sweep_ctx()
+    res = gemm_sweep(sm, ctx, torch, stream, args.gemv_only)
+    print(json.dumps({"gemm_sweep": res, "peak_gbs": peaks()[0], "peak_tflops": tensor_peak()[0]}), flush=True)
 
 
 def run_reference(args):
+    """The reference arm: the oracle's C++ restatement of the reference CPU decode path (the
+    reference itself is C# and no .NET runtime exists here), same model shape, context and
+    metric as our arm.  Rank 0 only; other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    steps = max(5, min(args.steps, 30))
-    tps, dt, build_s = cpu_decode_sample(TINYLLAMA, PROMPT, steps, threads)
+    steps = max(5, min(args.steps, 200))
+    tps, dt, build_s, host = cpu_decode_sample(TINYLLAMA, PROMPT, steps, threads, warmup=args.warmup)
+    st_steps = 3
+    tps1, _, _, _ = cpu_decode_sample(TINYLLAMA, PROMPT, st_steps, threads, warmup=1, linear_threads=1, host=host)
     sample = (f"{steps} greedy decode steps of the TinyLlama-shaped Q4_K_M model at context {PROMPT} "
-              f"(synthetic KV cache), C++ restatement of the reference algorithm, {threads} threads")
+              f"(synthetic KV cache) after {args.warmup} untimed steps; C++ restatement of the reference "
+              f"algorithm; quantized linears row-split over {threads} threads (the reference runs them "
+              f"single-threaded: see reference_threading), attention parallel over heads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(tps, 4), "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": 1, "ms_per_step": round(1000 * dt / steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "TinyLlama-1.1B-shaped Q4_K_M decode, bs1, ctx 2048", "global_batch": 1,
-                   "seq_len": PROMPT, "parallelism": "cpu"},
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(args.gpus),
         "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample},
+        "reference_threading": {"value": round(tps1, 4), "unit": "tok/s", "steps": st_steps,
+                                "note": "quantized linears single-threaded as in the reference "
+                                        "(MatMulF32Q8 / FusedQ4KMatMul / FusedQ6KMatMul), attention over "
+                                        f"{threads} threads"},
         "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -494,9 +547,7 @@ def run_ours(args):
     stream.synchronize()
     launches_w = ctx.launch_count()
 
-    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                                       else "_work", f"clocks_rank{rank}.csv"))
-    os.makedirs(os.path.dirname(clocks.out_path), exist_ok=True)
+    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -640,16 +691,24 @@ def run_ours(args):
     kv4.close()
     model_s.close()
 
+    sweeps = None
+    if world == 1 and not args.no_sweeps:
+        sweeps = {"gemv_m1": gemv_sweep(sm, ctx, torch),
+                  "gemm": gemm_sweep(sm, ctx, torch, stream),
+                  "peak_gbs": hbm, "peak_tflops": tensor_peak()[0]}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         steps = 20
-        tps, dt, _ = cpu_decode_sample(cfg, PROMPT, steps, os.cpu_count() or 1)
-        cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+        nt = os.cpu_count() or 1
+        tps, dt, _, _ = cpu_decode_sample(cfg, PROMPT, steps, nt)
+        cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": nt, "kind": "port",
                "sample": f"{steps} decode steps at context {PROMPT} (synthetic KV cache), same model shape, "
-                         f"C++ restatement of the reference algorithm"}
+                         f"C++ restatement of the reference algorithm, quantized linears row-split over {nt} "
+                         f"threads (the reference runs them single-threaded)"}
 
     if rank == 0:
-        clk = clocks.summary(local)
+        clk = clocks.summary()
         wbytes = weight_bytes_per_token(cfg)
         ctx_mid = args.prompt + args.warmup + args.steps / 2.0
         sbytes = step_bytes(cfg, ctx_mid)
@@ -659,14 +718,14 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, "
             "random token ids)",
-            "config": {"workload": "TinyLlama-1.1B-shaped Q4_K_M decode, bs1 per GPU, ctx 2048",
-                       "model": "TinyLlama-1.1B-shaped (H2048 L22 32q/4kv FFN5632 V32000)", "global_batch": world,
-                       "seq_len": PROMPT, "parallelism": f"replica x{world} (sequence sharding)",
-                       "l2": "no flush: 667 MB of weights per step > 126 MB L2"},
+            "config": bench_config(world),
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(ach / hbm, 4), "traffic": traffic,
+                         "traffic_source": ("read from profiles/decode_mega_traffic.json: dram__bytes_read.sum + "
+                                            "dram__bytes_write.sum of one decode_mega_kernel launch in an ncu "
+                                            "capture of this command, not measured in this run"),
                          "kernel": ("decode_mega_kernel (one launch per step)" if mega
                                     else "per-kernel decode step"),
                          "algorithmic_bytes_per_launch": int(sbytes), "peak_kind": peak_kind},
@@ -680,6 +739,7 @@ def run_ours(args):
             "attention_decode": attn,
             "smollm_q8_bs1_decode_tok_s": round(smol_tps, 1),
             "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
+            "op_sweep": sweeps,
             "gpu_launches": int(launches_timed),
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -696,6 +756,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-sweeps", action="store_true", help="skip the op-sweep GEMV/GEMM legs (config 2)")
     ap.add_argument("--no-serving", action="store_true", help="skip the 256-sequence serving run (config 5)")
     ap.add_argument("--attn-only", action="store_true", help="time the config-4 decode attention cases and exit")
     ap.add_argument("--sample-only", action="store_true", help="time device sampling (sm_sample) and exit")

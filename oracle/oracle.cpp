@@ -7,6 +7,7 @@
 #include <limits>
 #include <cmath>
 #include <cstring>
+#include <atomic>
 #include <thread>
 #include <vector>
 
@@ -754,8 +755,17 @@ void or_attention(const float* q, const float* k, const float* v, float* out, in
 }
 
 // ---------------------------------------------------------------------------
+// Threads of the quantized linears: 0 = the caller's n_threads (rows split across
+// threads); 1 = single-threaded, the reference's own threading (its MatMulF32Q8 /
+// FusedQ4KMatMul / FusedQ6KMatMul run on the calling thread).  Attention keeps
+// n_threads either way (Parallel.For over B*nH, MultiHeadAttention.cs:686-712).
+static std::atomic<int> g_linear_threads{0};
+void or_set_linear_threads(int n) { g_linear_threads.store(n < 0 ? 0 : n); }
+
 static void linear_fwd(const or_linear& L, const float* x, float* y, int M, int K, int N, int n_threads) {
   // x . W^T for W [N][K]; rows split across threads (each row is independent).
+  const int lt = g_linear_threads.load();
+  if (lt > 0) n_threads = lt;
   int chunks = std::max(1, std::min(n_threads, N / 64));
   parallel_for(chunks, chunks, [&](int c) {
     int n0 = (int)((int64_t)N * c / chunks), n1 = (int)((int64_t)N * (c + 1) / chunks);

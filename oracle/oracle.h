@@ -129,6 +129,8 @@ int or_model_forward(const or_model* m, const int* tokens, int T, int n_last, fl
 
 /* KV-cached decode twin used by the CPU baseline: same math, but keeps K/V
  * for past positions so each new token costs one row.  kv: [layers][2][max_ctx][n_kv*hd]. */
+/* 0: linears use the caller's n_threads; 1: single-threaded, as the reference runs them. */
+void or_set_linear_threads(int n);
 int or_model_step(const or_model* m, float* kv, int pos, const int* tokens, int T, float* last_logits, int n_threads);
 
 /* One token from one logits row through the reference sampling pipeline

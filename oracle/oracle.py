@@ -97,6 +97,7 @@ def _declare(L):
         "or_model_forward": (i, [C.POINTER(Model), vp, i, i, vp, i]),
         "or_model_step": (i, [C.POINTER(Model), vp, i, vp, i, vp, i]),
         "or_fill_normal": (None, [vp, i64, C.c_uint64, f, i]),
+        "or_set_linear_threads": (None, [i]),
         "or_sample": (i, [vp, i, C.c_double, i, C.c_double, C.c_double, f, f, f, i, vp, i, C.c_double, vp]),
         "or_deterministic_rng_doubles": (None, [C.c_int32, i, vp]),
     }
@@ -231,6 +232,12 @@ def matmul(t: QTensor, a: np.ndarray, m: int, k: int, n: int, mode: int, want64:
 
 
 # ---------------------------------------------------------------- model ops
+def set_linear_threads(n: int) -> None:
+    """0: quantized linears split rows over the caller's threads; 1: single-threaded,
+    the reference's own threading for MatMulF32Q8 / FusedQ4KMatMul / FusedQ6KMatMul."""
+    lib().or_set_linear_threads(int(n))
+
+
 def rmsnorm(x: np.ndarray, gamma: np.ndarray, eps: float = 1e-5) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     rows, feat = x.reshape(-1, x.shape[-1]).shape

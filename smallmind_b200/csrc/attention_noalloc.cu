@@ -57,10 +57,10 @@ int scratch_address(int device, float** out) {
 extern "C" SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, const float* k_cache,
                                                   const float* v_cache, float* out, const int* lens_dev, int B,
                                                   int max_ctx, int n_heads, int n_kv, int head_dim) {
-  if (!ctx || !q || !k_cache || !v_cache || !out || !lens_dev)
-    return sm::fail(SM_ERR_INVALID_ARG, "attention_decode_noalloc: null argument");
   if (B <= 0 || max_ctx <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv)
     return sm::fail(SM_ERR_SHAPE, "attention_decode_noalloc: bad shape");
+  if (!ctx || !q || !k_cache || !v_cache || !out || !lens_dev)
+    return sm::fail(SM_ERR_INVALID_ARG, "attention_decode_noalloc: null argument");
   const size_t need = sm::attention_decode_scratch_floats(B, n_heads, max_ctx);
   if (need > kNoAllocScratchFloats)
     return sm::fail(SM_ERR_SHAPE, "attention_decode_noalloc: B * n_heads * (max_ctx + 66 * ceil(max_ctx / 64)) "
@@ -70,7 +70,7 @@ extern "C" SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, c
   int64_t* launches = nullptr;
   SM_TRY(sm::ctx_view(ctx, &device, &stream, &launches));
   int prev = -1;
-  cudaGetDevice(&prev);
+  SM_CUDA_TRY(cudaGetDevice(&prev));
   if (prev != device) SM_CUDA_TRY(cudaSetDevice(device));
   float* scratch = nullptr;
   int rc = scratch_address(device, &scratch);

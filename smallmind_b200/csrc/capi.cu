@@ -541,8 +541,10 @@ SM_API int sm_attention(sm_ctx* ctx, const float* q, const float* k, const float
 
 SM_API int sm_attention_decode(sm_ctx* ctx, const float* q, const float* kc, const float* vc, float* out,
                                const int* lens_dev, int B, int max_ctx, int nH, int nKv, int hd) {
+  // shape first: a zero head count must come back as an error, never reach the modulo
+  if (B <= 0 || max_ctx <= 0 || nH <= 0 || nKv <= 0 || hd <= 0 || nH % nKv)
+    return fail(SM_ERR_SHAPE, "attention_decode: bad shape");
   if (!ctx || !q || !kc || !vc || !out || !lens_dev) return fail(SM_ERR_INVALID_ARG, "attention_decode: null argument");
-  if (B <= 0 || max_ctx <= 0 || nH % nKv) return fail(SM_ERR_SHAPE, "attention_decode: bad shape");
   DeviceGuard g(ctx->device);
   cudaStream_t st = ctx->stream;
   int nl = 0;
@@ -692,13 +694,9 @@ __global__ void decode_commit_kernel(const int* __restrict__ seq, int* __restric
 // One-row step (bs1 decode): fused launches built on the M = 1 GEMV.  Per layer:
 // [RMSNorm + Q|K|V] -> RoPE + KV append -> attention -> [O-proj + residual]
 // -> [RMSNorm + gate/up + SiLU-gate] -> [down-proj + residual].
-// warp-per-row-group GEMV; SMALLMIND_GEMV_STREAM=1 selects the TMA-ring streaming kernel
+// warp-per-row-group GEMV
 int launch_m1(const GemvArgs& a, sm_model* m, cudaStream_t st, int& nl) {
-  const char* e = std::getenv("SMALLMIND_GEMV_STREAM");
-  if (e && e[0] == '1') {
-    const int rc = launch_gemv_stream(a, m->ctx->dev_status, st, &nl);
-    if (rc != SM_ERR_UNSUPPORTED) return rc;
-  }
+  (void)m;
   return launch_gemv1(a, st, &nl);
 }
 

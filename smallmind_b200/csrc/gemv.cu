@@ -365,11 +365,6 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
       const int rc = launch_gemv_mma_q80(W, x, y, accumulate, nullptr, st, n_launch);
       if (rc != SM_ERR_UNSUPPORTED) return rc;
     }
-    const char* e = std::getenv("SMALLMIND_GEMV_STREAM");
-    if (e && e[0] == '1') {
-      const int rc = launch_gemv_stream(a, nullptr, st, n_launch);
-      if (rc != SM_ERR_UNSUPPORTED) return rc;
-    }
     return launch_gemv1(a, st, n_launch);
   }
   {

@@ -36,16 +36,6 @@ struct GemvArgs {
   int head_dim = 0, n_kv = 0, max_ctx = 0;
 };
 
-// Streaming variant (gemv_stream.cu): one persistent CTA per SM; returns
-// SM_ERR_UNSUPPORTED (without launching) when a shape does not fit it.
-struct StreamArgs {
-  GemvArgs g;
-  int* status = nullptr;  // SM_ERR_TIMEOUT from a bounded wait
-  int cta_begin[GEMV_MAX_SEG] = {}, cta_count[GEMV_MAX_SEG] = {}, stage_rows[GEMV_MAX_SEG] = {};
-  int nslots = 2;
-  int ring_offset = 0;  // bytes of shared memory before the stage ring
-};
-int launch_gemv_stream(const GemvArgs& g, int* status, cudaStream_t st, int* n_launch);
 
 bool gemv1_supports(const DevWeight& w, int K);
 // true when one gemv1 launch can mix segments of formats fa and fb (fa == fb, or Q4_K with Q6_K)

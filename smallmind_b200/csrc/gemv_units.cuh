@@ -1,5 +1,5 @@
 // Per-format 32-weight "units" and the row epilogues shared by the M = 1 GEMVs
-// (gemv1.cu, gemv_stream.cu).  Exact byte-permute dequant: see gemv1.cu.
+// (gemv1.cu, decode_mega.cu).  Exact byte-permute dequant: see gemv1.cu.
 #pragma once
 #include "common.cuh"
 #include "gemv1.cuh"

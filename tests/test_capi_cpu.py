@@ -41,6 +41,11 @@ def test_host_side_argument_checks():
     assert L.sm_prefill(None, None, 0, None, 0, None, None) == -1
     assert L.sm_decode(None, None, None, None, 0, None, None, 0) == -1
     assert "null" in sm.last_error()
+    # zero or non-dividing head counts are shape errors, checked before anything is dereferenced
+    for nh, nkv in ((4, 0), (0, 2), (5, 2)):
+        assert L.sm_attention_decode(None, None, None, None, None, None, 1, 16, nh, nkv, 64) == -2
+        assert L.sm_attention_decode_noalloc(None, None, None, None, None, None, 1, 16, nh, nkv, 64) == -2
+    assert "bad shape" in sm.last_error()
     assert L.sm_weight_destroy(None) == 0 and L.sm_ctx_destroy(None) == 0
     n = C.c_int(-1)
     rc = L.sm_device_count(C.byref(n))
