@@ -631,7 +631,9 @@ struct sm_kv {
   int pinned_cap = 0;
   // one-launch bs1 decode step (decode_mega.cu)
   MegaLayer* mega_layers = nullptr;  // device table of per-layer segments
-  unsigned* mega_sync = nullptr;     // grid barrier / combine counters
+  unsigned* mega_sync = nullptr;     // argmax arrival counter
+  unsigned long long* mega_ll = nullptr;  // tagged exchange words of the one-launch decode (+ its epoch)
+  size_t mega_ll_words = 0;
   unsigned long long* mega_trace = nullptr;  // SMALLMIND_MEGA_TRACE: per-CTA phase timestamps
   int mega_generation = -1;
   bool mega_mma_only = false;  // every segment of the layer table has the tensor-core path
@@ -1017,6 +1019,20 @@ int mega_args(sm_model* m, sm_kv* kv, MegaArgs& a) {
   sc += grid;
   a.amax_idx = (int*)sc;
   a.sync = kv->mega_sync;
+  {
+    const size_t words = mega_ll_words(a.H, a.qd, a.kd, a.F, a.nH, a.nKv, a.hd, grid);
+    if (kv->mega_ll_words < words) {
+      if (kv->mega_ll) cudaFree(kv->mega_ll);
+      kv->mega_ll = nullptr;
+      kv->mega_ll_words = 0;
+      SM_CUDA_TRY(cudaMalloc(&kv->mega_ll, words * sizeof(unsigned long long)));
+      // all-ones: no word carries a tag a launch waits for until it is written
+      SM_CUDA_TRY(cudaMemset(kv->mega_ll, 0xff, words * sizeof(unsigned long long)));
+      SM_CUDA_TRY(cudaMemset(kv->mega_ll, 0, sizeof(unsigned long long)));  // epoch 0
+      kv->mega_ll_words = words;
+    }
+    mega_ll_assign(a, kv->mega_ll, grid);
+  }
   a.status = m->ctx->dev_status;
   if (std::getenv("SMALLMIND_MEGA_TRACE")) {
     if (!kv->mega_trace)
@@ -1195,6 +1211,7 @@ SM_API int sm_kv_destroy(sm_kv* kv) {
     if (it.second.exec) cudaGraphExecDestroy(it.second.exec);
   if (kv->mega_layers) cudaFree(kv->mega_layers);
   if (kv->mega_sync) cudaFree(kv->mega_sync);
+  if (kv->mega_ll) cudaFree(kv->mega_ll);
   if (kv->mega_trace) cudaFree(kv->mega_trace);
   cudaFree(kv->k);
   cudaFree(kv->v);

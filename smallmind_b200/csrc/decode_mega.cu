@@ -16,10 +16,19 @@
 //    partials from the staged bytes (exact byte-permute dequant of
 //    gemv_units.cuh), reduce rows in a fixed order and run the epilogue (RoPE
 //    + KV append, residual add, SiLU gate).
-//  * Phases are separated by a global barrier (atomic counter, bounded spin).
-//    Attention is two phases: scores + slice max per (kv head, chunk), then
-//    Pade exp against the exact row max, partial e.V, and a last-arriving-CTA
-//    combine per kv head (threadfence + counter).
+//  * There is no grid-wide barrier.  Every vector one CTA hands to others (the
+//    residual stream after each residual add, q, this token's K/V rows, the
+//    attention chunk maxima / partials / output, the SiLU-gate output) is
+//    written as 64-bit words {value, tag}, tag = (launch epoch, layer), and a
+//    reader polls exactly the words it needs until their tags match.  A wait
+//    therefore costs one L2 round trip after the last producer's store instead
+//    of a release fence, an arrival, a counter poll and the reload of the data.
+//    Single buffers suffice: a word is rewritten one layer later only by a CTA
+//    whose own inputs needed (transitively) every reader's output of the layer
+//    before; a CTA with no output rows in a phase does not read its input.
+//  * Attention is three steps per (kv head, chunk) item: scores + chunk max,
+//    Pade exp against the exact row max (all chunk maxima polled) and partial
+//    e.V, then the combine of this CTA's slice of the outputs.
 //  * Every wait is bounded (~2 s of clock64); on timeout the kernel records
 //    SM_ERR_TIMEOUT in the context status word and returns.
 #include <algorithm>
@@ -43,6 +52,26 @@ constexpr int MGMAX = 8;             // q heads per kv head
 constexpr long long kSpin = 4000000000LL;
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
+
+// ---- tagged exchange words {float value (low 32 bits), uint32 tag (high 32 bits)}.
+// An aligned 8-byte access is single-copy atomic, so a reader that sees the tag it
+// expects also sees the value stored with it; gpu-scope relaxed accesses are served
+// by L2, where every SM's stores meet.
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 ll_ld(const u64* p) {
+  u64 v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ll_st(u64* p, float v, unsigned tag) {
+  const u64 w = ((u64)tag << 32) | (u64)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ bool ll_ok(u64 w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(u64 w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ unsigned ll_tag(unsigned epoch, int layer) {
+  return ((epoch + 1u) << 8) | ((unsigned)layer & 255u);
+}
 
 __host__ __device__ __forceinline__ int64_t row_bytes_fmt(int fmt, int K) {
   switch (fmt) {
@@ -131,6 +160,13 @@ struct SegPlan {
   MGeo mg;
   int nst, red_n, red_off;  // MMA: stages, block partials, their offset in part
   int slot0, par0;          // ring slot and parity of the segment's first stage
+  // tagged exchange: the input vector (null: `src` is a plain array), the residual
+  // rows (ADD; null: res_plain), the output words (null: plain stores to s->y)
+  const u64* src_ll;
+  const u64* res_ll;
+  const float* res_plain;
+  u64* dst;
+  unsigned src_tag, res_tag, dst_tag;
 };
 
 struct Shared {
@@ -246,7 +282,7 @@ struct Consumer {
   GemvArgs ep;  // epilogue context (RoPE / cache)
   int tid;
   int k = 0;  // stages consumed
-  unsigned barrier_gen = 0;
+  unsigned epoch = 0;  // this launch's exchange epoch (read once at the start)
   int ev = 0;
   int seq_v = 0;  // the sequence id (read once)
   int lx = 0;  // load_x calls (trace: the sub-steps of calls 4..11 go to events 900..)
@@ -296,8 +332,37 @@ struct Consumer {
     }
     const MegaSeg& sg = head ? a.head : (kind == 0 ? L.qkv[si] : (kind == 1 ? L.o : (kind == 2 ? L.gu : L.down)));
     P.s = &sg;
-    // RMSNorm (Q|K|V, gate|up, head) on the residual stream; O reads the attention output, down the GLU
-    P.src = (kind == 1 && !head) ? a.att : ((kind == 3 && !head) ? a.act : (ph == 0 ? emb : a.x));
+    // RMSNorm (Q|K|V, gate|up, head) on the residual stream; O reads the attention output, down the GLU.
+    // Exchange words: Q|K|V (and the head) read x1 of the previous layer, O reads att and adds x1,
+    // gate|up reads x0, down reads act and adds x0.
+    P.src = ph == 0 ? emb : nullptr;
+    const unsigned tl = ll_tag(epoch, l), tp = ll_tag(epoch, l - 1);
+    P.src_ll = nullptr;
+    P.res_ll = nullptr;
+    P.res_plain = nullptr;
+    P.dst = nullptr;
+    P.src_tag = P.res_tag = P.dst_tag = tl;
+    if (head) {
+      P.src_ll = a.ll_x1;
+      P.src_tag = tp;
+    } else if (kind == 0) {
+      if (ph > 0) P.src_ll = a.ll_x1;
+      P.src_tag = tp;
+      P.dst = si == 0 ? a.ll_q : (si == 1 ? a.ll_kv : a.ll_kv + a.kd);
+    } else if (kind == 1) {
+      P.src_ll = a.ll_att;
+      if (l == 0) P.res_plain = emb;
+      else P.res_ll = a.ll_x1;
+      P.res_tag = tp;
+      P.dst = a.ll_x0;
+    } else if (kind == 2) {
+      P.src_ll = a.ll_x0;
+      P.dst = a.ll_act;
+    } else {
+      P.src_ll = a.ll_act;
+      P.res_ll = a.ll_x0;
+      P.dst = a.ll_x1;
+    }
     P.gamma = head ? a.out_norm : (kind == 0 ? L.attn_norm : (kind == 2 ? L.ffn_norm : nullptr));
     P.amax_v = head ? &a.amax_val[blockIdx.x] : nullptr;
     P.amax_i = head ? &a.amax_idx[blockIdx.x] : nullptr;
@@ -320,23 +385,82 @@ struct Consumer {
     }
   }
 
-  // `next`: a layer table entry to bring on chip into lay[next_slot]; `prep`: the
-  // GEMV phase to plan (thread 64), both while thread 0 waits
-  __device__ bool grid_barrier(const MegaLayer* next = nullptr, int next_slot = 0, int prep = -1,
-                               const float* emb = nullptr, const MegaLayer* kvl = nullptr, int chunks = 0,
-                               int len = 0) {
-    // all consumer stores of this CTA are done before thread 0 arrives
+  // ---- polling the exchange words (bounded: ~2 s of clock64, then SM_ERR_TIMEOUT)
+  // One tick of a poll loop: false once the CTA has given up (its own timeout or
+  // another thread's); the loop then stops and the caller's values are garbage,
+  // which is harmless: the CTA leaves at its next phase transition.
+  __device__ bool poll_tick(long long& t0) {
+    if (*(volatile int*)&sh.abort) return false;
+    const long long now = clock64();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kSpin) {
+      atomicExch(a.status, SM_ERR_TIMEOUT);
+      *(volatile int*)&sh.abort = 1;
+      return false;
+    }
+    __nanosleep(32);
+    return true;
+  }
+
+  // Consumer threads gather n exchange words: value i (word at addr(i)) goes to
+  // put(i, v) once its tag is `tag`.  Up to B words per thread are in flight at a
+  // time; only the words not yet tagged are loaded again.
+  template <int B, class Addr, class Put>
+  __device__ void ll_gather(int n, unsigned tag, Addr addr, Put put) {
+    for (int base = 0; base < n; base += B * CT) {
+      u64 w[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int i = base + b * CT + tid;
+        w[b] = i < n ? ll_ld(addr(i)) : 0ull;
+      }
+      long long t0 = 0;
+      while (true) {
+        bool all = true;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int i = base + b * CT + tid;
+          if (i < n && !ll_ok(w[b], tag)) {
+            all = false;
+            w[b] = ll_ld(addr(i));
+          }
+        }
+        if (all || !poll_tick(t0)) break;
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int i = base + b * CT + tid;
+        if (i < n) put(i, ll_val(w[b]));
+      }
+    }
+  }
+
+  // one word, polled by the calling thread alone
+  __device__ float ll_wait1(const u64* p, unsigned tag) {
+    u64 w = ll_ld(p);
+    long long t0 = 0;
+    while (!ll_ok(w, tag) && poll_tick(t0)) w = ll_ld(p);
+    return ll_val(w);
+  }
+
+  // Phase transition inside the CTA (no grid-wide barrier: data readiness travels
+  // in the exchange words).  `next`: a layer table entry to bring on chip into
+  // lay[next_slot]; `prep`: the GEMV phase to plan (thread 64); `kvl`: the layer
+  // whose attention rows of this CTA are prefetched into L2.  False (uniformly
+  // across the consumer threads) once the CTA has given up.
+  __device__ bool transition(const MegaLayer* next = nullptr, int next_slot = 0, int prep = -1,
+                             const float* emb = nullptr, const MegaLayer* kvl = nullptr, int chunks = 0,
+                             int len = 0) {
     cons_sync();
     stamp();
-    // this CTA's attention chunks of the layer: K / V rows into L2 while thread 0
-    // waits (after the CTA barrier, so its arrival does not wait for them)
-    if (kvl && tid > 0) {
+    if (kvl) {
       for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
         const int per = (len + chunks - 1) / chunks, cc = it % chunks, gg = it / chunks;
         const int j0 = min(len, cc * per), j1 = min(len, j0 + per);
         const int64_t off = ((int64_t)seq_v * a.nKv + gg) * a.max_ctx * 64 + (int64_t)j0 * 64;
         const int lines = (j1 - j0) * 2;  // 256-byte rows
-        for (int t = tid - 1; t < 2 * lines; t += CT - 1) {
+        for (int t = tid; t < 2 * lines; t += CT) {
           const float* base = (t < lines ? kvl->kc : kvl->vc) + off;
           asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (t % lines) * 32));
         }
@@ -345,38 +469,18 @@ struct Consumer {
     if (next && tid >= 32 && tid < 32 + (int)(sizeof(MegaLayer) / 4))
       ((int*)&sh.lay[next_slot])[tid - 32] = __ldg((const int*)next + (tid - 32));
     if (prep >= 0 && tid == 64) prepare(prep, emb);
-    ++barrier_gen;
-    if (tid == 0) {
-      // release-ordered arrival without waiting for a return value: this CTA's
-      // stores (ordered before it by the CTA barrier) are visible before the
-      // count moves, and the poll below starts one L2 round trip earlier
-      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.sync), "r"(1u) : "memory");
-      const unsigned target = barrier_gen * gridDim.x;
-      const long long t0 = clock64();
-      int ok = 1;
-      while (true) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
-        if (v >= target) break;
-        if (clock64() - t0 > kSpin) {
-          atomicExch(a.status, SM_ERR_TIMEOUT);
-          ok = 0;
-          break;
-        }
-      }
-      sh.flag[0] = ok;
-    }
+    if (tid == 0) sh.flag[0] = !*(volatile int*)&sh.abort;
     cons_sync();
     stamp();
-    if (!sh.flag[0]) {
-      if (tid == 0) sh.abort = 1;
-      return false;
-    }
-    return true;
+    return sh.flag[0] != 0;
   }
 
   // x slice for a phase with K inputs (optionally RMS-normalised with gamma)
-  __device__ void load_x(const float* src, const float* gamma, int K, bool want_pair = true, int mma = 0) {
+  // need: this CTA has output rows in the phase.  A CTA without any does not wait
+  // for the vector (nothing downstream waits for it, so it could fall a layer
+  // behind and see the words of the next one); its planes hold zeros.
+  __device__ void load_x(const float* src, const u64* src_ll, unsigned src_tag, const float* gamma, int K,
+                         bool want_pair, int mma, bool need) {
     x_src = src;
     x_gamma = gamma;
     x_K = K;
@@ -400,7 +504,7 @@ struct Consumer {
     // different bank groups.
     if (AM || mma) {
       // the tensor-core path needs no staged copy: each lane reads its own elements
-      build_mma_planes(src, K, gamma, mma, lxe);
+      build_mma_planes(src, src_ll, src_tag, K, gamma, mma, lxe, need);
       return;
     }
     float4* xs = (float4*)part;        // [K/4]
@@ -408,8 +512,18 @@ struct Consumer {
     uint32_t* pls = (uint32_t*)(part + 2 * K);  // [U][28]: planes a, b, c (8 words each), inv, x16a, x16b
     for (int t = tid; t < K / 4; t += CT) {
       const int w = t >> 3, p = (w << 3) + (((t & 7) + w) & 7);
-      xs[p] = __ldcg((const float4*)src + t);
+      if (!src_ll) xs[p] = __ldcg((const float4*)src + t);
       if (gamma) gs[p] = __ldg((const float4*)gamma + t);
+    }
+    if (src_ll && !need) {
+      for (int t = tid; t < K / 4; t += CT) xs[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if (src_ll) {
+      // element i: float4 t = i / 4 of the staging order above, lane i % 4
+      float* xf = (float*)xs;
+      ll_gather<12>(K, src_tag, [&](int i) { return src_ll + i; }, [&](int i, float v) {
+        const int t = i >> 2, w = t >> 3;
+        xf[4 * ((w << 3) + (((t & 7) + w) & 7)) + (i & 3)] = v;
+      });
     }
     if (lxe >= 0) stamp_at(lxe + 1);
     cons_sync();
@@ -505,19 +619,30 @@ struct Consumer {
   // raw-byte positions (L: 21-bit low elements, H: 17-bit high elements), see
   // gemv_mma.cu; Q6_K: 22-bit values, six columns (three per 16-element half,
   // zero at the other half's positions).
-  __device__ void build_mma_planes(const float* src, int K, const float* gamma, int fmt, int lxe) {
+  __device__ void build_mma_planes(const float* src, const u64* src_ll, unsigned src_tag, int K,
+                                   const float* gamma, int fmt, int lxe, bool need) {
     const int U = K >> 5, NB = K >> 8, lane = tid & 31;
     const int pbase = K;  // part [0, K) stays free for the block partials
     uint2* mp = (uint2*)(part + pbase);        // [U][6][4] at most
     float* sx = part + pbase + 48 * U;         // [U][2] at most
     float* bx = sx + 2 * U;                    // [NB]
     mend = pbase + 50 * U + NB;
+    if (src_ll) {
+      // the vector arrives in exchange words: gathered into part [0, K) first (the
+      // block partials are written there only after the planes are built)
+      if (need)
+        ll_gather<12>(K, src_tag, [&](int i) { return src_ll + i; }, [&](int i, float v) { part[i] = v; });
+      else
+        for (int i = tid; i < K; i += CT) part[i] = 0.f;
+      cons_sync();
+      src = part;
+    }
     float sq = 0.f;
     for (int t0 = (tid >> 5) * 32; t0 < 4 * U; t0 += CT) {  // 4U is a multiple of 32: whole warps
       const int t = t0 + lane, uu = t >> 2, pp = t & 3;
-      // the vector was written by other CTAs: bypass L1
+      // the vector was written by other CTAs (or gathered above): bypass L1
       const float4* xg = (const float4*)(src + 32 * uu + 8 * pp);
-      const float4 v0 = __ldcg(xg), v1 = __ldcg(xg + 1);
+      const float4 v0 = src_ll ? xg[0] : __ldcg(xg), v1 = src_ll ? xg[1] : __ldcg(xg + 1);
       float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       if (gamma) {
         const float4* gg = (const float4*)(gamma + 32 * uu + 8 * pp);
@@ -854,6 +979,47 @@ struct Consumer {
     return g;
   }
 
+  // Epilogue of one group of rows (final values v[0..R-1]) into the exchange words
+  // PL.dst: SiLU gate (GLU), RoPE (queries; keys, which also go to the cache), the
+  // V row (also to the cache); STORE (the LM head) writes plain logits.
+  template <int R>
+  __device__ void mega_store(const GemvSeg& s, const SegPlan& PL, int lg, float* v) {
+    if (s.mode == GEMV_GLU) {
+#pragma unroll
+      for (int r = 0; r < R / 2; ++r) {
+        const int row = group_row<R>(s, lg, r);
+        if (row >= s.rows) continue;
+        const float gt = v[r], up = v[r + R / 2];
+        const float c = fmaxf(-20.f, fminf(gt, 20.f));
+        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));  // ActivationOps.cs:304-309
+        ll_st(PL.dst + row, __fmul_rn(__fmul_rn(gt, sig), up), PL.dst_tag);
+      }
+      return;
+    }
+    const int row0 = group_row<R>(s, lg, 0);
+    if (s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE) {
+      const int pos = *ep.pos;
+#pragma unroll
+      for (int r = 0; r < R; r += 2) rope_pair(v[r], v[r + 1], ep, pos, (row0 + r) % ep.head_dim);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = row0 + r;
+      if (row >= s.rows) continue;
+      if (s.mode == GEMV_ROPE_K_CACHE || s.mode == GEMV_V_CACHE) {
+        // head-major cache [seq][kv_head][pos][hd] (MultiHeadAttention.cs:262-274) for later steps;
+        // this step's attention reads the row from the exchange words
+        const int64_t seq = *ep.seq, pos = *ep.pos;
+        const int h = row / ep.head_dim, d = row - h * ep.head_dim;
+        s.y[((seq * ep.n_kv + h) * ep.max_ctx + pos) * ep.head_dim + d] = v[r];
+      }
+      if (PL.dst)
+        ll_st(PL.dst + row, v[r], PL.dst_tag);
+      else
+        s.y[row] = v[r];
+    }
+  }
+
   // GEMV rows of this CTA for one segment; `amax` (head only) tracks the local argmax.
   __device__ bool seg(const SegPlan& PL) {
     const MegaSeg& s = *PL.s;
@@ -868,7 +1034,9 @@ struct Consumer {
     float* mred = nullptr;
     // ADD: this thread's residual row, read before the GEMV rather than after it
     const bool addm = s.mode == GEMV_ADD;
-    const float resid = (addm && tid < nout) ? __ldcg(&s.y[r0 + tid]) : 0.f;
+    float resid = 0.f;
+    if (addm && tid < nout)
+      resid = PL.res_ll ? ll_wait1(PL.res_ll + r0 + tid, PL.res_tag) : __ldg(&PL.res_plain[r0 + tid]);
     const MGeo mg = PL.mg;
     // the caller staged the vector for this segment's path (one staging call site
     // keeps the kernel small): a mismatch is a scheduling error
@@ -880,15 +1048,17 @@ struct Consumer {
     if (AM || use_mma) {
       stamp();
       stamp();
-      if (!seg_mma_body(s, PL, mred)) return false;
+      // a failed wait leaves the loop early; the warp still meets the CTA barriers
+      // below and the epilogue is skipped (the CTA leaves at its next transition)
+      if (!seg_mma_body(s, PL, mred)) *(volatile int*)&sh.abort = 1;
     } else {
     stamp();
     for (int row = r0; row < r1; row += rb) {
       const int n = min(rb, r1 - row);
       const int slot = k % a.nslots;
       if (!mbar_wait_bounded(&sh.full[slot], (k / a.nslots) & 1, a.status)) {
-        sh.abort = 1;
-        return false;
+        *(volatile int*)&sh.abort = 1;
+        break;
       }
       if (row == r0) stamp();
       const uint8_t* st = ring + slot * slot_bytes;
@@ -928,7 +1098,10 @@ struct Consumer {
     stamp();
     cons_sync();
     const bool pairs = s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE;
-    const int nitems = pairs ? (nout + 1) / 2 : nout;
+    if (tid == 0) sh.flag[1] = *(volatile int*)&sh.abort;
+    cons_sync();
+    // after a failed wait nothing is stored: readers of these rows time out too
+    const int nitems = sh.flag[1] ? 0 : (pairs ? (nout + 1) / 2 : nout);
     const int lane = tid & 31, warp = tid >> 5;
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
@@ -956,14 +1129,18 @@ struct Consumer {
         }
         v[q] = t;
       }
-      if (addm && it == tid)
-        s.y[r0 + it] = resid + v[0];
-      else if (glu)
-        group_store<2>(ep, g, r0 + it, v);
-      else if (pairs)
-        group_store<2>(ep, g, (r0 >> 1) + it, v);
-      else
-        group_store<1>(ep, g, r0 + it, v);
+      if (addm) {
+        const float rs = it == tid ? resid
+                                   : (PL.res_ll ? ll_wait1(PL.res_ll + r0 + it, PL.res_tag)
+                                                : __ldg(&PL.res_plain[r0 + it]));
+        ll_st(PL.dst + r0 + it, rs + v[0], PL.dst_tag);
+      } else if (glu) {
+        mega_store<2>(g, PL, r0 + it, v);
+      } else if (pairs) {
+        mega_store<2>(g, PL, (r0 >> 1) + it, v);
+      } else {
+        mega_store<1>(g, PL, r0 + it, v);
+      }
       if (amax_v && (v[0] > bv || (v[0] == bv && r0 + it < bi))) {
         bv = v[0];
         bi = r0 + it;
@@ -1017,7 +1194,7 @@ struct Consumer {
   }
 
   // ---- attention, phase A: scores and slice max of item (kv head g, chunk c)
-  __device__ void attn_scores(const MegaLayer& L, int g, int c, int chunks, int len) {
+  __device__ void attn_scores(const MegaLayer& L, int lay_idx, int g, int c, int chunks, int len) {
     const int G = a.nH / a.nKv, HD = 64;
     const int per = (len + chunks - 1) / chunks;
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
@@ -1027,14 +1204,27 @@ struct Consumer {
     const float* kb = L.kc + (seq * a.nKv + g) * (int64_t)a.max_ctx * HD;
     const int sub = tid & 7, slot = tid >> 3;  // 60 key slots
     constexpr int SLOTS = CT / 8;
+    const unsigned tag = ll_tag(epoch, lay_idx);
+    // key row j: the cache for earlier tokens; this token's row (j = len - 1) from
+    // the exchange words its Q|K|V CTA wrote this step
+    auto key8 = [&](int j, float4& k0, float4& k1) {
+      if (j == len - 1) {
+        const u64* kp = a.ll_kv + g * HD + sub * 8;
+        float kv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kv[i] = ll_wait1(kp + i, tag);
+        k0 = make_float4(kv[0], kv[1], kv[2], kv[3]);
+        k1 = make_float4(kv[4], kv[5], kv[6], kv[7]);
+      } else {
+        const float4* kp = (const float4*)(kb + (int64_t)j * HD + sub * 8);
+        k0 = __ldcg(kp);
+        k1 = __ldcg(kp + 1);
+      }
+    };
     // the first pass's key rows load together with the queries (one round trip)
     float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), k1 = k0;
-    if (slot < n) {
-      const float4* kp = (const float4*)(kb + (int64_t)(j0 + slot) * HD + sub * 8);
-      k0 = __ldcg(kp);
-      k1 = __ldcg(kp + 1);
-    }
-    for (int t = tid; t < G * HD / 4; t += CT) ((float4*)qs)[t] = __ldcg((const float4*)&a.q[g * G * HD] + t);
+    if (slot < n) key8(j0 + slot, k0, k1);
+    ll_gather<2>(G * HD, tag, [&](int i) { return a.ll_q + g * G * HD + i; }, [&](int i, float v) { qs[i] = v; });
     cons_sync();
     float lmax[MGMAX];
 #pragma unroll
@@ -1045,11 +1235,7 @@ struct Consumer {
       const bool valid = jj < n;
       if (p > 0) {
         k0 = k1 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) {
-          const float4* kp = (const float4*)(kb + (int64_t)(j0 + jj) * HD + sub * 8);
-          k0 = __ldcg(kp);
-          k1 = __ldcg(kp + 1);
-        }
+        if (valid) key8(j0 + jj, k0, k1);
       }
       const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
@@ -1076,13 +1262,15 @@ struct Consumer {
     if (tid < G) {
       float m = -FLT_MAX;
       for (int w = 0; w < CWARPS; ++w) m = fmaxf(m, sh.red[w * MGMAX + tid]);
-      a.cmax[(g * chunks + c) * G + tid] = m;
+      ll_st(a.ll_cmax + (g * chunks + c) * G + tid, m, tag);
     }
     // the chunk's V rows (contiguous in the head-major cache) into shared memory
-    // with asynchronous copies that land while this CTA waits at the barrier
+    // with asynchronous copies that land while this CTA waits for the other chunks'
+    // maxima; this token's row comes from the exchange words in phase B
     const float* vb = L.vc + ((seq * a.nKv + g) * (int64_t)a.max_ctx + j0) * HD;
     float* vs = att_vs(per, chunks);
-    for (int t = tid; t < n * (HD / 4); t += CT)
+    const int ncp = j1 == len ? n - 1 : n;
+    for (int t = tid; t < ncp * (HD / 4); t += CT)
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(vs + 4 * t)), "l"(vb + 4 * t)
                    : "memory");
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -1090,17 +1278,19 @@ struct Consumer {
   }
 
   // ---- attention, phase B: e = FastExp(s*scale - max), partial sums, last CTA of the head combines
-  __device__ void attn_pv(const MegaLayer& L, int g, int c, int chunks, int len) {
+  __device__ void attn_pv(const MegaLayer& L, int lay_idx, int g, int c, int chunks, int len) {
     const int G = a.nH / a.nKv, HD = 64;
     const int per = (len + chunks - 1) / chunks;
     const int j0 = min(len, c * per), j1 = min(len, j0 + per), n = j1 - j0;
     const float scale = 1.0f / sqrtf((float)HD);
+    const unsigned tag = ll_tag(epoch, lay_idx);
     float* es = att_es();         // [G][per] scores from phase A
     float* pp = att_pp(per);      // [PH][G][64]
     {
       // exact row max of every head of the group: all chunk maxima, gathered in parallel
       float* cm = att_cm(per);  // [chunks][G]
-      for (int t = tid; t < chunks * G; t += CT) cm[t] = __ldcg(&a.cmax[g * chunks * G + t]);
+      ll_gather<2>(chunks * G, tag, [&](int i) { return a.ll_cmax + g * chunks * G + i; },
+                   [&](int i, float v) { cm[i] = v; });
       cons_sync();
       if (tid < G) {
         float m = -FLT_MAX;
@@ -1113,7 +1303,9 @@ struct Consumer {
       const int h = t / n, jj = t - h * n;
       es[h * per + jj] = pade_exp(__fsub_rn(__fmul_rn(es[h * per + jj], scale), sh.vec[h]));
     }
-    // the V rows copied in phase A
+    // the V rows copied in phase A, and this token's row from the exchange words
+    if (j1 == len && tid < HD)
+      att_vs(per, chunks)[(n - 1) * HD + tid] = ll_wait1(a.ll_kv + a.kd + g * HD + tid, tag);
     asm volatile("cp.async.wait_all;" ::: "memory");
     cons_sync();
     (void)L;
@@ -1141,7 +1333,7 @@ struct Consumer {
       const int h = t / 64, dd = t - h * 64;
       float s = 0.f;
       for (int p = 0; p < PH; ++p) s += pp[(p * MGMAX + h) * 64 + dd];
-      a.pacc[(int64_t)(base + h) * 64 + dd] = s;
+      ll_st(a.ll_pacc + (int64_t)(base + h) * 64 + dd, s, tag);
     }
     {
       const int w = tid >> 5, ln = tid & 31;
@@ -1149,54 +1341,36 @@ struct Consumer {
         float s = 0.f;
         for (int jj = ln; jj < n; jj += 32) s += es[w * per + jj];
         s = warp_sum(s);
-        if (ln == 0) a.psum[base + w] = s;
+        if (ln == 0) ll_st(a.ll_psum + base + w, s, tag);
       }
     }
     cons_sync();
   }
 
   // ---- attention, phase C: out[o] = sum_c pacc / sum_c psum for this CTA's slice of the outputs
-  __device__ void attn_combine(int chunks) {
+  __device__ void attn_combine(int lay_idx, int chunks) {
     const int G = a.nH / a.nKv, NO = a.nH * 64;
     const int o0 = (int)((int64_t)NO * blockIdx.x / gridDim.x), o1 = (int)((int64_t)NO * (blockIdx.x + 1) / gridDim.x);
     const int n = o1 - o0;
     if (n <= 0) return;
+    const unsigned tag = ll_tag(epoch, lay_idx);
     float* vals = part;                  // [n][chunks]
     float* tots = part + n * chunks;     // [2][chunks] partial sums of the (at most two) heads spanned
     const int h0 = o0 / 64;
     const int nh = (o1 - 1) / 64 - h0 + 1;
-    // every partial of this slice in one batch of loads (one L2 round trip, not one per pass)
+    // every partial of this slice in one batch of polled loads (tots follows vals)
     const int nv = n * chunks, nt = nh * chunks;
-    constexpr int B = 4;
-    float lv[B];
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const int t = tid + b * CT;
-      lv[b] = 0.f;
-      if (t < nv) {
-        const int o = o0 + t / chunks, c = t % chunks;
-        const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
-        lv[b] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
-      } else if (t < nv + nt) {
-        const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
-        lv[b] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const int t = tid + b * CT;
-      if (t < nv + nt) vals[t] = lv[b];  // tots follows vals
-    }
-    for (int t = tid + B * CT; t < nv + nt; t += CT) {  // more partials than the batch holds
-      if (t < nv) {
-        const int o = o0 + t / chunks, c = t % chunks;
-        const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
-        vals[t] = __ldcg(&a.pacc[(int64_t)((g * chunks + c) * G + hh) * 64 + d]);
-      } else {
-        const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
-        vals[t] = __ldcg(&a.psum[(g * chunks + c) * G + hh]);
-      }
-    }
+    ll_gather<4>(nv + nt, tag,
+                 [&](int t) {
+                   if (t < nv) {
+                     const int o = o0 + t / chunks, c = t % chunks;
+                     const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
+                     return (const u64*)a.ll_pacc + (int64_t)((g * chunks + c) * G + hh) * 64 + d;
+                   }
+                   const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
+                   return (const u64*)a.ll_psum + (g * chunks + c) * G + hh;
+                 },
+                 [&](int t, float v) { vals[t] = v; });
     cons_sync();
     for (int t = tid; t < n; t += CT) {
       const int o = o0 + t, hi = o / 64 - h0;
@@ -1205,7 +1379,7 @@ struct Consumer {
         s += vals[t * chunks + c];
         tot += tots[hi * chunks + c];
       }
-      a.att[o] = s * __fdiv_rn(1.f, tot);
+      ll_st(a.ll_att + o, s * __fdiv_rn(1.f, tot), tag);
     }
     cons_sync();
   }
@@ -1233,7 +1407,11 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   // the sequence id is read once: every later use (attention, KV append, the L2
   // prefetch of the layer's K/V rows) reads the shared copy
   __shared__ int seq_s;
-  if (tid == 0) seq_s = *a.seq;
+  __shared__ unsigned epoch_s;
+  if (tid == 0) {
+    seq_s = *a.seq;
+    epoch_s = __ldcg(a.epoch);
+  }
   __syncthreads();
   const int seqv = seq_s;
   const int len = a.kv_len[seqv] + 1;  // context including this token
@@ -1271,6 +1449,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   // -------------------------------------------------------------- consumers
   Consumer<AM> c{a, sh, ring, slot_bytes, part};
   c.tid = tid;
+  c.epoch = epoch_s;
   c.seq_v = seqv;
   c.ep.pos = nullptr;
   c.ep.seq = &seq_s;
@@ -1294,8 +1473,6 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   c.ep.cos_t = &rope_s[1][0] - (int64_t)(len - 1) * half;
   c.stamp();
   const float* emb = a.embd + (int64_t)(*a.token) * a.H;
-  if (blockIdx.x == 0)
-    for (int t = tid; t < a.H; t += CT) a.x[t] = emb[t];  // residual stream
   const int G = a.nH / a.nKv;
   const int chunks = max(1, (int)gridDim.x / a.nKv);
   (void)G;
@@ -1308,21 +1485,24 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     const int l = ph >> 2, kind = ph & 3;
     const MegaLayer& L = sh.lay[l & 1];
     if (kind == 1) {
-      if (!c.grid_barrier(nullptr, 0, -1, nullptr, &L, chunks, len)) return;
-      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_scores(L, it / chunks, it % chunks, chunks, len);
-      if (!c.grid_barrier()) return;
-      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) c.attn_pv(L, it / chunks, it % chunks, chunks, len);
-      if (!c.grid_barrier()) return;
-      c.attn_combine(chunks);
+      // attention: every wait on another CTA's result is a poll of its exchange words
+      if (!c.transition(nullptr, 0, -1, nullptr, &L, chunks, len)) return;
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x)
+        c.attn_scores(L, l, it / chunks, it % chunks, chunks, len);
+      if (!c.transition()) return;
+      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x)
+        c.attn_pv(L, l, it / chunks, it % chunks, chunks, len);
+      if (!c.transition()) return;
+      c.attn_combine(l, chunks);
     }
-    // the barrier before a GEMV phase also plans it; the one before a layer's
+    // the transition before a GEMV phase also plans it; the one before a layer's
     // gate|up brings the next layer's table entry on chip
     if (ph > 0) {
       const bool nx = kind == 2 && l + 1 < a.n_layers;
-      if (!c.grid_barrier(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb)) return;
+      if (!c.transition(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb)) return;
     }
     const SegPlan& P = sh.plan;
-    c.load_x(P.src, P.gamma, P.K, P.s->fmt != SM_Q8_0, P.mma ? P.s->fmt : 0);
+    c.load_x(P.src, P.src_ll, P.src_tag, P.gamma, P.K, P.s->fmt != SM_Q8_0, P.mma ? P.s->fmt : 0, P.r1 > P.r0);
     if (tid == 0) sh.phase = ph;
     if (!c.seg(P)) return;
   }
@@ -1361,6 +1541,9 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     if (tid == 0) {
       *a.next_token = bi;
       a.kv_len[seqv] = len;
+      // every CTA has read the epoch and finished its exchange (it arrived above):
+      // the next launch tags its words with the next epoch
+      *a.epoch = epoch_s + 1u;
     }
   }
 }
@@ -1378,6 +1561,46 @@ size_t mega_scratch_floats(int nH, int nKv, int hd, int max_ctx, int grid) {
   const int chunks = std::max(1, grid / nKv);
   const int G = nH / nKv;
   return (size_t)nH * max_ctx + (size_t)nKv * chunks * G * (2 + hd) + 2 * (size_t)grid + 64;
+}
+
+namespace {
+// region sizes in 64-bit words, each rounded up to a 16-byte multiple
+struct LLLayout {
+  size_t off[10];
+  size_t total;
+};
+LLLayout ll_layout(int H, int qd, int kd, int F, int nH, int nKv, int hd, int grid) {
+  const size_t chunks = std::max(1, grid / nKv), G = nH / nKv;
+  const size_t n[10] = {2,  // epoch word (+ pad)
+                        (size_t)H, (size_t)H, (size_t)qd, 2 * (size_t)kd, nKv * chunks * G, nKv * chunks * G * hd,
+                        nKv * chunks * G, (size_t)qd, (size_t)F};
+  LLLayout L;
+  size_t o = 0;
+  for (int i = 0; i < 10; ++i) {
+    L.off[i] = o;
+    o += (n[i] + 1) & ~(size_t)1;
+  }
+  L.total = o;
+  return L;
+}
+}  // namespace
+
+size_t mega_ll_words(int H, int qd, int kd, int F, int nH, int nKv, int hd, int grid) {
+  return ll_layout(H, qd, kd, F, nH, nKv, hd, grid).total;
+}
+
+void mega_ll_assign(MegaArgs& a, unsigned long long* base, int grid) {
+  const LLLayout L = ll_layout(a.H, a.qd, a.kd, a.F, a.nH, a.nKv, a.hd, grid);
+  a.epoch = (unsigned*)base;
+  a.ll_x0 = base + L.off[1];
+  a.ll_x1 = base + L.off[2];
+  a.ll_q = base + L.off[3];
+  a.ll_kv = base + L.off[4];
+  a.ll_cmax = base + L.off[5];
+  a.ll_pacc = base + L.off[6];
+  a.ll_psum = base + L.off[7];
+  a.ll_att = base + L.off[8];
+  a.ll_act = base + L.off[9];
 }
 
 bool mega_supported(const MegaArgs& a) {

@@ -54,7 +54,22 @@ struct MegaArgs {
   float* pacc = nullptr;    // [nKv][chunks][G][hd]
   float* amax_val = nullptr;  // [grid]
   int* amax_idx = nullptr;    // [grid]
-  unsigned* sync = nullptr;   // [0] grid barrier, [1..nKv] head counters, [63] argmax counter (zeroed per launch)
+  unsigned* sync = nullptr;   // [63] argmax counter (zeroed per launch)
+  // Tagged exchange words: the CTAs hand each other the step's vectors as 64-bit
+  // words {float value, uint32 tag} (low / high half), stored and polled with
+  // gpu-scope relaxed 8-byte accesses, so a word carries its own readiness and no
+  // grid-wide barrier is needed.  tag = ((epoch + 1) << 8) | (layer & 255); the
+  // epoch advances once per launch (last CTA), so no buffer is ever cleared.
+  unsigned long long* ll_x0 = nullptr;    // [H] residual stream after attention (O + residual)
+  unsigned long long* ll_x1 = nullptr;    // [H] residual stream after the MLP (down + residual)
+  unsigned long long* ll_q = nullptr;     // [qd] rotated queries
+  unsigned long long* ll_kv = nullptr;    // [2 kd] this token's rotated K row, then its V row
+  unsigned long long* ll_cmax = nullptr;  // [nKv][chunks][G] chunk maxima of the scaled scores
+  unsigned long long* ll_pacc = nullptr;  // [nKv][chunks][G][hd] chunk partials of e.V
+  unsigned long long* ll_psum = nullptr;  // [nKv][chunks][G] chunk partial sums of e
+  unsigned long long* ll_att = nullptr;   // [qd] attention output
+  unsigned long long* ll_act = nullptr;   // [F] silu(gate) * up
+  unsigned* epoch = nullptr;              // launch counter (device word, never reset)
   int* status = nullptr;
   unsigned long long* trace = nullptr;  // optional [grid][MEGA_TRACE_EVENTS] globaltimer stamps
   // schedule
@@ -69,6 +84,11 @@ constexpr int MEGA_TRACE_EVENTS = 1024;
 
 // Sizes of the scratch the launcher expects (floats / ints) for a given grid.
 size_t mega_scratch_floats(int nH, int nKv, int hd, int max_ctx, int grid);
+// 64-bit words of the tagged exchange buffer (epoch word + every ll_* region,
+// each region starting on a 16-byte boundary)
+size_t mega_ll_words(int H, int qd, int kd, int F, int nH, int nKv, int hd, int grid);
+// points a's ll_* regions and epoch into `base` (mega_ll_words words)
+void mega_ll_assign(MegaArgs& a, unsigned long long* base, int grid);
 bool mega_supported(const MegaArgs& a);
 // Q|K|V CTA ranges of a layer for a grid of `grid` CTAs, in proportion to each segment's bytes
 void mega_layer_split(MegaLayer& L, int K, int grid);
