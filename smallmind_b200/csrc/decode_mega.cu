@@ -63,6 +63,12 @@ __device__ __forceinline__ u64 ll_ld(const u64* p) {
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// two consecutive words (16-byte aligned): each 8-byte half is single-copy atomic
+__device__ __forceinline__ ulonglong2 ll_ld2(const u64* p) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void ll_st(u64* p, float v, unsigned tag) {
   const u64 w = ((u64)tag << 32) | (u64)__float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -176,6 +182,7 @@ struct Shared {
   SegPlan plan;      // the next GEMV phase
   float red[MW * MGMAX];
   float vec[4 * MGMAX];
+  __align__(16) float kvrow[64];  // this token's K row of the attention item's kv head
   int flag[4];
   int consumed;
   int abort;
@@ -183,6 +190,8 @@ struct Shared {
 };
 
 // ---------------------------------------------------------------- producer
+// AM: every segment is on the tensor-core path (no dp4a staging code compiled in)
+template <bool AM>
 struct Producer {
   const MegaArgs& a;
   Shared& sh;
@@ -236,7 +245,7 @@ struct Producer {
     }
     int r0, r1;
     seg_rows_in(s.rows, blockIdx.x, c0, c1 < 0 ? (int)gridDim.x : c1, r0, r1);
-    if (mma_seg(a, s)) {
+    if (AM || mma_seg(a, s)) {
       mseg(s, K, r0, r1);
       return;
     }
@@ -286,20 +295,30 @@ struct Consumer {
   int ev = 0;
   int seq_v = 0;  // the sequence id (read once)
   int lx = 0;  // load_x calls (trace: the sub-steps of calls 4..11 go to events 900..)
+  // Phase timestamps (SMALLMIND_MEGA_TRACE) exist only in a build with
+  // -DSMALLMIND_MEGA_TRACE_BUILD: the kernel's code is kept small, because every
+  // layer runs all of it once and what does not fit the SM's instruction cache
+  // is fetched again each layer.
   __device__ void stamp_at(int e) {
+#ifdef SMALLMIND_MEGA_TRACE_BUILD
     if (a.trace && tid == 0 && e < MEGA_TRACE_EVENTS) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.trace[(size_t)blockIdx.x * MEGA_TRACE_EVENTS + e] = t;
     }
+#else
+    (void)e;
+#endif
   }
   __device__ void stamp() {
+#ifdef SMALLMIND_MEGA_TRACE_BUILD
     if (a.trace && tid == 0 && ev < MEGA_TRACE_EVENTS) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.trace[(size_t)blockIdx.x * MEGA_TRACE_EVENTS + ev] = t;
     }
     ++ev;
+#endif
   }
   // this thread's slice of the current input vector, as dp4a byte planes
   XPlanes xp;
@@ -434,6 +453,52 @@ struct Consumer {
         if (i < n) put(i, ll_val(w[b]));
       }
     }
+  }
+
+  // Consumer threads gather n (even) consecutive exchange words from src (16-byte
+  // aligned) into dst[0, n): two words per 16-byte load, up to 2B words per thread
+  // in flight.
+  template <int B>
+  __device__ void ll_gather2(int n, unsigned tag, const u64* src, float* dst) {
+    const int np = n >> 1;
+    for (int base = 0; base < np; base += B * CT) {
+      ulonglong2 w[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int i = base + b * CT + tid;
+        w[b] = i < np ? ll_ld2(src + 2 * i) : make_ulonglong2(0ull, 0ull);
+      }
+      long long t0 = 0;
+      while (true) {
+        bool all = true;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int i = base + b * CT + tid;
+          if (i < np && !(ll_ok(w[b].x, tag) && ll_ok(w[b].y, tag))) {
+            all = false;
+            w[b] = ll_ld2(src + 2 * i);
+          }
+        }
+        if (all || !poll_tick(t0)) break;
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int i = base + b * CT + tid;
+        if (i < np) *(float2*)&dst[2 * i] = make_float2(ll_val(w[b].x), ll_val(w[b].y));
+      }
+    }
+  }
+
+  // two words, polled together by the calling thread alone
+  __device__ void ll_wait2(const u64* p0, const u64* p1, unsigned tag, float& v0, float& v1) {
+    u64 w0 = ll_ld(p0), w1 = ll_ld(p1);
+    long long t0 = 0;
+    while (!(ll_ok(w0, tag) && ll_ok(w1, tag)) && poll_tick(t0)) {
+      w0 = ll_ld(p0);
+      w1 = ll_ld(p1);
+    }
+    v0 = ll_val(w0);
+    v1 = ll_val(w1);
   }
 
   // one word, polled by the calling thread alone
@@ -631,10 +696,12 @@ struct Consumer {
       // the vector arrives in exchange words: gathered into part [0, K) first (the
       // block partials are written there only after the planes are built)
       if (need)
-        ll_gather<12>(K, src_tag, [&](int i) { return src_ll + i; }, [&](int i, float v) { part[i] = v; });
+        ll_gather2<6>(K, src_tag, src_ll, part);
       else
         for (int i = tid; i < K; i += CT) part[i] = 0.f;
+      if (lxe >= 0) stamp_at(lxe + 1);
       cons_sync();
+      if (lxe >= 0) stamp_at(lxe + 2);
       src = part;
     }
     float sq = 0.f;
@@ -979,47 +1046,6 @@ struct Consumer {
     return g;
   }
 
-  // Epilogue of one group of rows (final values v[0..R-1]) into the exchange words
-  // PL.dst: SiLU gate (GLU), RoPE (queries; keys, which also go to the cache), the
-  // V row (also to the cache); STORE (the LM head) writes plain logits.
-  template <int R>
-  __device__ void mega_store(const GemvSeg& s, const SegPlan& PL, int lg, float* v) {
-    if (s.mode == GEMV_GLU) {
-#pragma unroll
-      for (int r = 0; r < R / 2; ++r) {
-        const int row = group_row<R>(s, lg, r);
-        if (row >= s.rows) continue;
-        const float gt = v[r], up = v[r + R / 2];
-        const float c = fmaxf(-20.f, fminf(gt, 20.f));
-        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));  // ActivationOps.cs:304-309
-        ll_st(PL.dst + row, __fmul_rn(__fmul_rn(gt, sig), up), PL.dst_tag);
-      }
-      return;
-    }
-    const int row0 = group_row<R>(s, lg, 0);
-    if (s.mode == GEMV_ROPE_Q || s.mode == GEMV_ROPE_K_CACHE) {
-      const int pos = *ep.pos;
-#pragma unroll
-      for (int r = 0; r < R; r += 2) rope_pair(v[r], v[r + 1], ep, pos, (row0 + r) % ep.head_dim);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = row0 + r;
-      if (row >= s.rows) continue;
-      if (s.mode == GEMV_ROPE_K_CACHE || s.mode == GEMV_V_CACHE) {
-        // head-major cache [seq][kv_head][pos][hd] (MultiHeadAttention.cs:262-274) for later steps;
-        // this step's attention reads the row from the exchange words
-        const int64_t seq = *ep.seq, pos = *ep.pos;
-        const int h = row / ep.head_dim, d = row - h * ep.head_dim;
-        s.y[((seq * ep.n_kv + h) * ep.max_ctx + pos) * ep.head_dim + d] = v[r];
-      }
-      if (PL.dst)
-        ll_st(PL.dst + row, v[r], PL.dst_tag);
-      else
-        s.y[row] = v[r];
-    }
-  }
-
   // GEMV rows of this CTA for one segment; `amax` (head only) tracks the local argmax.
   __device__ bool seg(const SegPlan& PL) {
     const MegaSeg& s = *PL.s;
@@ -1129,17 +1155,36 @@ struct Consumer {
         }
         v[q] = t;
       }
-      if (addm) {
-        const float rs = it == tid ? resid
-                                   : (PL.res_ll ? ll_wait1(PL.res_ll + r0 + it, PL.res_tag)
-                                                : __ldg(&PL.res_plain[r0 + it]));
-        ll_st(PL.dst + r0 + it, rs + v[0], PL.dst_tag);
-      } else if (glu) {
-        mega_store<2>(g, PL, r0 + it, v);
+      // one epilogue for every mode: GLU (gate row it, up row nout + it -> row r0 + it),
+      // RoPE pairs (rows r0 + 2it, + 1), residual add, plain store
+      const int row0 = r0 + (pairs ? 2 * it : it);
+      int nst = 1;
+      float o0 = v[0], o1 = v[1];
+      if (glu) {
+        const float c = fmaxf(-20.f, fminf(v[0], 20.f));
+        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));  // ActivationOps.cs:304-309
+        o0 = __fmul_rn(__fmul_rn(v[0], sig), v[1]);
       } else if (pairs) {
-        mega_store<2>(g, PL, (r0 >> 1) + it, v);
-      } else {
-        mega_store<1>(g, PL, r0 + it, v);
+        rope_pair(o0, o1, ep, *ep.pos, row0 % ep.head_dim);
+        nst = nr;
+      } else if (addm) {
+        o0 += it == tid ? resid
+                        : (PL.res_ll ? ll_wait1(PL.res_ll + row0, PL.res_tag) : __ldg(&PL.res_plain[row0]));
+      }
+      for (int q = 0; q < nst; ++q) {
+        const int row = row0 + q;
+        const float val = q ? o1 : o0;
+        if (s.mode == GEMV_ROPE_K_CACHE || s.mode == GEMV_V_CACHE) {
+          // head-major cache [seq][kv_head][pos][hd] (MultiHeadAttention.cs:262-274) for later
+          // steps; this step's attention reads the row from the exchange words
+          const int64_t seq = *ep.seq, pos = *ep.pos;
+          const int h = row / ep.head_dim, d = row - h * ep.head_dim;
+          s.y[((seq * ep.n_kv + h) * ep.max_ctx + pos) * ep.head_dim + d] = val;
+        }
+        if (PL.dst)
+          ll_st(PL.dst + row, val, PL.dst_tag);
+        else
+          s.y[row] = val;
       }
       if (amax_v && (v[0] > bv || (v[0] == bv && r0 + it < bi))) {
         bv = v[0];
@@ -1205,27 +1250,23 @@ struct Consumer {
     const int sub = tid & 7, slot = tid >> 3;  // 60 key slots
     constexpr int SLOTS = CT / 8;
     const unsigned tag = ll_tag(epoch, lay_idx);
-    // key row j: the cache for earlier tokens; this token's row (j = len - 1) from
-    // the exchange words its Q|K|V CTA wrote this step
-    auto key8 = [&](int j, float4& k0, float4& k1) {
-      if (j == len - 1) {
-        const u64* kp = a.ll_kv + g * HD + sub * 8;
-        float kv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) kv[i] = ll_wait1(kp + i, tag);
-        k0 = make_float4(kv[0], kv[1], kv[2], kv[3]);
-        k1 = make_float4(kv[4], kv[5], kv[6], kv[7]);
-      } else {
-        const float4* kp = (const float4*)(kb + (int64_t)j * HD + sub * 8);
-        k0 = __ldcg(kp);
-        k1 = __ldcg(kp + 1);
-      }
-    };
+    // key row j: the cache for earlier tokens; this token's row (j = len - 1) comes
+    // from the exchange words its Q|K|V CTA wrote this step, staged in sh.kvrow
+    const int jn = len - 1 - j0;  // local index of this token's row (>= n: not in this chunk)
     // the first pass's key rows load together with the queries (one round trip)
     float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), k1 = k0;
-    if (slot < n) key8(j0 + slot, k0, k1);
-    ll_gather<2>(G * HD, tag, [&](int i) { return a.ll_q + g * G * HD + i; }, [&](int i, float v) { qs[i] = v; });
+    if (slot < n && slot != jn) {
+      const float4* kp = (const float4*)(kb + (int64_t)(j0 + slot) * HD + sub * 8);
+      k0 = __ldcg(kp);
+      k1 = __ldcg(kp + 1);
+    }
+    if (jn < n && tid < HD) sh.kvrow[tid] = ll_wait1(a.ll_kv + g * HD + tid, tag);
+    ll_gather2<1>(G * HD, tag, a.ll_q + g * G * HD, qs);
     cons_sync();
+    if (slot == jn) {
+      k0 = *(const float4*)&sh.kvrow[sub * 8];
+      k1 = *(const float4*)&sh.kvrow[sub * 8 + 4];
+    }
     float lmax[MGMAX];
 #pragma unroll
     for (int h = 0; h < MGMAX; ++h) lmax[h] = -FLT_MAX;
@@ -1235,7 +1276,12 @@ struct Consumer {
       const bool valid = jj < n;
       if (p > 0) {
         k0 = k1 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) key8(j0 + jj, k0, k1);
+        if (valid) {
+          const float4* kp = jj == jn ? (const float4*)&sh.kvrow[sub * 8]
+                                      : (const float4*)(kb + (int64_t)(j0 + jj) * HD + sub * 8);
+          k0 = jj == jn ? kp[0] : __ldcg(kp);
+          k1 = jj == jn ? kp[1] : __ldcg(kp + 1);
+        }
       }
       const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
@@ -1289,7 +1335,7 @@ struct Consumer {
     {
       // exact row max of every head of the group: all chunk maxima, gathered in parallel
       float* cm = att_cm(per);  // [chunks][G]
-      ll_gather<2>(chunks * G, tag, [&](int i) { return a.ll_cmax + g * chunks * G + i; },
+      ll_gather<1>(chunks * G, tag, [&](int i) { return a.ll_cmax + g * chunks * G + i; },
                    [&](int i, float v) { cm[i] = v; });
       cons_sync();
       if (tid < G) {
@@ -1347,39 +1393,56 @@ struct Consumer {
     cons_sync();
   }
 
-  // ---- attention, phase C: out[o] = sum_c pacc / sum_c psum for this CTA's slice of the outputs
+  // ---- attention, phase C: out[o] = sum_c pacc / sum_c psum for this CTA's slice of the outputs.
+  // Output o's partials over the chunks are split into P interleaved parts (one thread
+  // each, two chunks polled per round trip); the parts are then added in part order.
+  // The last two warps add each spanned head's psum over the chunks.
   __device__ void attn_combine(int lay_idx, int chunks) {
     const int G = a.nH / a.nKv, NO = a.nH * 64;
     const int o0 = (int)((int64_t)NO * blockIdx.x / gridDim.x), o1 = (int)((int64_t)NO * (blockIdx.x + 1) / gridDim.x);
     const int n = o1 - o0;
     if (n <= 0) return;
     const unsigned tag = ll_tag(epoch, lay_idx);
-    float* vals = part;                  // [n][chunks]
-    float* tots = part + n * chunks;     // [2][chunks] partial sums of the (at most two) heads spanned
-    const int h0 = o0 / 64;
-    const int nh = (o1 - 1) / 64 - h0 + 1;
-    // every partial of this slice in one batch of polled loads (tots follows vals)
-    const int nv = n * chunks, nt = nh * chunks;
-    ll_gather<4>(nv + nt, tag,
-                 [&](int t) {
-                   if (t < nv) {
-                     const int o = o0 + t / chunks, c = t % chunks;
-                     const int h = o / 64, d = o % 64, g = h / G, hh = h % G;
-                     return (const u64*)a.ll_pacc + (int64_t)((g * chunks + c) * G + hh) * 64 + d;
-                   }
-                   const int u = t - nv, h = h0 + u / chunks, c = u % chunks, g = h / G, hh = h % G;
-                   return (const u64*)a.ll_psum + (g * chunks + c) * G + hh;
-                 },
-                 [&](int t, float v) { vals[t] = v; });
+    const int h0 = o0 >> 6, nh = ((o1 - 1) >> 6) - h0 + 1;
+    const int P = max(1, min(chunks, (CT - 64) / n));
+    float* sums = part;           // [P][n]
+    float* tots = part + P * n;   // [nh]
+    const int64_t cstride = (int64_t)G * 64;
+    if (tid < P * n) {
+      const int r = tid % n, pp = tid / n;
+      const int o = o0 + r, h = o >> 6, g = h / G;
+      const u64* base = a.ll_pacc + (int64_t)g * chunks * cstride + (int64_t)(h - g * G) * 64 + (o & 63);
+      float sm = 0.f;
+      for (int c = pp; c < chunks; c += 2 * P) {
+        const bool two = c + P < chunks;
+        float v0, v1;
+        ll_wait2(base + c * cstride, base + (two ? c + P : c) * cstride, tag, v0, v1);
+        sm += v0;
+        if (two) sm += v1;
+      }
+      sums[pp * n + r] = sm;
+    }
+    const int w = tid >> 5, ln = tid & 31;
+    if (w >= CWARPS - 2) {
+      for (int hi = CWARPS - 1 - w; hi < nh; hi += 2) {
+        const int h = h0 + hi, g = h / G;
+        const u64* base = a.ll_psum + (int64_t)g * chunks * G + (h - g * G);
+        float sm = 0.f;
+        for (int c = ln; c < chunks; c += 64) {
+          float v0, v1;
+          ll_wait2(base + (int64_t)c * G, base + (int64_t)min(c + 32, chunks - 1) * G, tag, v0, v1);
+          sm += v0;
+          if (c + 32 < chunks) sm += v1;
+        }
+        sm = warp_sum(sm);
+        if (ln == 0) tots[hi] = sm;
+      }
+    }
     cons_sync();
     for (int t = tid; t < n; t += CT) {
-      const int o = o0 + t, hi = o / 64 - h0;
-      float s = 0.f, tot = 0.f;
-      for (int c = 0; c < chunks; ++c) {
-        s += vals[t * chunks + c];
-        tot += tots[hi * chunks + c];
-      }
-      ll_st(a.ll_att + o, s * __fdiv_rn(1.f, tot), tag);
+      float sm = 0.f;
+      for (int pp = 0; pp < P; ++pp) sm += sums[pp * n + t];
+      ll_st(a.ll_att + o0 + t, sm * __fdiv_rn(1.f, tots[((o0 + t) >> 6) - h0]), tag);
     }
     cons_sync();
   }
@@ -1422,7 +1485,7 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   if (warp == CWARPS) {
     // ------------------------------------------------------------ producer
     if ((tid & 31) == 0) {
-      Producer p{a, sh, ring, slot_bytes};
+      Producer<AM> p{a, sh, ring, slot_bytes};
       // one call site per kind of work keeps the kernel's code small (phase p:
       // layer p / 4, Q|K|V, O, gate|up, down; the last one is the LM head)
       for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
@@ -1479,29 +1542,39 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
   // one call site per kind of work keeps the kernel's code small: phase p is
   // layer p / 4, kind Q|K|V (attention follows), O, gate|up, down; the last
   // phase is the LM head
-  if (tid == 64) c.prepare(0, emb);
-  cons_sync();
-  for (int ph = 0; ph <= 4 * a.n_layers; ++ph) {
-    const int l = ph >> 2, kind = ph & 3;
+  // Steps of a layer: 0 Q|K|V, 1 attention scores, 2 exp / P.V, 3 combine, 4 O,
+  // 5 gate|up, 6 down; the last step is the LM head.  One transition call site and
+  // one call site per kind of work keep the kernel's code small (every layer runs
+  // all of it once; what misses the instruction cache is fetched again).
+  const int nsteps = 7 * a.n_layers + 1;
+  for (int st = 0; st < nsteps; ++st) {
+    const int l = st / 7, k = st - 7 * l;
+    const bool attn = k >= 1 && k <= 3;
+    // the GEMV phase of this step (layer l; kind Q|K|V, O, gate|up, down; the head)
+    const int ph = attn ? -1 : 4 * l + (k == 0 ? 0 : k - 3);
     const MegaLayer& L = sh.lay[l & 1];
-    if (kind == 1) {
-      // attention: every wait on another CTA's result is a poll of its exchange words
-      if (!c.transition(nullptr, 0, -1, nullptr, &L, chunks, len)) return;
-      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x)
-        c.attn_scores(L, l, it / chunks, it % chunks, chunks, len);
-      if (!c.transition()) return;
-      for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x)
-        c.attn_pv(L, l, it / chunks, it % chunks, chunks, len);
-      if (!c.transition()) return;
-      c.attn_combine(l, chunks);
-    }
-    // the transition before a GEMV phase also plans it; the one before a layer's
-    // gate|up brings the next layer's table entry on chip
-    if (ph > 0) {
-      const bool nx = kind == 2 && l + 1 < a.n_layers;
-      if (!c.transition(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb)) return;
+    // the transition before a GEMV step plans it; the one before gate|up brings the
+    // next layer's table entry on chip; the one before the scores prefetches this
+    // CTA's K / V rows into L2
+    const bool nx = k == 5 && l + 1 < a.n_layers;
+    if (!c.transition(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb, k == 1 ? &L : nullptr, chunks, len))
+      return;
+    if (attn) {
+      // every wait on another CTA's result is a poll of its exchange words
+      if (k == 3) {
+        c.attn_combine(l, chunks);
+      } else {
+        for (int it = blockIdx.x; it < a.nKv * chunks; it += gridDim.x) {
+          if (k == 1)
+            c.attn_scores(L, l, it / chunks, it % chunks, chunks, len);
+          else
+            c.attn_pv(L, l, it / chunks, it % chunks, chunks, len);
+        }
+      }
+      continue;
     }
     const SegPlan& P = sh.plan;
+    if (c.lx >= 4 && c.lx < 12) c.stamp_at(900 + 8 * (c.lx - 4) + 6);
     c.load_x(P.src, P.src_ll, P.src_tag, P.gamma, P.K, P.s->fmt != SM_Q8_0, P.mma ? P.s->fmt : 0, P.r1 > P.r0);
     if (tid == 0) sh.phase = ph;
     if (!c.seg(P)) return;
