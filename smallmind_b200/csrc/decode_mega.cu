@@ -692,6 +692,15 @@ struct Consumer {
     float* sx = part + pbase + 48 * U;         // [U][2] at most
     float* bx = sx + 2 * U;                    // [NB]
     mend = pbase + 50 * U + NB;
+    // this thread's first 8 RMSNorm weights, loaded before the exchange wait so the two
+    // round trips overlap
+    float4 gpre0 = make_float4(0.f, 0.f, 0.f, 0.f), gpre1 = gpre0;
+    const int t_first = (tid >> 5) * 32 + lane;
+    if (gamma && t_first < 4 * U) {
+      const float4* gg = (const float4*)(gamma + 8 * t_first);
+      gpre0 = __ldg(gg);
+      gpre1 = __ldg(gg + 1);
+    }
     if (src_ll) {
       // the vector arrives in exchange words: gathered into part [0, K) first (the
       // block partials are written there only after the planes are built)
@@ -713,7 +722,8 @@ struct Consumer {
       float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       if (gamma) {
         const float4* gg = (const float4*)(gamma + 32 * uu + 8 * pp);
-        const float4 g0 = __ldg(gg), g1 = __ldg(gg + 1);
+        const bool first = t == t_first;
+        const float4 g0 = first ? gpre0 : __ldg(gg), g1 = first ? gpre1 : __ldg(gg + 1);
         const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -1554,10 +1564,10 @@ __global__ void __launch_bounds__(MT, 1) decode_mega_kernel(const __grid_constan
     const int ph = attn ? -1 : 4 * l + (k == 0 ? 0 : k - 3);
     const MegaLayer& L = sh.lay[l & 1];
     // the transition before a GEMV step plans it; the one before gate|up brings the
-    // next layer's table entry on chip; the one before the scores prefetches this
-    // CTA's K / V rows into L2
+    // next layer's table entry on chip; the one before Q|K|V prefetches this CTA's
+    // attention K / V rows of the layer into L2 (they are read two steps later)
     const bool nx = k == 5 && l + 1 < a.n_layers;
-    if (!c.transition(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb, k == 1 ? &L : nullptr, chunks, len))
+    if (!c.transition(nx ? &a.layers[l + 1] : nullptr, (l + 1) & 1, ph, emb, k == 0 && l < a.n_layers ? &L : nullptr, chunks, len))
       return;
     if (attn) {
       // every wait on another CTA's result is a poll of its exchange words
