@@ -190,6 +190,91 @@ def build_gpu_model(sm, ctx, cfg, seed=1234, schemes=None, block_size=32):
     return model, weights
 
 
+def build_host_model(sm, ctx, cfg, seed=1234, schemes=None, block_size=32):
+    """The bench model's packed weights on the host (quantized on the device as in
+    build_gpu_model, then copied back): the input of tensor-parallel sharding."""
+    import torch
+
+    from smallmind_b200 import _lib as L
+    from smallmind_b200.tp import PackedWeight, ShardModel
+    lib = L.lib()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+
+    def make(name, rows, cols):
+        sch = int(getattr(sm.QuantScheme, (schemes or SCHEMES)[name]))
+        n = rows * cols
+        src = torch.randn(n, generator=gen, device="cuda") * 0.02
+        nbytes = {6: n // 256 * 144, 7: n // 256 * 210, 2: n, 3: n // 2}[sch]
+        data = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        scales = torch.empty(max(1, n // block_size), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        L.check(lib.sm_quantize(ctx.handle, sch, src.data_ptr(), n, block_size, data.data_ptr(), scales.data_ptr()),
+                "quantize")
+        torch.cuda.synchronize()
+        return PackedWeight(sch, rows, cols, data.cpu().numpy(), scales.cpu().numpy() if sch in (2, 3) else None,
+                            block_size)
+
+    sh = linear_shapes(cfg)
+    emb = (torch.randn(cfg["vocab_size"] * cfg["hidden"], generator=gen, device="cuda") * 0.02).cpu().numpy()
+    ones = np.ones(cfg["hidden"], np.float32)
+    out = make("output", *sh["output"])
+    layers = []
+    for _ in range(cfg["n_layers"]):
+        L_ = {"attn_norm": ones, "ffn_norm": ones}
+        for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+            L_[n] = make(n, *sh[n])
+        layers.append(L_)
+    return ShardModel(dict(cfg), emb, ones, out, layers)
+
+
+def time_tp_decode(sm, ctx, torch, stream, world, rank, steps, warmup, prompt_len):
+    """Tensor-parallel bs1 decode of the TinyLlama-shaped model over the whole group:
+    device time per step (max over ranks) and the time of the step's 2 x n_layers
+    all-reduces of one hidden row, timed alone through the same NCCL group."""
+    from smallmind_b200 import sharding, tp
+    cfg = dict(TINYLLAMA)
+    group = tp.TensorParallelGroup(ctx, world, rank)
+    host = build_host_model(sm, ctx, cfg)
+    model = sm.CudaModel.from_host(ctx, tp.shard_model(host, world, rank))
+    del host
+    group.shard(model)
+    kv = sm.KVCache(model, 1, prompt_len + warmup + steps + 8)
+    prompt = np.random.RandomState(100).randint(0, cfg["vocab_size"], prompt_len).astype(np.int32)
+    t0, _ = kv.prefill(0, prompt, want_logits=False)
+    seq = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tok = torch.tensor([t0], dtype=torch.int32, device="cuda")
+    for _ in range(warmup):
+        kv.decode_device(seq.data_ptr(), tok.data_ptr(), 1, None, tok.data_ptr())
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.distributed.barrier()
+    e0.record(stream)
+    for _ in range(steps):
+        kv.decode_device(seq.data_ptr(), tok.data_ptr(), 1, None, tok.data_ptr())
+    e1.record(stream)
+    e1.synchronize()
+    ms = sharding.max_over_ranks(e0.elapsed_time(e1) / steps, device="cuda")
+    # the step's all-reduces alone: 2 per layer, one hidden row of fp32 each
+    buf = torch.zeros(cfg["hidden"], device="cuda")
+    n_ar = 2 * cfg["n_layers"]
+    for _ in range(3):
+        group.allreduce_(buf.data_ptr(), cfg["hidden"])
+    stream.synchronize()
+    torch.distributed.barrier()
+    e0.record(stream)
+    for _ in range(20):
+        for _ in range(n_ar):
+            group.allreduce_(buf.data_ptr(), cfg["hidden"])
+    e1.record(stream)
+    e1.synchronize()
+    ar_us = sharding.max_over_ranks(e0.elapsed_time(e1) * 1000 / 20, device="cuda")
+    kv.close()
+    model.close()
+    return {"tp": world, "tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 4),
+            "allreduce_us_per_token": round(ar_us, 1), "allreduces_per_token": n_ar,
+            "allreduce_bytes": 4 * cfg["hidden"], "path": "per-kernel decode step, NCCL all-reduce after O and down"}
+
+
 def time_gemv(sm, ctx, ws, torch, reps=5):
     """Device time of the M=1 GEMV over a rotating set of layer weights (> L2), launched from a
     CUDA graph so host launch overhead is not timed."""
@@ -707,6 +792,10 @@ def run_ours(args):
                          f"C++ restatement of the reference algorithm, quantized linears row-split over {nt} "
                          f"threads (the reference runs them single-threaded)"}
 
+    tp_res = None
+    if world > 1 and not args.no_tp:
+        tp_res = time_tp_decode(sm, ctx, torch, stream, world, rank, min(args.steps, 100), args.warmup, args.prompt)
+
     if rank == 0:
         clk = clocks.summary()
         wbytes = weight_bytes_per_token(cfg)
@@ -740,6 +829,7 @@ def run_ours(args):
             "smollm_q8_bs1_decode_tok_s": round(smol_tps, 1),
             "prefill_tok_s": round(args.prompt / (prefill_ms / 1000.0), 1),
             "op_sweep": sweeps,
+            "tp_decode_bs1": tp_res,
             "gpu_launches": int(launches_timed),
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -756,6 +846,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel decode leg (N > 1)")
     ap.add_argument("--no-sweeps", action="store_true", help="skip the op-sweep GEMV/GEMM legs (config 2)")
     ap.add_argument("--no-serving", action="store_true", help="skip the 256-sequence serving run (config 5)")
     ap.add_argument("--attn-only", action="store_true", help="time the config-4 decode attention cases and exit")

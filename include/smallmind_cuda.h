@@ -211,6 +211,27 @@ SM_API int sm_model_destroy(sm_model* m);
 /* Device bytes held by the model's own buffers (embedding, norms, tables, workspace). */
 SM_API int sm_model_nbytes(const sm_model* m, size_t* out);
 
+/* ---- tensor-parallel decode (one process per GPU, NCCL loaded at run time) ----
+ * The reference runs one CPU process; these entry points split one model over a
+ * group of GPUs.  Each rank builds an ordinary model from its weight shards: the
+ * column-split projections keep its q / kv heads and its FFN units (the rows of
+ * Wq / Wk / Wv, MultiHeadAttention.cs:92-93 _qkv, and of gate / up,
+ * GatedMLP.cs:38-40), the row-split ones keep the matching input columns (Wo,
+ * MultiHeadAttention.cs:92-93 _proj; down, GatedMLP.cs:38-40) in whole 256-weight
+ * blocks; embedding, norms and LM head are replicated.  After the O and down
+ * projections every rank sums the partial outputs with one all-reduce before the
+ * residual add (TransformerBlock.cs:170, :184), so all ranks hold the same
+ * residual stream and produce the same logits. */
+/* Writes the group's 128-byte id (rank 0 makes it; every rank passes the same bytes). */
+SM_API int sm_tp_unique_id(void* id, size_t n);
+/* Joins ctx to the group as rank tp_rank of tp_size (blocking until all ranks join). */
+SM_API int sm_tp_init(sm_ctx* ctx, int tp_size, int tp_rank, const void* id, size_t n);
+/* In-place sum of n floats (device pointer) over the group, on the context stream. */
+SM_API int sm_tp_allreduce(sm_ctx* ctx, float* buf, size_t n);
+/* Marks m as this rank's shard of a tensor-parallel model (enable = 1) or not (0).
+ * SM_ERR_STATE if ctx has no group. */
+SM_API int sm_model_set_tp(sm_model* m, int enable);
+
 /* HBM KV cache for up to max_seqs sequences of max_tokens positions each
  * (replaces the per-layer caches of MultiHeadAttention.cs:252-274 and the session
  * store semantics of KvCacheEntry.cs:42-43).  fp32, [layer][seq][kv_head][pos][hd]. */

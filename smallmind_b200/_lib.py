@@ -74,6 +74,10 @@ SIGNATURES = {
     "sm_model_finalize": (i, [vp]),
     "sm_model_destroy": (i, [vp]),
     "sm_model_nbytes": (i, [vp, C.POINTER(C.c_size_t)]),
+    "sm_tp_unique_id": (i, [vp, sz]),
+    "sm_tp_init": (i, [vp, i, i, vp, sz]),
+    "sm_tp_allreduce": (i, [vp, vp, sz]),
+    "sm_model_set_tp": (i, [vp, i]),
     "sm_kv_create": (i, [vp, i, i, PP]),
     "sm_kv_destroy": (i, [vp]),
     "sm_kv_reset": (i, [vp, i]),

@@ -29,6 +29,8 @@ struct sm_ctx {
   bool own_stream = false;
   int64_t launches = 0;
   int* dev_status = nullptr;  // device-side status word (bounded waits, range checks)
+  void* tp_comm = nullptr;    // tensor-parallel group (NCCL communicator), sm_tp_init
+  int tp_size = 1, tp_rank = 0;
 };
 
 struct sm_weight {
@@ -282,6 +284,7 @@ SM_API int sm_ctx_destroy(sm_ctx* ctx) {
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->dev_status) cudaFree(ctx->dev_status);
+  if (ctx->tp_comm) tp_comm_destroy(ctx->tp_comm);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return SM_OK;
@@ -605,6 +608,7 @@ struct sm_model {
   float* sin_t = nullptr;
   float* cos_t = nullptr;
   bool finalized = false;
+  bool tp = false;  // a tensor-parallel shard: O / down outputs are all-reduced over ctx->tp_comm
   Work work;
   size_t own_bytes = 0;
   int qd() const { return cfg.n_heads * cfg.head_dim; }
@@ -722,6 +726,16 @@ bool m1_supported(const sm_model* m) {
   return gemv1_supports(*m->output, c.hidden);
 }
 
+// Tensor-parallel shard: the partial output of a row-split projection (rows x H in
+// `partial`) is summed over the group in place, then added to the residual stream.
+int tp_reduce_residual(sm_model* m, float* partial, int rows, int& nl) {
+  const size_t n = (size_t)rows * m->cfg.hidden;
+  SM_TRY(tp_allreduce_sum(m->ctx->tp_comm, partial, n, m->ctx->stream));
+  SM_TRY(launch_add(m->work.x, partial, (int64_t)n, m->ctx->stream));
+  nl += 2;
+  return SM_OK;
+}
+
 int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
   const auto& c = m->cfg;
   Work& w = m->work;
@@ -764,8 +778,9 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       GemvArgs o;
       o.K = qd;
       o.x = w.att;
-      SM_TRY(gemv1_segment(o, *L.w[SM_ROLE_WO], nullptr, w.x, GEMV_ADD));
+      SM_TRY(gemv1_segment(o, *L.w[SM_ROLE_WO], nullptr, m->tp ? w.h : w.x, m->tp ? GEMV_STORE : GEMV_ADD));
       SM_TRY(launch_m1(o, m, st, nl));
+      if (m->tp) SM_TRY(tp_reduce_residual(m, w.h, 1, nl));
       GemvArgs gu;
       gu.K = H;
       gu.x = w.x;
@@ -784,8 +799,9 @@ int forward_m1(sm_model* m, sm_kv* kv, bool prefill_head_only, int& nl) {
       GemvArgs dn;
       dn.K = c.ffn_hidden;
       dn.x = w.g;
-      SM_TRY(gemv1_segment(dn, *L.w[SM_ROLE_W_DOWN], nullptr, w.x, GEMV_ADD));
+      SM_TRY(gemv1_segment(dn, *L.w[SM_ROLE_W_DOWN], nullptr, m->tp ? w.h : w.x, m->tp ? GEMV_STORE : GEMV_ADD));
       SM_TRY(launch_m1(dn, m, st, nl));
+      if (m->tp) SM_TRY(tp_reduce_residual(m, w.h, 1, nl));
     }
   }
   return SM_OK;
@@ -877,8 +893,14 @@ int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs,
                                       w.attn_scratch_floats, st, &nl);
       SM_TRY(arc);
     }
-    // o-proj with the residual add fused in its epilogue (TransformerBlock.cs:170)
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.x, rows, H, 1, st, &nl));
+    // o-proj with the residual add fused in its epilogue (TransformerBlock.cs:170); a
+    // tensor-parallel shard all-reduces its partial output first
+    if (m->tp) {
+      SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.h, rows, H, 0, st, &nl));
+      SM_TRY(tp_reduce_residual(m, w.h, rows, nl));
+    } else {
+      SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.x, rows, H, 1, st, &nl));
+    }
     SM_TRY(launch_rmsnorm(w.x, L.ffn_norm, w.h, rows, H, c.norm_eps, st));
     ++nl;
     {
@@ -889,7 +911,12 @@ int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs,
     }
     SM_TRY(launch_silu_mul(w.g, w.u, w.g, (int64_t)rows * F, st));
     ++nl;
-    SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.x, rows, H, 1, st, &nl));  // + residual (:184)
+    if (m->tp) {
+      SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.h, rows, H, 0, st, &nl));
+      SM_TRY(tp_reduce_residual(m, w.h, rows, nl));
+    } else {
+      SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.x, rows, H, 1, st, &nl));  // + residual (:184)
+    }
   }
   // final norm + LM head: each prompt's last row only for prefill (what the loop reads), every
   // row for decode
@@ -931,6 +958,7 @@ MegaSeg mega_seg(const DevWeight& w, const DevWeight* w2, int mode, float* y) {
 bool mega_enabled(sm_model* m) {
   const char* e = std::getenv("SMALLMIND_MEGA");
   if (e && e[0] == '0') return false;
+  if (m->tp) return false;  // the all-reduce between layers runs as NCCL calls
   if (!m1_supported(m)) return false;
   for (const auto& L : m->layers)
     if (L.w[SM_ROLE_W_GATE]->scheme != L.w[SM_ROLE_W_UP]->scheme) return false;
@@ -1137,6 +1165,38 @@ SM_API int sm_model_set_vector(sm_model* m, int layer, int role, const float* da
   }
   SM_CUDA_TRY(cudaMemcpy(*dst, data, need * 4, cudaMemcpyHostToDevice));
   m->finalized = false;
+  return SM_OK;
+}
+
+SM_API int sm_tp_unique_id(void* id, size_t n) { return tp_unique_id(id, n); }
+
+SM_API int sm_tp_init(sm_ctx* ctx, int tp_size, int tp_rank, const void* id, size_t n) {
+  if (!ctx) return fail(SM_ERR_INVALID_ARG, "tp_init: null ctx");
+  if (ctx->tp_comm) return fail(SM_ERR_STATE, "tp_init: the context already belongs to a group");
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail(SM_ERR_INVALID_ARG, "tp_init: rank outside [0, size)");
+  DeviceGuard g(ctx->device);
+  void* comm = nullptr;
+  SM_TRY(tp_comm_create(tp_size, tp_rank, id, n, &comm));
+  ctx->tp_comm = comm;
+  ctx->tp_size = tp_size;
+  ctx->tp_rank = tp_rank;
+  return SM_OK;
+}
+
+SM_API int sm_tp_allreduce(sm_ctx* ctx, float* buf, size_t n) {
+  if (!ctx || !buf) return fail(SM_ERR_INVALID_ARG, "tp_allreduce: null argument");
+  if (!ctx->tp_comm) return fail(SM_ERR_STATE, "tp_allreduce: the context has no group (sm_tp_init)");
+  DeviceGuard g(ctx->device);
+  SM_TRY(tp_allreduce_sum(ctx->tp_comm, buf, n, ctx->stream));
+  ctx->launches += 1;
+  return SM_OK;
+}
+
+SM_API int sm_model_set_tp(sm_model* m, int enable) {
+  if (!m) return fail(SM_ERR_INVALID_ARG, "model_set_tp: null model");
+  if (enable && !m->ctx->tp_comm) return fail(SM_ERR_STATE, "model_set_tp: the context has no group (sm_tp_init)");
+  m->tp = enable != 0;
+  m->work.generation += 1000000;  // captured steps of the other mode are rebuilt
   return SM_OK;
 }
 

@@ -158,6 +158,12 @@ int launch_rope_rows(float* x, int rows, int row_stride, int n_heads, int hd, co
                      const float* sin_t, const float* cos_t, cudaStream_t st);
 int launch_silu_mul(const float* g, const float* u, float* out, int64_t n, cudaStream_t st);
 int launch_embed(const float* table, const int* tokens, float* x, int n, int H, cudaStream_t st);
+// Tensor-parallel group (tp.cu): NCCL loaded at run time
+int tp_unique_id(void* out, size_t n);
+int tp_comm_create(int size, int rank, const void* id, size_t n, void** comm);
+void tp_comm_destroy(void* comm);
+int tp_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st);
+int launch_add(float* x, const float* p, int64_t n, cudaStream_t st);
 int launch_argmax(const float* logits, int rows, int V, int* out, cudaStream_t st);
 // attention.cu  (K/V element d of key j, kv head g: base + j*row_stride + g*head_stride + d)
 // causal GQA prefill attention on tcgen05 (hd 64); SM_ERR_UNSUPPORTED when the shape is not handled
