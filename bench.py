@@ -794,7 +794,11 @@ def run_ours(args):
 
     tp_res = None
     if world > 1 and not args.no_tp:
-        tp_res = time_tp_decode(sm, ctx, torch, stream, world, rank, min(args.steps, 100), args.warmup, args.prompt)
+        try:
+            tp_res = time_tp_decode(sm, ctx, torch, stream, world, rank, min(args.steps, 100), args.warmup,
+                                    args.prompt)
+        except Exception as e:  # the replica line above stands on its own
+            tp_res = {"tp": world, "error": repr(e)[:300]}
 
     if rank == 0:
         clk = clocks.summary()

@@ -14,61 +14,17 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-CFG = dict(vocab_size=640, hidden=512, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=64, ffn_hidden=1536,
-           max_context=96, norm_eps=1e-5, rope_theta=10000.0)
-STEPS = 5
-
-
-def _schemes(O):
-    return dict(wq=O.Q4_K, wk=O.Q4_K, wv=O.Q6_K, wo=O.Q4_K, w_gate=O.Q4_K, w_up=O.Q4_K, w_down=O.Q6_K,
-                output=O.Q6_K)
-
-
-def _rank(rank, world, port, out_dir, mega):
-    import sys
-    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), SMALLMIND_MEGA=mega)
-    import torch
-    import torch.distributed as dist
-    torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
-    import smallmind_b200 as sm
-    from smallmind_b200 import tp
-    from oracle import oracle as O
-    host = O.make_model(CFG, _schemes(O), seed=17)
-    ctx = sm.CudaContext(rank)
-    group = tp.TensorParallelGroup(ctx, world, rank)
-    model = sm.CudaModel.from_host(ctx, tp.shard_model(host, world, rank))
-    group.shard(model)
-    kv = sm.KVCache(model, 1, 64)
-    prompt = np.random.RandomState(3).randint(0, CFG["vocab_size"], 21).astype(np.int32)
-    tok, lg = kv.prefill(0, prompt)
-    toks, logits = [tok], [lg]
-    for _ in range(STEPS):
-        t, l2 = kv.decode([0], [toks[-1]])
-        toks.append(int(t[0]))
-        logits.append(l2[0])
-    np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks))
-    if rank == 0:
-        np.save(os.path.join(out_dir, "logits.npy"), np.stack(logits))
-        # the unsharded model on this GPU, fed the same tokens
-        ref_model = sm.CudaModel.from_host(ctx, host)
-        rkv = sm.KVCache(ref_model, 1, 64)
-        _, r0 = rkv.prefill(0, prompt)
-        ref = [r0]
-        for t in toks[:-1]:
-            _, r = rkv.decode([0], [t])
-            ref.append(r[0])
-        np.save(os.path.join(out_dir, "ref.npy"), np.stack(ref))
-    dist.barrier()
-    dist.destroy_process_group()
+HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mega", ["1", "0"])
 def test_tp_decode_matches_single_gpu(tmp_path, world, mega):
+    """Ranks run tests/tp_rank_main.py under torch.distributed.run (bounded: 300 s)."""
+    import subprocess
+    import sys
+
     import torch
-    import torch.multiprocessing as mp
 
     from conftest import cosine
     if torch.cuda.device_count() < world:
@@ -77,11 +33,16 @@ def test_tp_decode_matches_single_gpu(tmp_path, world, mega):
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    mp.spawn(_rank, args=(world, port, str(tmp_path), mega), nprocs=world, join=True)
+    env = dict(os.environ, SMALLMIND_MEGA=mega)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", f"--master-port={port}", os.path.join(HERE, "tp_rank_main.py"),
+           str(tmp_path)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, (r.stdout[-3000:], r.stderr[-3000:])
     logits, ref = np.load(tmp_path / "logits.npy"), np.load(tmp_path / "ref.npy")
-    toks = [np.load(tmp_path / f"tok{r}.npy") for r in range(world)]
-    for r in range(1, world):
-        assert np.array_equal(toks[r], toks[0])
+    toks = [np.load(tmp_path / f"tok{r_}.npy") for r_ in range(world)]
+    for r_ in range(1, world):
+        assert np.array_equal(toks[r_], toks[0])
     for step in range(len(ref)):
         assert cosine(logits[step], ref[step]) >= 0.9999, step
         assert int(np.argmax(logits[step])) == int(np.argmax(ref[step])) == int(toks[0][step])
