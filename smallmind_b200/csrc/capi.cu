@@ -838,6 +838,25 @@ int matmul_multi(const DevWeight* const* ws, float* const* ys, const int* ld, in
   return SM_OK;
 }
 
+// As matmul_multi, with x first passed through a prologue (RMSNorm or the SiLU gate,
+// XPro).  On the tensor-core GEMM the prologue runs inside its x-split pass; other
+// paths apply it into `tmp` (rows x K) and read that.
+int matmul_multi_pro(const DevWeight* const* ws, float* const* ys, const int* ld, int nw, const float* x, int rows,
+                     const XPro& pro, float* tmp, int accumulate, cudaStream_t st, int& nl) {
+  const char* et = std::getenv("SMALLMIND_GEMM_TC");
+  if (!(et && et[0] == '0') && gemm_tc_supports_multi(ws, nw, rows))
+    return launch_gemm_tc_multi(ws, ys, ld, nw, x, rows, accumulate, nullptr, st, &nl, &pro);
+  const int K = ws[0]->K();
+  if (pro.kind == XPRO_RMSNORM) {
+    SM_TRY(launch_rmsnorm(x, pro.gamma, tmp, rows, K, pro.eps, st));
+  } else {
+    SM_TRY(launch_silu_mul(x, pro.u, tmp, (int64_t)rows * K, st));
+  }
+  ++nl;
+  for (int i = 0; i < nw; ++i) SM_TRY(launch_matmul(*ws[i], tmp, ys[i], rows, ld[i], accumulate, st, &nl));
+  return SM_OK;
+}
+
 // One prompt of a prefill: its rows [r0, r0 + T) of the step, its slot and its first position.
 struct PrefillSeg {
   int seq, pos0, r0, T;
@@ -865,14 +884,16 @@ int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs,
     const sm_model::Layer& L = m->layers[l];
     float* kc = kv->k + kv->layer_stride() * l;
     float* vc = kv->v + kv->layer_stride() * l;
-    SM_TRY(launch_rmsnorm(w.x, L.attn_norm, w.h, rows, H, c.norm_eps, st));
-    ++nl;
-    // merged [Q | K | V] rows (MultiHeadAttention.cs:213, layout :395-462)
+    // RMSNorm, then the merged [Q | K | V] rows (MultiHeadAttention.cs:213, layout :395-462)
     {
       const DevWeight* ws[3] = {L.w[SM_ROLE_WQ], L.w[SM_ROLE_WK], L.w[SM_ROLE_WV]};
       float* ys[3] = {w.qkv, w.qkv + qd, w.qkv + qd + kd};
       const int ld[3] = {QS, QS, QS};
-      SM_TRY(matmul_multi(ws, ys, ld, 3, w.h, rows, st, nl));
+      XPro pro;
+      pro.kind = XPRO_RMSNORM;
+      pro.gamma = L.attn_norm;
+      pro.eps = c.norm_eps;
+      SM_TRY(matmul_multi_pro(ws, ys, ld, 3, w.x, rows, pro, w.h, 0, st, nl));
     }
     SM_TRY(launch_rope_qk_append(w.qkv, rows, QS, c.n_heads, c.n_kv_heads, hd, w.pos(), w.seq(), m->sin_t, m->cos_t,
                                  kc, vc, mt, st));
@@ -901,21 +922,27 @@ int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs,
     } else {
       SM_TRY(launch_matmul(*L.w[SM_ROLE_WO], w.att, w.x, rows, H, 1, st, &nl));
     }
-    SM_TRY(launch_rmsnorm(w.x, L.ffn_norm, w.h, rows, H, c.norm_eps, st));
-    ++nl;
     {
       const DevWeight* ws[2] = {L.w[SM_ROLE_W_GATE], L.w[SM_ROLE_W_UP]};
       float* ys[2] = {w.g, w.u};
       const int ld[2] = {F, F};
-      SM_TRY(matmul_multi(ws, ys, ld, 2, w.h, rows, st, nl));
+      XPro pro;
+      pro.kind = XPRO_RMSNORM;
+      pro.gamma = L.ffn_norm;
+      pro.eps = c.norm_eps;
+      SM_TRY(matmul_multi_pro(ws, ys, ld, 2, w.x, rows, pro, w.h, 0, st, nl));
     }
-    SM_TRY(launch_silu_mul(w.g, w.u, w.g, (int64_t)rows * F, st));
-    ++nl;
-    if (m->tp) {
-      SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.h, rows, H, 0, st, &nl));
-      SM_TRY(tp_reduce_residual(m, w.h, rows, nl));
-    } else {
-      SM_TRY(launch_matmul(*L.w[SM_ROLE_W_DOWN], w.g, w.x, rows, H, 1, st, &nl));  // + residual (:184)
+    {
+      // down(silu(gate) * up) (GatedMLP.cs:51-93), + residual (TransformerBlock.cs:184); a
+      // tensor-parallel shard all-reduces its partial output first
+      const DevWeight* ws[1] = {L.w[SM_ROLE_W_DOWN]};
+      float* ys[1] = {m->tp ? w.h : w.x};
+      const int ld[1] = {H};
+      XPro pro;
+      pro.kind = XPRO_SILU;
+      pro.u = w.u;
+      SM_TRY(matmul_multi_pro(ws, ys, ld, 1, w.g, rows, pro, w.g, m->tp ? 0 : 1, st, nl));
+      if (m->tp) SM_TRY(tp_reduce_residual(m, w.h, rows, nl));
     }
   }
   // final norm + LM head: each prompt's last row only for prefill (what the loop reads), every
@@ -930,8 +957,18 @@ int forward(sm_model* m, sm_kv* kv, int rows, const PrefillSeg* segs, int nsegs,
       ++nl;
     }
   } else {
-    SM_TRY(launch_rmsnorm(w.x, m->out_norm, w.h, nrows, H, c.norm_eps, st));
+    // decode rows: the final RMSNorm runs in the head GEMM's x-split pass when it takes the rows
+    const DevWeight* ws[1] = {m->output};
+    float* ys[1] = {w.logits};
+    const int ld[1] = {c.vocab_size};
+    XPro pro;
+    pro.kind = XPRO_RMSNORM;
+    pro.gamma = m->out_norm;
+    pro.eps = c.norm_eps;
+    SM_TRY(matmul_multi_pro(ws, ys, ld, 1, w.x, nrows, pro, w.h, 0, st, nl));
+    SM_TRY(launch_argmax(w.logits, nrows, c.vocab_size, w.amax(), st));
     ++nl;
+    return SM_OK;
   }
   SM_TRY(launch_matmul(*m->output, w.h, w.logits, nrows, c.vocab_size, 0, st, &nl));
   SM_TRY(launch_argmax(w.logits, nrows, c.vocab_size, w.amax(), st));

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemv1.cuh"
 #include "mbar.cuh"
 
 namespace sm {
@@ -576,6 +577,62 @@ __global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint
   }
 }
 
+// One row of x per block: the prologue (RMSNorm over the row, or the SiLU gate)
+// and the fp16 hi / lo split, with the element arithmetic of rmsnorm_kernel /
+// silu_mul_kernel (ops.cu) so the planes hold the values those kernels produce.
+__global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int K, const XPro pro,
+                                                        uint2* __restrict__ hi, uint2* __restrict__ lo) {
+  const int row = blockIdx.x;
+  const float* xr = x + (int64_t)row * K;
+  float inv = 1.f;
+  if (pro.kind == XPRO_RMSNORM) {
+    float s = 0.f;
+    for (int f = threadIdx.x; f < K; f += blockDim.x) s = fmaf(xr[f], xr[f], s);
+    __shared__ float red[32];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), pro.eps)));
+  }
+  const float* ur = pro.u ? pro.u + (int64_t)row * K : nullptr;
+  for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
+    const float4 v = ((const float4*)xr)[q];
+    float f[4] = {v.x, v.y, v.z, v.w};
+    if (pro.kind == XPRO_RMSNORM) {
+      const float4 g = ((const float4*)pro.gamma)[q];
+      const float gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = __fmul_rn(gv[e], __fmul_rn(f[e], inv));
+    } else if (pro.kind == XPRO_SILU) {
+      const float4 uu = ((const float4*)ur)[q];
+      const float uv[4] = {uu.x, uu.y, uu.z, uu.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float c = fmaxf(-20.f, fminf(f[e], 20.f));
+        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));
+        f[e] = __fmul_rn(__fmul_rn(f[e], sig), uv[e]);
+      }
+    }
+    uint32_t hp[2] = {0, 0}, lp[2] = {0, 0};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __half h = __float2half_rn(f[e]);
+      const __half l = __float2half_rn(__fsub_rn(f[e], __half2float(h)));
+      hp[e >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (e & 1));
+      lp[e >> 1] |= (uint32_t)__half_as_ushort(l) << (16 * (e & 1));
+    }
+    const int64_t o = (int64_t)row * (K / 4) + q;
+    hi[o] = make_uint2(hp[0], hp[1]);
+    lo[o] = make_uint2(lp[0], lp[1]);
+  }
+}
+
 // W -> fp16 hi / lo planes [N][K] (one thread per 32-weight unit), for GEMMs
 // with enough x rows that dequantizing each weight once up front is cheaper than
 // once per 128-row tile of x.
@@ -761,7 +818,7 @@ bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M) {
 }
 
 int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
-                         int accumulate, int* status, cudaStream_t st, int* n_launch) {
+                         int accumulate, int* status, cudaStream_t st, int* n_launch, const XPro* pro) {
   if (!gemm_tc_supports_multi(Ws, nw, M)) return SM_ERR_UNSUPPORTED;
   const int K = Ws[0]->K();
   int N = 0;
@@ -793,9 +850,13 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
   __half* wlo = resident ? rlo : whi + nw_el;
   int rc = SM_OK;
   {
-    const int64_t n4 = n / 4;
-    const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
-    gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
+    if (pro && pro->kind != XPRO_NONE) {
+      gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, *pro, (uint2*)hi, (uint2*)lo);
+    } else {
+      const int64_t n4 = n / 4;
+      const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
+      gemm_split_kernel<<<blocks, 256, 0, st>>>((const float4*)x, n4, (uint2*)hi, (uint2*)lo);
+    }
     if (n_launch) ++*n_launch;
     if (wt && !resident) {
       int64_t row0 = 0;

@@ -52,8 +52,19 @@ bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M);
 // Drops the resident fp16 planes of every weight group that contains this weight
 // (called before the weight's memory is freed).
 void gemm_tc_release_weight(const void* data);
+// What the GEMM's x-split pass applies to x first (the producer of the fp16 planes):
+// nothing, RMSNorm (RMSNormOps.cs:28-220, gamma / eps) or the SiLU gate
+// silu(x) * u (ActivationOps.cs:565-580), so the block's norm / activation
+// kernels and their fp32 round trip are not needed.
+enum { XPRO_NONE = 0, XPRO_RMSNORM = 1, XPRO_SILU = 2 };
+struct XPro {
+  int kind = XPRO_NONE;
+  const float* gamma = nullptr;
+  float eps = 0.f;
+  const float* u = nullptr;  // SILU: the up rows (same shape as x)
+};
 int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
-                         int accumulate, int* status, cudaStream_t st, int* n_launch);
+                         int accumulate, int* status, cudaStream_t st, int* n_launch, const XPro* pro = nullptr);
 // Q4_K (INTENDED) y[m] (+)= W x[m] for M rows of x (stride K), y rows of stride ldy
 int launch_gemv_mma_q4k_rows(const DevWeight& W, const float* x, int M, float* y, int ldy, int accumulate,
                              int* status, cudaStream_t st, int* n_launch);
