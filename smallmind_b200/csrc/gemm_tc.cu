@@ -790,7 +790,7 @@ void gemm_tc_release_weight(const void* data) {
 }
 
 bool gemm_tc_supports(const DevWeight& W, int M) {
-  if (W.layout != SM_LAYOUT_INTENDED || M < 16) return false;
+  if (W.layout != SM_LAYOUT_INTENDED || M < 5) return false;
   const int K = W.K();
   if (K % BK) return false;
   switch (W.scheme) {

@@ -368,19 +368,20 @@ int launch_matmul(const DevWeight& W, const float* x, float* y, int M, int ldy, 
     return launch_gemv1(a, st, n_launch);
   }
   {
-    // 2 <= M <= 15, Q4_K / Q6_K: the integer tensor-core GEMV over up to four x rows per pass
+    // 2 <= M <= 4, Q4_K / Q6_K: the integer tensor-core GEMV, all x rows in one pass over the
+    // packed weights (more rows would take several passes: the tcgen05 GEMM is faster there)
     const char* em = std::getenv("SMALLMIND_GEMV_MMA");
-    if (!(em && em[0] == '0') && W.scheme == SM_Q4_K && M > 1 && M < 16) {
+    if (!(em && em[0] == '0') && W.scheme == SM_Q4_K && M > 1 && M <= 4) {
       const int rc = launch_gemv_mma_q4k_rows(W, x, M, y, ldy, accumulate, nullptr, st, n_launch);
       if (rc != SM_ERR_UNSUPPORTED) return rc;
     }
-    if (!(em && em[0] == '0') && W.scheme == SM_Q6_K && M > 1 && M < 16) {
+    if (!(em && em[0] == '0') && W.scheme == SM_Q6_K && M > 1 && M <= 4) {
       const int rc = launch_gemv_mma_q6k_rows(W, x, M, y, ldy, accumulate, nullptr, st, n_launch);
       if (rc != SM_ERR_UNSUPPORTED) return rc;
     }
   }
   {
-    // M >= 16: tcgen05 GEMM (SMALLMIND_GEMM_TC=0 selects the CUDA-core row kernel)
+    // M >= 5: tcgen05 GEMM (SMALLMIND_GEMM_TC=0 selects the CUDA-core row kernel)
     const char* et = std::getenv("SMALLMIND_GEMM_TC");
     if (!(et && et[0] == '0') && gemm_tc_supports(W, M)) {
       const int rc = launch_gemm_tc(W, x, y, M, ldy, accumulate, nullptr, st, n_launch);

@@ -42,7 +42,7 @@ bool gemv1_supports(const DevWeight& w, int K);
 bool gemv1_mix_ok(int fa, int fb);
 int gemv1_segment(GemvArgs& a, const DevWeight& w, const DevWeight* w2, float* y, int mode);
 int launch_gemv1(const GemvArgs& a, cudaStream_t st, int* n_launch);
-// y[M][N] (+)= x[M][K] W^T on tcgen05 (INTENDED layout, M >= 16, K % 64 == 0)
+// y[M][N] (+)= x[M][K] W^T on tcgen05 (INTENDED layout, M >= 5, K % 64 == 0)
 bool gemm_tc_supports(const DevWeight& W, int M);
 int launch_gemm_tc(const DevWeight& W, const float* x, float* y, int M, int ldy, int accumulate, int* status,
                    cudaStream_t st, int* n_launch);
