@@ -39,7 +39,6 @@ namespace {
 constexpr int BM = 128;  // x rows per tile (MMA M)
 constexpr int BN = 128;  // weight rows per tile (MMA N)
 constexpr int BK = 64;   // k per stage: one 128-byte swizzle atom of fp16
-constexpr int STAGES = 3;
 // warp roles: WT = false (weights dequantized in the kernel): warps 0..7 load
 // weight tiles, 8 = TMA, 9 = MMA; WT = true (weights pre-split into fp16
 // planes and loaded by TMA): 4 = TMA, 5 = MMA.  Warps 0..3 run the epilogue.
@@ -50,10 +49,19 @@ struct Roles {
   static constexpr int THREADS = (TMA_WARP + 2) * 32;
 };
 constexpr int TILE_A = BM * BK * 2;  // bytes of one fp16 plane of the x tile
-constexpr int TILE_W = BN * BK * 2;
-constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
-constexpr int TMEM_COLS = BN;  // fp32 accumulator: 128 lanes x BN columns
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+// Tile geometry per weight-tile width NB (the MMA N): 128, or 256 for GEMMs with
+// several x-row tiles whose weights come as resident planes.  A 256-wide tile reads
+// A and B from shared memory once per twice the MACs of a 128-wide one; it leaves
+// room for 2 stages instead of 3.
+template <int NB>
+struct Geo {
+  static constexpr int TILE_W = NB * BK * 2;
+  static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_W;
+  static constexpr int STAGES = NB == 256 ? 2 : 3;
+  static constexpr int TMEM_COLS = NB;  // fp32 accumulator: 128 lanes x NB columns
+  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+};
+constexpr size_t SMEM_BYTES = Geo<BN>::SMEM_BYTES;
 
 constexpr int MAX_SEG = 3;
 
@@ -85,13 +93,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 
 // kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both
 // K-major, N = BN, M = BM.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+template <int NB>
+constexpr uint32_t idesc() { return (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(BM >> 4) << 24); }
 
+template <int NB = BN>
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(IDESC), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc<NB>()), "r"(acc)
       : "memory");
 }
 
@@ -357,13 +367,18 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
-template <bool WT>
+template <bool WT, int NB = BN>
 __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
                    const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo,
                    const __grid_constant__ TcArgs a) {
   constexpr int LOADER_WARPS = Roles<WT>::LOADER_WARPS;
   constexpr int TMA_WARP = Roles<WT>::TMA_WARP;
+  static_assert(WT || NB == BN, "the loader warps fill 128-row weight tiles");
+  constexpr int STAGES = Geo<NB>::STAGES;
+  constexpr int STAGE_BYTES = Geo<NB>::STAGE_BYTES;
+  constexpr int TILE_W = Geo<NB>::TILE_W;
+  constexpr int TMEM_COLS = Geo<NB>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full_a = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -374,7 +389,7 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // x-row tiles vary fastest: consecutive CTAs share one weight tile, which then
   // comes from L2 for all the row tiles instead of from DRAM once per row tile
-  const int n0 = blockIdx.y * BN, m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * NB, m0 = blockIdx.x * BM;
   const int K = a.K;
   const int nk_all = K / BK;
   const int kt0 = (int)((int64_t)nk_all * blockIdx.z / a.kslices);
@@ -483,9 +498,9 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
 #pragma unroll
         for (int ks = 0; ks < BK / 16; ++ks) {
           const uint64_t adv = (uint64_t)((ks * 32) >> 4);  // 16 fp16 = 32 bytes along k
-          mma_f16(tmem, dah + adv, dwh + adv, (kt | ks) != 0);
-          mma_f16(tmem, dah + adv, dwl + adv, 1);
-          mma_f16(tmem, dal + adv, dwh + adv, 1);
+          mma_f16<NB>(tmem, dah + adv, dwh + adv, (kt | ks) != 0);
+          mma_f16<NB>(tmem, dah + adv, dwl + adv, 1);
+          mma_f16<NB>(tmem, dal + adv, dwh + adv, 1);
         }
         mma_commit(&empty[s]);  // stage s may be refilled once these MMAs have read it
       }
@@ -508,10 +523,10 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
       // 512-byte output row: lane = 4 consecutive columns, not lane = row.
       // Row stride 132 floats: the 8 rows of a quarter-warp's 16-byte writes
       // land in distinct bank groups.
-      constexpr int SR = BN + 4;
+      constexpr int SR = NB + 4;
       float* stile = (float*)smem + warp * 32 * SR;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 0; c0 < NB; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
         float4* d = (float4*)(stile + lane * SR + c0);
@@ -522,7 +537,9 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
       }
       __syncwarp();
       const bool rmw = a.accumulate && !part;
-      const int nc = n0 + 4 * lane;  // this lane's 4 columns
+#pragma unroll 1
+      for (int cb = 0; cb < NB; cb += 128) {
+      const int nc = n0 + cb + 4 * lane;  // this lane's 4 columns
       const bool full = nc + 3 < ne;
 #pragma unroll 1
       for (int rr = 0; rr < 32; ++rr) {
@@ -530,7 +547,7 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
         if (mr >= a.M) break;
         float* yrow = part ? a.partial + ((int64_t)blockIdx.z * a.M + mr) * a.N
                            : a.seg_y[sg] + (int64_t)mr * a.seg_ldy[sg] - nb;
-        float4 t = *(const float4*)(stile + rr * SR + 4 * lane);
+        float4 t = *(const float4*)(stile + rr * SR + cb + 4 * lane);
         float* dst = yrow + nc;
         if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
           if (rmw) {
@@ -547,6 +564,7 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
           for (int e = 0; e < 4; ++e)
             if (nc + e < ne) dst[e] = rmw ? dst[e] + tv[e] : tv[e];
         }
+      }
       }
     }
   }
@@ -686,10 +704,10 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-int make_plane_map(CUtensorMap* map, void* base, int M, int K) {
+int make_plane_map(CUtensorMap* map, void* base, int M, int K, int box_rows = BM) {
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   // the driver entry point is resolved at run time, so the library loads (and
   // its symbols can be checked) on machines without a CUDA driver
@@ -831,6 +849,8 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
         cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     SM_CUDA_TRY(
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<true, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Geo<256>::SMEM_BYTES));
     attr_set[dev] = true;
   }
   // More than one 128-row tile of x: the weights come as fp16 planes (resident, or split for this
@@ -872,8 +892,13 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
     CUtensorMap mh, ml, mwh, mwl;
     rc = make_plane_map(&mh, hi, M, K);
     if (rc == SM_OK) rc = make_plane_map(&ml, lo, M, K);
-    if (rc == SM_OK) rc = make_plane_map(&mwh, wt ? (void*)whi : (void*)hi, wt ? N : M, K);
-    if (rc == SM_OK) rc = make_plane_map(&mwl, wt ? (void*)wlo : (void*)lo, wt ? N : M, K);
+    // 256-wide weight tiles for GEMMs with several x-row tiles (prefill, large batches),
+    // when the stacked segments meet on 256-row boundaries
+    bool wide = wt && M > BM;
+    for (int i = 0; i + 1 < nw; ++i) wide = wide && Ws[i]->N() % 256 == 0;
+    const int nbw = wide ? 256 : BN;
+    if (rc == SM_OK) rc = make_plane_map(&mwh, wt ? (void*)whi : (void*)hi, wt ? N : M, K, nbw);
+    if (rc == SM_OK) rc = make_plane_map(&mwl, wt ? (void*)wlo : (void*)lo, wt ? N : M, K, nbw);
     if (rc == SM_OK) {
       TcArgs a;
       a.nseg = nw;
@@ -889,7 +914,7 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
       a.K = K;
       a.accumulate = accumulate;
       a.status = status;
-      const int gn = (N + BN - 1) / BN, gm = (M + BM - 1) / BM;
+      const int gn = (N + nbw - 1) / nbw, gm = (M + BM - 1) / BM;
       // split K when the output tiles alone cannot fill the SMs
       int sms = 148;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -909,7 +934,9 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
         a.partial = (float*)pbuf;
       }
       dim3 grid(gm, gn, S);
-      if (wt)
+      if (wt && wide)
+        gemm_tc_kernel<true, 256><<<grid, Roles<true>::THREADS, Geo<256>::SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
+      else if (wt)
         gemm_tc_kernel<true><<<grid, Roles<true>::THREADS, SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
       else
         gemm_tc_kernel<false><<<grid, Roles<false>::THREADS, SMEM_BYTES, st>>>(mh, ml, mwh, mwl, a);
