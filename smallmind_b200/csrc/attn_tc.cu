@@ -383,40 +383,39 @@ __global__ void __launch_bounds__(THREADS, 1)
 // q rows [T][q_stride] (head h at column h * 64) -> planes [nH][T][64];
 // k / v cache rows (kv head g at base + g * head_stride, position j at
 // + j * row_stride) -> k planes [nKv][S][64] and v^T planes [nKv][64][Sp].
-__global__ void attn_split_kernel(const float* __restrict__ q, int q_stride, const float* __restrict__ k,
-                                  const float* __restrict__ v, int64_t row_stride, int64_t head_stride, int T, int S,
-                                  int Sp, int nH, int nKv, __half* qh, __half* ql, __half* kh, __half* kl, __half* vh,
-                                  __half* vl) {
-  const int64_t nq = (int64_t)nH * T * HD, nk = (int64_t)nKv * S * HD, nv = (int64_t)nKv * HD * Sp;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nq + nk + nv;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float x;
-    __half *dh, *dl;
-    int64_t di;
-    if (i < nq) {
-      const int d = (int)(i % HD);
-      const int64_t ht = i / HD;
-      const int t = (int)(ht % T), h = (int)(ht / T);
-      x = q[(int64_t)t * q_stride + h * HD + d];
-      dh = qh, dl = ql, di = i;
-    } else if (i < nq + nk) {
-      const int64_t ii = i - nq;
-      const int d = (int)(ii % HD);
-      const int64_t gj = ii / HD;
-      const int j = (int)(gj % S), g = (int)(gj / S);
-      x = k[g * head_stride + j * row_stride + d];
-      dh = kh, dl = kl, di = ii;
-    } else {
-      const int64_t ii = i - nq - nk;  // [g][d][j]
-      const int j = (int)(ii % Sp);
-      const int64_t gd = ii / Sp;
-      const int d = (int)(gd % HD), g = (int)(gd / HD);
-      x = j < S ? v[g * head_stride + j * row_stride + d] : 0.f;
-      dh = vh, dl = vl, di = ii;
-    }
-    const __half hi = __float2half_rn(x);
-    dh[di] = hi;
-    dl[di] = __float2half_rn(x - __half2float(hi));
+// q, k and v^T -> fp16 hi / lo planes.  Block (x, y): 64 rows (tokens / keys) of
+// head y (q heads, then k heads, then v heads); v is transposed through shared
+// memory to [kv head][d][key] (keys padded to Sp with zeros).
+__device__ __forceinline__ void split_store(float x, __half* dh, __half* dl, int64_t di) {
+  const __half hi = __float2half_rn(x);
+  dh[di] = hi;
+  dl[di] = __float2half_rn(x - __half2float(hi));
+}
+
+__global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, int q_stride,
+                                                         const float* __restrict__ k, const float* __restrict__ v,
+                                                         int64_t row_stride, int64_t head_stride, int T, int S, int Sp,
+                                                         int nH, int nKv, __half* qh, __half* ql, __half* kh,
+                                                         __half* kl, __half* vh, __half* vl) {
+  const int y = blockIdx.y, r0 = blockIdx.x * 64, d = threadIdx.x & 63, rs = threadIdx.x >> 6;
+  if (y < nH) {
+    if (r0 >= T) return;
+    for (int r = r0 + rs; r < min(T, r0 + 64); r += 4)
+      split_store(q[(int64_t)r * q_stride + y * HD + d], qh, ql, ((int64_t)y * T + r) * HD + d);
+  } else if (y < nH + nKv) {
+    const int g = y - nH;
+    if (r0 >= S) return;
+    for (int r = r0 + rs; r < min(S, r0 + 64); r += 4)
+      split_store(k[g * head_stride + r * row_stride + d], kh, kl, ((int64_t)g * S + r) * HD + d);
+  } else {
+    const int g = y - nH - nKv;
+    if (r0 >= Sp) return;
+    __shared__ float tile[64][65];
+    for (int r = rs; r < 64; r += 4) tile[r][d] = r0 + r < S ? v[g * head_stride + (r0 + r) * row_stride + d] : 0.f;
+    __syncthreads();
+    // thread: key j = threadIdx & 63 (contiguous in the output), dims dd = rs, rs + 4, ...
+    for (int dd = rs; dd < HD; dd += 4)
+      split_store(tile[d][dd], vh, vl, ((int64_t)g * HD + dd) * Sp + r0 + d);
   }
 }
 
@@ -470,9 +469,9 @@ int launch_attention_prefill_tc(const float* q, int q_stride, const float* k, co
   __half* vl = vh + nv;
   int rc = SM_OK;
   {
-    const int64_t n = nq + nk + nv;
-    attn_split_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 32), 256, 0, st>>>(
-        q, q_stride, k, v, row_stride, head_stride, T, S, Sp, nH, nKv, qh, ql, kh, kl, vh, vl);
+    dim3 grid((std::max(T, Sp) + 63) / 64, nH + 2 * nKv);
+    attn_split_kernel<<<grid, 256, 0, st>>>(q, q_stride, k, v, row_stride, head_stride, T, S, Sp, nH, nKv, qh, ql,
+                                            kh, kl, vh, vl);
     if (n_launch) ++*n_launch;
     CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
     rc = make_map3(&mqh, qh, HD, T, nH, HD, QB);
