@@ -576,6 +576,236 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------- two-MMA Q4_K GEMM
+// y (+)= sum_b d[n][b] * sum_{k in b} (sc q)[n][k] x[m][k]   (the -dmin m term runs as
+// a separate small GEMM over per-32 sums of x, see launch_gemm_q4k2).  The weight
+// operand sc*q is an exact fp16 integer, so each 16-wide k step needs two MMAs
+// (x_hi and x_lo) instead of three; the block scale d varies every 256 k, so the
+// accumulator of each 256-weight block is read from TMEM (double-buffered: the MMAs
+// of block b + 1 run while block b is read) and added into registers times d.
+// Warps 0..3: epilogue (TMEM lanes = x rows), warp 4: TMA, warp 5: MMA issuer.
+namespace q2 {
+constexpr int THREADS = 192;
+constexpr int STAGES = 4;
+constexpr int TILE_Q = BN * BK * 2;
+constexpr int STAGE_BYTES = 2 * TILE_A + TILE_Q;
+constexpr int MAX_NB = 32;  // 256-weight blocks per k slice (K <= 8192)
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + (size_t)MAX_NB * BN * 4 + 1024 + 256;
+}  // namespace q2
+
+__global__ void __launch_bounds__(q2::THREADS, 1)
+    gemm_q4k2_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_xh,
+                     const __grid_constant__ CUtensorMap tm_xl, const __grid_constant__ CUtensorMap tm_mh,
+                     const __grid_constant__ CUtensorMap tm_ml, const float* __restrict__ dv, int Kp,
+                     const __grid_constant__ TcArgs a) {
+  using namespace q2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  float* dsm = (float*)(smem + STAGES * STAGE_BYTES);  // [block of the slice][128 columns]
+  uint64_t* full = (uint64_t*)(dsm + MAX_NB * BN);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* accm = acce + 2;  // the -dmin m accumulator is complete
+  uint32_t* tmem_slot = (uint32_t*)(accm + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.y * BN, m0 = blockIdx.x * BM;
+  const int K = a.K, NBall = K >> 8;
+  const int b0 = (int)((int64_t)NBall * blockIdx.z / a.kslices);
+  const int nbs = (int)((int64_t)NBall * (blockIdx.z + 1) / a.kslices) - b0;
+  const int nk = 4 * nbs;  // 64-wide k stages of the slice
+  // slice 0 also runs the -dmin m term: per 64 columns of the x sums, two stages
+  // (x sums hi + lo with -dmin m hi, then x sums hi with -dmin m lo) into TMEM
+  // columns 256..383
+  const bool mterm = blockIdx.z == 0;
+  const int nm = mterm ? 2 * (Kp / BK) : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    mbar_init(accm, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(4 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // this tile's block scales, staged once (columns past N read as 0)
+  for (int i = tid; i < nbs * BN; i += THREADS) {
+    const int bl = i / BN, c = i - bl * BN;
+    dsm[i] = n0 + c < a.N ? dv[(int64_t)(n0 + c) * NBall + b0 + bl] : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const int kg = (4 * b0 + kt) * BK;
+        mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
+        tma_load_2d(st, &tm_hi, kg, m0, &full[s]);
+        tma_load_2d(st + TILE_A, &tm_lo, kg, m0, &full[s]);
+        tma_load_2d(st + 2 * TILE_A, &tm_q, kg, n0, &full[s]);
+      }
+      for (int j = 0; j < nm; ++j) {
+        const int kt = nk + j, s = kt % STAGES;
+        if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const int kc = (j >> 1) * BK;
+        if ((j & 1) == 0) {
+          mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
+          tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
+          tma_load_2d(st + TILE_A, &tm_xl, kc, m0, &full[s]);
+          tma_load_2d(st + 2 * TILE_A, &tm_mh, kc, n0, &full[s]);
+        } else {
+          mbar_expect_tx(&full[s], TILE_A + TILE_Q);
+          tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
+          tma_load_2d(st + 2 * TILE_A, &tm_ml, kc, n0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int bl = 0; bl < nbs && ok; ++bl) {
+        const int b = bl & 1;
+        if (bl >= 2) ok = mbar_wait_bounded(&acce[b], ((bl >> 1) - 1) & 1, a.status);
+        tc_fence_after();
+        for (int s4 = 0; s4 < 4 && ok; ++s4) {
+          const int kt = 4 * bl + s4, s = kt % STAGES;
+          ok = mbar_wait_bounded(&full[s], (kt / STAGES) & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint64_t dah = sw128_desc(base), dal = sw128_desc(base + TILE_A), dq = sw128_desc(base + 2 * TILE_A);
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+            mma_f16(tmem + b * BN, dah + adv, dq + adv, (s4 | ks) != 0);
+            mma_f16(tmem + b * BN, dal + adv, dq + adv, 1);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&accf[b]);
+      }
+      for (int j = 0; j < nm && ok; ++j) {
+        const int kt = nk + j, s = kt % STAGES;
+        ok = mbar_wait_bounded(&full[s], (kt / STAGES) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint64_t dah = sw128_desc(base), dal = sw128_desc(base + TILE_A), dm = sw128_desc(base + 2 * TILE_A);
+#pragma unroll
+        for (int ks = 0; ks < BK / 16; ++ks) {
+          const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+          mma_f16(tmem + 2 * BN, dah + adv, dm + adv, (j | ks) != 0);
+          if ((j & 1) == 0) mma_f16(tmem + 2 * BN, dal + adv, dm + adv, 1);
+        }
+        mma_commit(&empty[s]);
+      }
+      if (ok && nm) mma_commit(accm);
+    }
+  } else {
+    // ---- epilogue warps 0..3: row m0 + 32 warp + lane, 128 columns in registers
+    float y[BN];
+#pragma unroll
+    for (int c = 0; c < BN; ++c) y[c] = 0.f;
+    bool ok = true;
+    for (int bl = 0; bl < nbs; ++bl) {
+      const int b = bl & 1;
+      ok = mbar_wait_bounded(&accf[b], (bl >> 1) & 1, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      const float* db = dsm + bl * BN;
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN + c0), v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) y[c0 + e] = fmaf(__uint_as_float(v[e]), db[c0 + e], y[c0 + e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
+    }
+    if (ok && nm) {
+      ok = mbar_wait_bounded(accm, 0, a.status);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(2 * BN + c0), v);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) y[c0 + e] += __uint_as_float(v[e]);
+        }
+      }
+    }
+    // every MMA has completed (the last block's accumulator was read), so the
+    // stage buffers are free: rows go through shared memory for whole-row stores
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+    if (ok) {
+      const bool part = a.kslices > 1;
+      int sg = 0;
+      while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
+      const int nb = a.seg_n0[sg], ne = a.seg_n0[sg + 1];
+      constexpr int SR = BN + 4;
+      float* stile = (float*)smem + warp * 32 * SR;
+#pragma unroll
+      for (int c = 0; c < BN; c += 4)
+        *(float4*)(stile + lane * SR + c) = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
+      __syncwarp();
+      const bool rmw = a.accumulate && !part;
+      const int nc = n0 + 4 * lane;
+      const bool fullc = nc + 3 < ne;
+#pragma unroll 1
+      for (int rr = 0; rr < 32; ++rr) {
+        const int mr = m0 + warp * 32 + rr;
+        if (mr >= a.M) break;
+        float* yrow = part ? a.partial + ((int64_t)blockIdx.z * a.M + mr) * a.N
+                           : a.seg_y[sg] + (int64_t)mr * a.seg_ldy[sg] - nb;
+        float4 t = *(const float4*)(stile + rr * SR + 4 * lane);
+        float* dst = yrow + nc;
+        if (fullc && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+          if (rmw) {
+            const float4 o = *(const float4*)dst;
+            t.x += o.x;
+            t.y += o.y;
+            t.z += o.z;
+            t.w += o.w;
+          }
+          *(float4*)dst = t;
+        } else {
+          const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (nc + e < ne) dst[e] = rmw ? dst[e] + tv[e] : tv[e];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * BN) : "memory");
+  }
+}
+
 // x (fp32, rows of K) -> fp16 hi and lo planes
 __global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint2* __restrict__ hi,
                                   uint2* __restrict__ lo) {
@@ -599,7 +829,8 @@ __global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint
 // and the fp16 hi / lo split, with the element arithmetic of rmsnorm_kernel /
 // silu_mul_kernel (ops.cu) so the planes hold the values those kernels produce.
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int K, const XPro pro,
-                                                        uint2* __restrict__ hi, uint2* __restrict__ lo) {
+                                                        uint2* __restrict__ hi, uint2* __restrict__ lo,
+                                                        __half* __restrict__ xsh, __half* __restrict__ xsl, int Kp) {
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * K;
   float inv = 1.f;
@@ -648,6 +879,19 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     const int64_t o = (int64_t)row * (K / 4) + q;
     hi[o] = make_uint2(hp[0], hp[1]);
     lo[o] = make_uint2(lp[0], lp[1]);
+    if (xsh) {
+      // sums of the values over each 32-element sub-block (8 consecutive threads)
+      float sm = (f[0] + f[1]) + (f[2] + f[3]);
+      const unsigned act = __activemask();
+      sm += __shfl_xor_sync(act, sm, 1);
+      sm += __shfl_xor_sync(act, sm, 2);
+      sm += __shfl_xor_sync(act, sm, 4);
+      if ((q & 7) == 0) {
+        const __half h = __float2half_rn(sm);
+        xsh[(int64_t)row * Kp + (q >> 3)] = h;
+        xsl[(int64_t)row * Kp + (q >> 3)] = __float2half_rn(__fsub_rn(sm, __half2float(h)));
+      }
+    }
   }
 }
 
@@ -682,6 +926,48 @@ __global__ void weight_split_kernel(const DevWeight W, int N, int K, uint4* __re
       hi[u * 4 + c] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
       lo[u * 4 + c] = make_uint4(lp[0], lp[1], lp[2], lp[3]);
     }
+  }
+}
+
+// Q4_K weight [N][K] -> the three arrays of the two-MMA path (one thread per
+// 32-weight sub-block j of block b of row n; Q4KTensor.cs:129-147 element formula
+// w = (d sc_j) q - dmin m_j, regrouped as d (sc_j q) - dmin m_j):
+//   qp[n][k]   = fp16(sc_j q_k), an integer <= 945, exact in fp16;
+//   dv[n][b]   = d of block b;
+//   mh / ml[n][32b + j] = fp16 hi / lo of -(dmin m_j) (the reference's own fp32
+//                product), columns past K / 32 up to Kp left as they are (zero).
+__global__ void q4k2_weight_kernel(const DevWeight W, int N, int K, int Kp, __half* __restrict__ qp,
+                                   float* __restrict__ dv, __half* __restrict__ mh, __half* __restrict__ ml) {
+  const int NB = K >> 8;
+  const int64_t units = (int64_t)N * NB * 8;
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(u & 7);
+    const int64_t nb = u >> 3;
+    const int n = (int)(nb / NB), b = (int)(nb - (int64_t)n * NB);
+    const uint8_t* blk = (const uint8_t*)W.data + ((int64_t)n * NB + b) * Q4K_BLOCK_BYTES;
+    const uint32_t h0 = *(const uint32_t*)blk;
+    const float d = half_bits_to_float((uint16_t)(h0 & 0xFFFF)), dmin = half_bits_to_float((uint16_t)(h0 >> 16));
+    int sc, mn;
+    unpack_q4k_scales(blk + 4, j, sc, mn);
+    if (j == 0) dv[(int64_t)n * NB + b] = d;
+    {
+      const float mv = -__fmul_rn(dmin, (float)mn);
+      const __half h = __float2half_rn(mv);
+      mh[(int64_t)n * Kp + 8 * b + j] = h;
+      ml[(int64_t)n * Kp + 8 * b + j] = __float2half_rn(__fsub_rn(mv, __half2float(h)));
+    }
+    const uint4 q = *(const uint4*)(blk + 16 + 16 * j);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    uint32_t hv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t by = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      const __half lo = __int2half_rn(sc * (int)(by & 0xF)), hi = __int2half_rn(sc * (int)(by >> 4));
+      hv[i] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+    }
+    uint4* dst = (uint4*)(qp + (int64_t)n * K + 256 * b + 32 * j);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) dst[c] = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
   }
 }
 
@@ -741,6 +1027,19 @@ struct PlaneEntry {
 std::mutex g_plane_mu;
 std::vector<PlaneEntry> g_planes;
 
+// Two-MMA Q4_K data of a weight group (q4k2_weight_kernel): the sc*q plane, the
+// block d values and the -(dmin m) matrix as an fp32 weight per segment.
+struct Q4k2Entry {
+  std::vector<const void*> keys;
+  int dev;
+  int N, K, Kp;
+  __half* qp;
+  float* dv;
+  __half* mh;  // fp16 hi / lo of -(dmin m), [N][Kp]
+  __half* ml;
+};
+std::vector<Q4k2Entry> g_q4k2;
+
 bool planes_enabled() {
   const char* e = std::getenv("SMALLMIND_WEIGHT_PLANES");
   return !(e && e[0] == '0');
@@ -788,10 +1087,75 @@ int resident_planes(const DevWeight* const* Ws, int nw, int N, int K, int dev, c
   return SM_OK;
 }
 
+// the group's two-MMA Q4_K data (entry nullptr when not resident); creates it when allowed
+int resident_q4k2(const DevWeight* const* Ws, int nw, int N, int K, int dev, cudaStream_t st, Q4k2Entry* out,
+                  bool* found, int* n_launch) {
+  *found = false;
+  std::vector<const void*> keys(nw);
+  for (int i = 0; i < nw; ++i) keys[i] = Ws[i]->data;
+  std::lock_guard<std::mutex> g(g_plane_mu);
+  for (const auto& e : g_q4k2)
+    if (e.dev == dev && e.keys == keys) {
+      *out = e;
+      *found = true;
+      return SM_OK;
+    }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return SM_OK;
+  const int NB = K / 256, Kp = (K / 32 + 63) / 64 * 64;
+  const size_t bytes = (size_t)N * K * 2 + (size_t)N * NB * 4 + (size_t)N * Kp * 4;  // qp, dv, mh + ml
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || free_b < bytes + total_b / 8) return SM_OK;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return SM_OK;
+  }
+  Q4k2Entry e;
+  e.keys = keys;
+  e.dev = dev;
+  e.N = N;
+  e.K = K;
+  e.Kp = Kp;
+  e.qp = (__half*)p;
+  e.dv = (float*)(e.qp + (size_t)N * K);
+  e.mh = (__half*)(e.dv + (size_t)N * NB);
+  e.ml = e.mh + (size_t)N * Kp;
+  SM_CUDA_TRY(cudaMemsetAsync(e.mh, 0, (size_t)N * Kp * 4, st));
+  int64_t row0 = 0;
+  for (int i = 0; i < nw; ++i) {
+    const int Ni = Ws[i]->N();
+    const int64_t units = (int64_t)Ni * NB * 8;
+    q4k2_weight_kernel<<<(int)std::min<int64_t>((units + 255) / 256, 148 * 16), 256, 0, st>>>(
+        *Ws[i], Ni, K, Kp, e.qp + row0 * K, e.dv + row0 * NB, e.mh + row0 * Kp, e.ml + row0 * Kp);
+    if (n_launch) ++*n_launch;
+    row0 += Ni;
+  }
+  SM_CUDA_TRY(cudaGetLastError());
+  SM_CUDA_TRY(cudaStreamSynchronize(st));
+  g_q4k2.push_back(e);
+  *out = e;
+  *found = true;
+  return SM_OK;
+}
+
 }  // namespace
 
 void gemm_tc_release_weight(const void* data) {
   std::lock_guard<std::mutex> g(g_plane_mu);
+  for (size_t i = 0; i < g_q4k2.size();) {
+    const auto& k = g_q4k2[i].keys;
+    if (std::find(k.begin(), k.end(), data) != k.end()) {
+      int prev = -1;
+      cudaGetDevice(&prev);
+      if (prev != g_q4k2[i].dev) cudaSetDevice(g_q4k2[i].dev);
+      cudaFree(g_q4k2[i].qp);
+      if (prev >= 0 && prev != g_q4k2[i].dev) cudaSetDevice(prev);
+      g_q4k2.erase(g_q4k2.begin() + i);
+    } else {
+      ++i;
+    }
+  }
   for (size_t i = 0; i < g_planes.size();) {
     const auto& k = g_planes[i].keys;
     if (std::find(k.begin(), k.end(), data) != k.end()) {
@@ -835,6 +1199,92 @@ bool gemm_tc_supports_multi(const DevWeight* const* W, int nw, int M) {
   return true;
 }
 
+namespace {
+// Every segment Q4_K with K a whole number of blocks (at most 8192): the two-MMA path applies.
+bool q4k2_ok(const DevWeight* const* Ws, int nw) {
+  for (int i = 0; i < nw; ++i)
+    if (Ws[i]->scheme != SM_Q4_K || Ws[i]->layout != SM_LAYOUT_INTENDED || Ws[i]->K() % 256 ||
+        Ws[i]->K() > 256 * q2::MAX_NB)
+      return false;
+  return true;
+}
+
+int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw,
+                     const float* x, int M, int N, int K, int accumulate, int* status, cudaStream_t st,
+                     int* n_launch, const XPro* pro, int dev) {
+  static bool attr_set[64] = {};
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_q4k2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)q2::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const int Kp = e.Kp;
+  const int64_t n = (int64_t)M * K;
+  void* buf = nullptr;
+  SM_CUDA_TRY(cudaMallocAsync(&buf, (size_t)n * 4 + (size_t)M * Kp * 4, st));
+  __half* hi = (__half*)buf;
+  __half* lo = hi + n;
+  __half* xsh = lo + n;  // x sums per 32 (fp16 hi / lo), [M][Kp]
+  __half* xsl = xsh + (size_t)M * Kp;
+  int rc = SM_OK;
+  if (Kp > K / 32) SM_CUDA_TRY(cudaMemsetAsync(xsh, 0, (size_t)M * Kp * 4, st));
+  XPro none;
+  gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, pro ? *pro : none, (uint2*)hi, (uint2*)lo, xsh, xsl, Kp);
+  if (n_launch) ++*n_launch;
+  CUtensorMap mh, ml, mq, mxh, mxl, mmh, mml;
+  rc = make_plane_map(&mh, hi, M, K);
+  if (rc == SM_OK) rc = make_plane_map(&ml, lo, M, K);
+  if (rc == SM_OK) rc = make_plane_map(&mq, e.qp, N, K);
+  if (rc == SM_OK) rc = make_plane_map(&mxh, xsh, M, Kp);
+  if (rc == SM_OK) rc = make_plane_map(&mxl, xsl, M, Kp);
+  if (rc == SM_OK) rc = make_plane_map(&mmh, e.mh, N, Kp);
+  if (rc == SM_OK) rc = make_plane_map(&mml, e.ml, N, Kp);
+  if (rc == SM_OK) {
+    TcArgs a;
+    a.nseg = nw;
+    a.seg_n0[0] = 0;
+    for (int i = 0; i < nw; ++i) {
+      a.W[i] = *Ws[i];
+      a.seg_y[i] = ys[i];
+      a.seg_ldy[i] = ldys[i];
+      a.seg_n0[i + 1] = a.seg_n0[i] + Ws[i]->N();
+    }
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.accumulate = accumulate;
+    a.status = status;
+    const int gn = (N + BN - 1) / BN, gm = (M + BM - 1) / BM;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int S = 1;
+    if (gn * gm < sms) S = std::max(1, std::min(sms / (gn * gm), K / 256));
+    void* pbuf = nullptr;
+    if (S > 1 && cudaMallocAsync(&pbuf, (size_t)S * M * N * 4, st) != cudaSuccess) {
+      cudaGetLastError();
+      S = 1;
+      pbuf = nullptr;
+    }
+    a.kslices = S;
+    a.partial = (float*)pbuf;
+    gemm_q4k2_kernel<<<dim3(gm, gn, S), q2::THREADS, q2::SMEM_BYTES, st>>>(mh, ml, mq, mxh, mxl, mmh, mml, e.dv,
+                                                                           Kp, a);
+    if (cudaGetLastError() != cudaSuccess) rc = fail(SM_ERR_CUDA, "gemm: launch failed");
+    if (n_launch) ++*n_launch;
+    if (S > 1) {
+      if (rc == SM_OK) {
+        const int64_t MN = (int64_t)M * N;
+        gemm_reduce_kernel<<<(int)std::min<int64_t>((MN + 255) / 256, 148 * 8), 256, 0, st>>>(a.partial, S, a);
+        if (n_launch) ++*n_launch;
+      }
+      cudaFreeAsync(pbuf, st);
+    }
+  }
+  cudaFreeAsync(buf, st);
+  return rc;
+}
+}  // namespace
+
 int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
                          int accumulate, int* status, cudaStream_t st, int* n_launch, const XPro* pro) {
   if (!gemm_tc_supports_multi(Ws, nw, M)) return SM_ERR_UNSUPPORTED;
@@ -852,6 +1302,13 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
     SM_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<true, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)Geo<256>::SMEM_BYTES));
     attr_set[dev] = true;
+  }
+  // Q4_K weights: the two-MMA path on its resident sc*q plane, when it exists or can be made
+  if (planes_enabled() && q4k2_ok(Ws, nw)) {
+    Q4k2Entry e;
+    bool found = false;
+    SM_TRY(resident_q4k2(Ws, nw, N, K, dev, st, &e, &found, n_launch));
+    if (found) return launch_gemm_q4k2(e, Ws, ys, ldys, nw, x, M, N, K, accumulate, status, st, n_launch, pro, dev);
   }
   // More than one 128-row tile of x: the weights come as fp16 planes (resident, or split for this
   // call).  One tile (M <= 128): resident planes when they exist or can be made, since reading
@@ -871,7 +1328,7 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
   int rc = SM_OK;
   {
     if (pro && pro->kind != XPRO_NONE) {
-      gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, *pro, (uint2*)hi, (uint2*)lo);
+      gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, *pro, (uint2*)hi, (uint2*)lo, nullptr, nullptr, 0);
     } else {
       const int64_t n4 = n / 4;
       const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
