@@ -577,49 +577,55 @@ __global__ void __launch_bounds__(Roles<WT>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------- two-MMA Q4_K GEMM
-// y (+)= sum_b d[n][b] * sum_{k in b} (sc q)[n][k] x[m][k]   (the -dmin m term runs as
-// a separate small GEMM over per-32 sums of x, see launch_gemm_q4k2).  The weight
-// operand sc*q is an exact fp16 integer, so each 16-wide k step needs two MMAs
-// (x_hi and x_lo) instead of three; the block scale d varies every 256 k, so the
-// accumulator of each 256-weight block is read from TMEM (double-buffered: the MMAs
-// of block b + 1 run while block b is read) and added into registers times d.
-// Warps 0..3: epilogue (TMEM lanes = x rows), warp 4: TMA, warp 5: MMA issuer.
-namespace q2 {
-constexpr int THREADS = 192;
-constexpr int STAGES = 4;
-constexpr int TILE_Q = BN * BK * 2;
-constexpr int STAGE_BYTES = 2 * TILE_A + TILE_Q;
-constexpr int MAX_NB = 32;  // 256-weight blocks per k slice (K <= 8192)
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + (size_t)MAX_NB * BN * 4 + 1024 + 256;
-}  // namespace q2
+// y (+)= sum_b d[n][b] sum_{k in b} (sc q)[n][k] x[m][k]  -  sum_j (dmin m_j)[n] X_j[m]
+// where X_j is the sum of x over 32-element sub-block j.  The weight operand sc*q is
+// an exact fp16 integer, so each 16-wide k step needs two MMAs (x_hi and x_lo)
+// instead of three.  The block scale d changes every 256 k, so each block's
+// accumulator is read from TMEM and added into registers times d; two TMEM buffers
+// let the MMAs of the next block run meanwhile.  "Virtual block" 0 of k slice 0 is
+// the -dmin m term: an fp16 hi / lo GEMM over the x sums (three MMAs per step,
+// K = Kp), read back with scale 1.
+// Warps 0..EW-1: epilogue (warp w: TMEM lanes 32 (w % 4).., 128 columns from 128 (w / 4)),
+// warp EW: TMA, warp EW + 1: MMA issuer.  NB = 256 for GEMMs with several x-row
+// tiles (half the L2 traffic per MAC), 128 otherwise (more CTAs to split K over).
+template <int NB>
+struct Q2 {
+  static constexpr int EW = NB / 32;  // epilogue warps
+  static constexpr int THREADS = (EW + 2) * 32;
+  static constexpr int TILE_Q = NB * BK * 2;
+  static constexpr int STAGE_BYTES = 2 * TILE_A + TILE_Q;
+  static constexpr int STAGES = NB == 256 ? 3 : 4;
+  static constexpr int MAX_NB = 24;  // 256-weight blocks per k slice (K <= 6144)
+  static constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + (size_t)(MAX_NB + 1) * NB * 4 + 1024 + 256;
+};
+constexpr int Q2_MAX_K = 256 * Q2<256>::MAX_NB;
 
-__global__ void __launch_bounds__(q2::THREADS, 1)
+template <int NB>
+__global__ void __launch_bounds__(Q2<NB>::THREADS, 1)
     gemm_q4k2_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_xh,
                      const __grid_constant__ CUtensorMap tm_xl, const __grid_constant__ CUtensorMap tm_mh,
                      const __grid_constant__ CUtensorMap tm_ml, const float* __restrict__ dv, int Kp,
                      const __grid_constant__ TcArgs a) {
-  using namespace q2;
+  using G = Q2<NB>;
+  constexpr int STAGES = G::STAGES, STAGE_BYTES = G::STAGE_BYTES, TILE_Q = G::TILE_Q, EW = G::EW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* dsm = (float*)(smem + STAGES * STAGE_BYTES);  // [block of the slice][128 columns]
-  uint64_t* full = (uint64_t*)(dsm + MAX_NB * BN);
+  float* dsm = (float*)(smem + STAGES * STAGE_BYTES);  // [virtual block][NB columns] read-back scales
+  uint64_t* full = (uint64_t*)(dsm + (G::MAX_NB + 1) * NB);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;
   uint64_t* acce = accf + 2;
-  uint64_t* accm = acce + 2;  // the -dmin m accumulator is complete
-  uint32_t* tmem_slot = (uint32_t*)(accm + 1);
+  uint32_t* tmem_slot = (uint32_t*)(acce + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.y * BN, m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * NB, m0 = blockIdx.x * BM;
   const int K = a.K, NBall = K >> 8;
   const int b0 = (int)((int64_t)NBall * blockIdx.z / a.kslices);
   const int nbs = (int)((int64_t)NBall * (blockIdx.z + 1) / a.kslices) - b0;
-  const int nk = 4 * nbs;  // 64-wide k stages of the slice
-  // slice 0 also runs the -dmin m term: per 64 columns of the x sums, two stages
-  // (x sums hi + lo with -dmin m hi, then x sums hi with -dmin m lo) into TMEM
-  // columns 256..383
-  const bool mterm = blockIdx.z == 0;
-  const int nm = mterm ? 2 * (Kp / BK) : 0;
+  const int nmin = blockIdx.z == 0 ? 1 : 0;  // virtual block 0: the -dmin m term
+  const int nvb = nbs + nmin;
+  const int nm = nmin * 2 * (Kp / BK);      // its stages: x sums hi + lo with mh, then hi with ml
+  const int nk = nm + 4 * nbs;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -628,65 +634,64 @@ __global__ void __launch_bounds__(q2::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 4);
+      mbar_init(&acce[b], EW);
     }
-    mbar_init(accm, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(4 * BN)
+                 "r"(2 * NB)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // this tile's block scales, staged once (columns past N read as 0)
-  for (int i = tid; i < nbs * BN; i += THREADS) {
-    const int bl = i / BN, c = i - bl * BN;
-    dsm[i] = n0 + c < a.N ? dv[(int64_t)(n0 + c) * NBall + b0 + bl] : 0.f;
+  for (int i = tid; i < nvb * NB; i += G::THREADS) {
+    const int vb = i / NB, c = i - vb * NB;
+    dsm[i] = vb < nmin ? 1.f : (n0 + c < a.N ? dv[(int64_t)(n0 + c) * NBall + b0 + vb - nmin] : 0.f);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == EW) {
     if (lane == 0) {
       for (int kt = 0; kt < nk; ++kt) {
         const int s = kt % STAGES;
         if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
         uint8_t* st = smem + s * STAGE_BYTES;
-        const int kg = (4 * b0 + kt) * BK;
-        mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
-        tma_load_2d(st, &tm_hi, kg, m0, &full[s]);
-        tma_load_2d(st + TILE_A, &tm_lo, kg, m0, &full[s]);
-        tma_load_2d(st + 2 * TILE_A, &tm_q, kg, n0, &full[s]);
-      }
-      for (int j = 0; j < nm; ++j) {
-        const int kt = nk + j, s = kt % STAGES;
-        if (kt >= STAGES && !mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1, a.status)) break;
-        uint8_t* st = smem + s * STAGE_BYTES;
-        const int kc = (j >> 1) * BK;
-        if ((j & 1) == 0) {
-          mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
-          tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
-          tma_load_2d(st + TILE_A, &tm_xl, kc, m0, &full[s]);
-          tma_load_2d(st + 2 * TILE_A, &tm_mh, kc, n0, &full[s]);
+        if (kt < nm) {
+          const int kc = (kt >> 1) * BK;
+          if ((kt & 1) == 0) {
+            mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
+            tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
+            tma_load_2d(st + TILE_A, &tm_xl, kc, m0, &full[s]);
+            tma_load_2d(st + 2 * TILE_A, &tm_mh, kc, n0, &full[s]);
+          } else {
+            mbar_expect_tx(&full[s], TILE_A + TILE_Q);
+            tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
+            tma_load_2d(st + 2 * TILE_A, &tm_ml, kc, n0, &full[s]);
+          }
         } else {
-          mbar_expect_tx(&full[s], TILE_A + TILE_Q);
-          tma_load_2d(st, &tm_xh, kc, m0, &full[s]);
-          tma_load_2d(st + 2 * TILE_A, &tm_ml, kc, n0, &full[s]);
+          const int kg = (4 * b0 + kt - nm) * BK;
+          mbar_expect_tx(&full[s], 2 * TILE_A + TILE_Q);
+          tma_load_2d(st, &tm_hi, kg, m0, &full[s]);
+          tma_load_2d(st + TILE_A, &tm_lo, kg, m0, &full[s]);
+          tma_load_2d(st + 2 * TILE_A, &tm_q, kg, n0, &full[s]);
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == EW + 1) {
     if (lane == 0) {
       bool ok = true;
-      for (int bl = 0; bl < nbs && ok; ++bl) {
-        const int b = bl & 1;
-        if (bl >= 2) ok = mbar_wait_bounded(&acce[b], ((bl >> 1) - 1) & 1, a.status);
+      int kt = 0;
+      for (int vb = 0; vb < nvb && ok; ++vb) {
+        const int b = vb & 1;
+        if (vb >= 2) ok = mbar_wait_bounded(&acce[b], ((vb >> 1) - 1) & 1, a.status);
         tc_fence_after();
-        for (int s4 = 0; s4 < 4 && ok; ++s4) {
-          const int kt = 4 * bl + s4, s = kt % STAGES;
+        const bool mt = vb < nmin;
+        const int ns = mt ? nm : 4;
+        for (int j = 0; j < ns && ok; ++j, ++kt) {
+          const int s = kt % STAGES;
           ok = mbar_wait_bounded(&full[s], (kt / STAGES) & 1, a.status);
           if (!ok) break;
           tc_fence_after();
@@ -695,46 +700,31 @@ __global__ void __launch_bounds__(q2::THREADS, 1)
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-            mma_f16(tmem + b * BN, dah + adv, dq + adv, (s4 | ks) != 0);
-            mma_f16(tmem + b * BN, dal + adv, dq + adv, 1);
+            mma_f16<NB>(tmem + b * NB, dah + adv, dq + adv, (j | ks) != 0);
+            if (!mt || (j & 1) == 0) mma_f16<NB>(tmem + b * NB, dal + adv, dq + adv, 1);
           }
           mma_commit(&empty[s]);
         }
         if (ok) mma_commit(&accf[b]);
       }
-      for (int j = 0; j < nm && ok; ++j) {
-        const int kt = nk + j, s = kt % STAGES;
-        ok = mbar_wait_bounded(&full[s], (kt / STAGES) & 1, a.status);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-        const uint64_t dah = sw128_desc(base), dal = sw128_desc(base + TILE_A), dm = sw128_desc(base + 2 * TILE_A);
-#pragma unroll
-        for (int ks = 0; ks < BK / 16; ++ks) {
-          const uint64_t adv = (uint64_t)((ks * 32) >> 4);
-          mma_f16(tmem + 2 * BN, dah + adv, dm + adv, (j | ks) != 0);
-          if ((j & 1) == 0) mma_f16(tmem + 2 * BN, dal + adv, dm + adv, 1);
-        }
-        mma_commit(&empty[s]);
-      }
-      if (ok && nm) mma_commit(accm);
     }
   } else {
-    // ---- epilogue warps 0..3: row m0 + 32 warp + lane, 128 columns in registers
-    float y[BN];
+    // ---- epilogue: row m0 + 32 (warp % 4) + lane, columns 128 (warp / 4) .. + 127
+    const int lq = warp & 3, ch = (warp >> 2) * 128;
+    float y[128];
 #pragma unroll
-    for (int c = 0; c < BN; ++c) y[c] = 0.f;
+    for (int c = 0; c < 128; ++c) y[c] = 0.f;
     bool ok = true;
-    for (int bl = 0; bl < nbs; ++bl) {
-      const int b = bl & 1;
-      ok = mbar_wait_bounded(&accf[b], (bl >> 1) & 1, a.status);
+    for (int vb = 0; vb < nvb; ++vb) {
+      const int b = vb & 1;
+      ok = mbar_wait_bounded(&accf[b], (vb >> 1) & 1, a.status);
       if (!ok) break;
       tc_fence_after();
-      const float* db = dsm + bl * BN;
+      const float* db = dsm + vb * NB + ch;
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 0; c0 < 128; c0 += 16) {
         uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN + c0), v);
+        tmem_ld16(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * NB + ch + c0), v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) y[c0 + e] = fmaf(__uint_as_float(v[e]), db[c0 + e], y[c0 + e]);
       }
@@ -742,39 +732,26 @@ __global__ void __launch_bounds__(q2::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[b]);
     }
-    if (ok && nm) {
-      ok = mbar_wait_bounded(accm, 0, a.status);
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(2 * BN + c0), v);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) y[c0 + e] += __uint_as_float(v[e]);
-        }
-      }
-    }
-    // every MMA has completed (the last block's accumulator was read), so the
-    // stage buffers are free: rows go through shared memory for whole-row stores
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+    // every MMA has completed (the last accumulator was read): the stage buffers are
+    // free, rows go through shared memory for whole-row stores
+    asm volatile("bar.sync 2, %0;" ::"n"(EW * 32) : "memory");
     if (ok) {
       const bool part = a.kslices > 1;
       int sg = 0;
       while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
       const int nb = a.seg_n0[sg], ne = a.seg_n0[sg + 1];
-      constexpr int SR = BN + 4;
+      constexpr int SR = 128 + 4;
       float* stile = (float*)smem + warp * 32 * SR;
 #pragma unroll
-      for (int c = 0; c < BN; c += 4)
+      for (int c = 0; c < 128; c += 4)
         *(float4*)(stile + lane * SR + c) = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
       __syncwarp();
       const bool rmw = a.accumulate && !part;
-      const int nc = n0 + 4 * lane;
+      const int nc = n0 + ch + 4 * lane;
       const bool fullc = nc + 3 < ne;
 #pragma unroll 1
       for (int rr = 0; rr < 32; ++rr) {
-        const int mr = m0 + warp * 32 + rr;
+        const int mr = m0 + lq * 32 + rr;
         if (mr >= a.M) break;
         float* yrow = part ? a.partial + ((int64_t)blockIdx.z * a.M + mr) * a.N
                            : a.seg_y[sg] + (int64_t)mr * a.seg_ldy[sg] - nb;
@@ -802,7 +779,7 @@ __global__ void __launch_bounds__(q2::THREADS, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NB) : "memory");
   }
 }
 
@@ -1204,7 +1181,7 @@ namespace {
 bool q4k2_ok(const DevWeight* const* Ws, int nw) {
   for (int i = 0; i < nw; ++i)
     if (Ws[i]->scheme != SM_Q4_K || Ws[i]->layout != SM_LAYOUT_INTENDED || Ws[i]->K() % 256 ||
-        Ws[i]->K() > 256 * q2::MAX_NB)
+        Ws[i]->K() > Q2_MAX_K)
       return false;
   return true;
 }
@@ -1214,10 +1191,16 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
                      int* n_launch, const XPro* pro, int dev) {
   static bool attr_set[64] = {};
   if (dev < 64 && !attr_set[dev]) {
-    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_q4k2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)q2::SMEM_BYTES));
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_q4k2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Q2<128>::SMEM_BYTES));
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_q4k2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Q2<256>::SMEM_BYTES));
     attr_set[dev] = true;
   }
+  // 256-wide tiles with several x-row tiles, when the stacked segments meet on 256 rows
+  bool wide = M > BM;
+  for (int i = 0; i + 1 < nw; ++i) wide = wide && Ws[i]->N() % 256 == 0;
+  const int nbw = wide ? 256 : BN;
   const int Kp = e.Kp;
   const int64_t n = (int64_t)M * K;
   void* buf = nullptr;
@@ -1234,11 +1217,11 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
   CUtensorMap mh, ml, mq, mxh, mxl, mmh, mml;
   rc = make_plane_map(&mh, hi, M, K);
   if (rc == SM_OK) rc = make_plane_map(&ml, lo, M, K);
-  if (rc == SM_OK) rc = make_plane_map(&mq, e.qp, N, K);
+  if (rc == SM_OK) rc = make_plane_map(&mq, e.qp, N, K, nbw);
   if (rc == SM_OK) rc = make_plane_map(&mxh, xsh, M, Kp);
   if (rc == SM_OK) rc = make_plane_map(&mxl, xsl, M, Kp);
-  if (rc == SM_OK) rc = make_plane_map(&mmh, e.mh, N, Kp);
-  if (rc == SM_OK) rc = make_plane_map(&mml, e.ml, N, Kp);
+  if (rc == SM_OK) rc = make_plane_map(&mmh, e.mh, N, Kp, nbw);
+  if (rc == SM_OK) rc = make_plane_map(&mml, e.ml, N, Kp, nbw);
   if (rc == SM_OK) {
     TcArgs a;
     a.nseg = nw;
@@ -1254,7 +1237,7 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
     a.K = K;
     a.accumulate = accumulate;
     a.status = status;
-    const int gn = (N + BN - 1) / BN, gm = (M + BM - 1) / BM;
+    const int gn = (N + nbw - 1) / nbw, gm = (M + BM - 1) / BM;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int S = 1;
@@ -1267,8 +1250,12 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
     }
     a.kslices = S;
     a.partial = (float*)pbuf;
-    gemm_q4k2_kernel<<<dim3(gm, gn, S), q2::THREADS, q2::SMEM_BYTES, st>>>(mh, ml, mq, mxh, mxl, mmh, mml, e.dv,
-                                                                           Kp, a);
+    if (wide)
+      gemm_q4k2_kernel<256><<<dim3(gm, gn, S), Q2<256>::THREADS, Q2<256>::SMEM_BYTES, st>>>(
+          mh, ml, mq, mxh, mxl, mmh, mml, e.dv, Kp, a);
+    else
+      gemm_q4k2_kernel<128><<<dim3(gm, gn, S), Q2<128>::THREADS, Q2<128>::SMEM_BYTES, st>>>(
+          mh, ml, mq, mxh, mxl, mmh, mml, e.dv, Kp, a);
     if (cudaGetLastError() != cudaSuccess) rc = fail(SM_ERR_CUDA, "gemm: launch failed");
     if (n_launch) ++*n_launch;
     if (S > 1) {
