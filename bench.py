@@ -233,6 +233,9 @@ def time_tp_decode(sm, ctx, torch, stream, world, rank, steps, warmup, prompt_le
     all-reduces of one hidden row, timed alone through the same NCCL group."""
     from smallmind_b200 import sharding, tp
     cfg = dict(TINYLLAMA)
+    # the group lives on its own context, released on every rank at the end
+    ctx = sm.CudaContext(torch.cuda.current_device())
+    ctx.set_stream(stream.cuda_stream)
     group = tp.TensorParallelGroup(ctx, world, rank)
     host = build_host_model(sm, ctx, cfg)
     model = sm.CudaModel.from_host(ctx, tp.shard_model(host, world, rank))
@@ -270,6 +273,10 @@ def time_tp_decode(sm, ctx, torch, stream, world, rank, steps, warmup, prompt_le
     ar_us = sharding.max_over_ranks(e0.elapsed_time(e1) * 1000 / 20, device="cuda")
     kv.close()
     model.close()
+    stream.synchronize()
+    torch.distributed.barrier()
+    ctx.close()
+    torch.distributed.barrier()
     return {"tp": world, "tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 4),
             "allreduce_us_per_token": round(ar_us, 1), "allreduces_per_token": n_ar,
             "allreduce_bytes": 4 * cfg["hidden"], "path": "per-kernel decode step, NCCL all-reduce after O and down"}

@@ -17,7 +17,7 @@ STEPS = 5
 
 
 def main(out_dir):
-    faulthandler.dump_traceback_later(200, exit=True)  # a stuck rank prints where it is and ends
+    faulthandler.dump_traceback_later(int(os.environ.get("TP_RANK_STACK_AFTER", "200")), exit=True)  # a stuck rank prints where it is and ends
     import torch
     import torch.distributed as dist
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -52,9 +52,22 @@ def main(out_dir):
             _, r = rkv.decode([0], [t])
             ref.append(r[0])
         np.save(os.path.join(out_dir, "ref.npy"), np.stack(ref))
+    # release the library's objects on every rank while all ranks are alive (the
+    # context owns the NCCL communicator), then leave without interpreter teardown:
+    # a rank must not sit in CUDA / NCCL clean-up waiting for a peer that has gone
+    kv.close()
+    model.close()
+    if rank == 0:
+        rkv.close()
+        ref_model.close()
+    dist.barrier()
+    ctx.close()
     dist.barrier()
     dist.destroy_process_group()
     faulthandler.cancel_dump_traceback_later()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":
