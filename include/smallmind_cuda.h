@@ -83,6 +83,8 @@ SM_API int sm_device_count(int* out);
 /* One device + one CUDA stream.  Replaces nothing in the reference (managed
  * arrays need no context); the C# shim owns it as an IDisposable. */
 SM_API int sm_ctx_create(int device, sm_ctx** out);
+/* Destroying the context does not free the weights, models and KV caches made on it;
+ * their destroy calls stay valid afterwards (they wait on the whole device). */
 SM_API int sm_ctx_destroy(sm_ctx* ctx);
 /* Use an external cudaStream_t (e.g. one owned by a host framework); NULL = own stream. */
 SM_API int sm_ctx_set_stream(sm_ctx* ctx, void* cuda_stream);

@@ -236,6 +236,7 @@ class CudaModel:
             for n in ROLE_OF:
                 m.set_weight(li, n, CudaWeightTensor.from_qtensor(ctx, layer[n]))
         m.finalize()
+        m._owns_weights = True
         return m
 
     def nbytes(self) -> int:
@@ -244,9 +245,15 @@ class CudaModel:
         return v.value
 
     def close(self):
+        """Releases the model; weights uploaded by from_host go with it (weights passed to
+        set_weight by the caller stay the caller's)."""
         if self.handle:
             L.lib().sm_model_destroy(self.handle)
             self.handle = None
+        if getattr(self, "_owns_weights", False):
+            for w in self._weights:
+                w.close()
+            self._weights = []
 
 
 class KVCache:

@@ -35,6 +35,7 @@ struct sm_ctx {
 
 struct sm_weight {
   sm_ctx* ctx = nullptr;
+  int device = 0;  // destroy needs only this, so a weight may outlive its context
   DevWeight w;
 };
 
@@ -130,6 +131,7 @@ int upload_weight(sm_ctx* ctx, int scheme, int rows, int cols, int bs, const voi
   DeviceGuard g(ctx->device);
   auto* w = new sm_weight();
   w->ctx = ctx;
+  w->device = ctx->device;
   DevWeight& d = w->w;
   d.scheme = scheme;
   d.layout = layout;
@@ -339,8 +341,8 @@ SM_API int sm_weight_upload_device(sm_ctx* ctx, int scheme, int rows, int cols, 
 
 SM_API int sm_weight_destroy(sm_weight* w) {
   if (!w) return SM_OK;
-  DeviceGuard g(w->ctx->device);
-  cudaStreamSynchronize(w->ctx->stream);
+  DeviceGuard g(w->device);
+  cudaDeviceSynchronize();
   gemm_tc_release_weight(w->w.data);
   if (w->w.data) cudaFree(w->w.data);
   if (w->w.aux) cudaFree(w->w.aux);
@@ -595,6 +597,7 @@ struct Work {
 
 struct sm_model {
   sm_ctx* ctx = nullptr;
+  int device = 0;  // destroy needs only this
   sm_model_config cfg{};
   struct Layer {
     const DevWeight* w[N_LAYER_ROLES] = {};
@@ -618,6 +621,7 @@ struct sm_model {
 
 struct sm_kv {
   sm_model* m = nullptr;
+  int device = 0;  // destroy needs only this
   int max_seqs = 0, max_tokens = 0;
   float* k = nullptr;
   float* v = nullptr;
@@ -1130,6 +1134,7 @@ SM_API int sm_model_create(sm_ctx* ctx, const sm_model_config* cfg, sm_model** o
   DeviceGuard g(ctx->device);
   auto* m = new sm_model();
   m->ctx = ctx;
+  m->device = ctx->device;
   m->cfg = c;
   m->layers.resize(c.n_layers);
   std::vector<float> hs, hc;
@@ -1252,8 +1257,8 @@ SM_API int sm_model_finalize(sm_model* m) {
 
 SM_API int sm_model_destroy(sm_model* m) {
   if (!m) return SM_OK;
-  DeviceGuard g(m->ctx->device);
-  cudaStreamSynchronize(m->ctx->stream);
+  DeviceGuard g(m->device);
+  cudaDeviceSynchronize();
   Work& w = m->work;
   for (void* p : {(void*)w.x, (void*)w.h, (void*)w.qkv, (void*)w.att, (void*)w.g, (void*)w.u, (void*)w.logits,
                   (void*)w.ints, (void*)w.attn_scratch, (void*)m->embd, (void*)m->out_norm, (void*)m->sin_t,
@@ -1283,6 +1288,7 @@ SM_API int sm_kv_create(sm_model* m, int max_seqs, int max_tokens, sm_kv** out) 
   DeviceGuard g(m->ctx->device);
   auto* kv = new sm_kv();
   kv->m = m;
+  kv->device = m->device;
   kv->max_seqs = max_seqs;
   kv->max_tokens = max_tokens;
   const size_t bytes = kv->layer_stride() * m->cfg.n_layers * sizeof(float);
@@ -1302,8 +1308,8 @@ SM_API int sm_kv_create(sm_model* m, int max_seqs, int max_tokens, sm_kv** out) 
 
 SM_API int sm_kv_destroy(sm_kv* kv) {
   if (!kv) return SM_OK;
-  DeviceGuard g(kv->m->ctx->device);
-  cudaStreamSynchronize(kv->m->ctx->stream);
+  DeviceGuard g(kv->device);
+  cudaDeviceSynchronize();
   for (auto& it : kv->graphs)
     if (it.second.exec) cudaGraphExecDestroy(it.second.exec);
   if (kv->mega_layers) cudaFree(kv->mega_layers);
