@@ -159,12 +159,15 @@ SM_API int sm_attention_decode(sm_ctx* ctx, const float* q, const float* k_cache
 /* Same computation as sm_attention_decode, for callers that cannot let the
  * library allocate device memory (hosts that reserve their whole device budget
  * up front, or run where another allocator owns the device).  No counterpart in
- * the reference: it has no device memory at all.  Working memory comes from a
- * fixed 16 MiB static device array held by every GPU that loads the library; sizes
- * needing more (B * n_heads * (max_ctx + 66 * ceil(max_ctx/64)) floats) return
- * SM_ERR_SHAPE.  The first call on a device looks up the array's address and
- * should come before any stream capture.  Calls share the array: calls that
- * overlap on the GPU race and must be serialised.  Device pointers only. */
+ * the reference: it has no device memory at all.  Shapes the scratch-free
+ * cluster kernel takes (head_dim 64, at most 8 q heads per kv head) use it;
+ * other shapes take working memory from a fixed 16 MiB static device array held
+ * by every GPU that loads the library, and those needing more
+ * (B * n_heads * (max_ctx + 66 * ceil(max_ctx/64)) floats) return SM_ERR_SHAPE.
+ * The first call on a device that uses the array looks up its address (make it
+ * before any stream capture; a later reset of the device's primary context is
+ * not supported).  Calls share the array: calls that overlap on the GPU race and
+ * must be serialised.  Device pointers only. */
 SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
                                        float* out, const int* lens_dev, int B, int max_ctx, int n_heads, int n_kv,
                                        int head_dim);

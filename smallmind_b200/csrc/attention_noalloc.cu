@@ -9,13 +9,20 @@
 // takes the same inputs and outputs but uses a fixed scratch array that lives
 // in this library's device image instead.
 //
+//  * The single-launch cluster kernel, which needs no scratch at all, runs
+//    whenever it takes the shape (head_dim 64, at most 8 q heads per kv head);
+//    only the other shapes use the split-context kernels and the array below.
 //  * The scratch is a file-scope static __device__ array of 16 MiB.  Every GPU
 //    that loads the library holds it until the process exits.
 //  * Host code cannot use the array's name as a device address (in host code
 //    it names a host-side stand-in), so the first call on each device, with
 //    that device current, looks up the real address with cudaGetSymbolAddress
 //    and caches it.  Make that first call before any stream capture.
-//  * Sizes whose scratch would exceed 16 MiB are rejected with SM_ERR_SHAPE.
+//  * Shapes the cluster kernel does not take and whose scratch would exceed
+//    16 MiB are rejected with SM_ERR_SHAPE.
+//  * The cached address belongs to the CUDA context current at the first call:
+//    resetting or re-creating a device's primary context afterwards is not
+//    supported by this entry point.
 //  * All calls share the one array and it keeps the previous call's contents.
 //    Nothing needs clearing: every scratch element a call reads is written
 //    earlier in the same call.  Calls that overlap on the GPU (two streams,
@@ -61,10 +68,6 @@ extern "C" SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, c
     return sm::fail(SM_ERR_SHAPE, "attention_decode_noalloc: bad shape");
   if (!ctx || !q || !k_cache || !v_cache || !out || !lens_dev)
     return sm::fail(SM_ERR_INVALID_ARG, "attention_decode_noalloc: null argument");
-  const size_t need = sm::attention_decode_scratch_floats(B, n_heads, max_ctx);
-  if (need > kNoAllocScratchFloats)
-    return sm::fail(SM_ERR_SHAPE, "attention_decode_noalloc: B * n_heads * (max_ctx + 66 * ceil(max_ctx / 64)) "
-                                  "floats exceed the 16 MiB static scratch");
   int device = 0;
   cudaStream_t stream = nullptr;
   int64_t* launches = nullptr;
@@ -72,11 +75,24 @@ extern "C" SM_API int sm_attention_decode_noalloc(sm_ctx* ctx, const float* q, c
   int prev = -1;
   SM_CUDA_TRY(cudaGetDevice(&prev));
   if (prev != device) SM_CUDA_TRY(cudaSetDevice(device));
-  float* scratch = nullptr;
-  int rc = scratch_address(device, &scratch);
+  const int64_t head_stride = (int64_t)max_ctx * head_dim;
   int nl = 0;
+  int rc = sm::launch_attention_decode_cluster(q, n_heads * head_dim, k_cache, v_cache, head_stride * n_kv, head_dim,
+                                               head_stride, max_ctx, out, n_heads * head_dim, lens_dev, nullptr, B,
+                                               n_heads, n_kv, head_dim, stream, &nl);
+  if (rc != SM_ERR_UNSUPPORTED) {
+    *launches += nl;
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    return rc;
+  }
+  nl = 0;
+  float* scratch = nullptr;
+  if (sm::attention_decode_scratch_floats(B, n_heads, max_ctx) > kNoAllocScratchFloats)
+    rc = sm::fail(SM_ERR_SHAPE, "attention_decode_noalloc: B * n_heads * (max_ctx + 66 * ceil(max_ctx / 64)) "
+                                "floats exceed the 16 MiB static scratch");
+  else
+    rc = scratch_address(device, &scratch);
   if (rc == SM_OK) {
-    const int64_t head_stride = (int64_t)max_ctx * head_dim;
     rc = sm::launch_attention_decode(q, n_heads * head_dim, k_cache, v_cache, head_stride * n_kv, head_dim,
                                      head_stride, max_ctx, out, n_heads * head_dim, lens_dev, nullptr, B, n_heads,
                                      n_kv, head_dim, scratch, kNoAllocScratchFloats, stream, &nl);

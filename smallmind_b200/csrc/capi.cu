@@ -828,23 +828,10 @@ int head_m1(sm_model* m, const float* x_row, int& nl) {
   return SM_OK;
 }
 
-// The transformer stack over `rows` token rows whose tok/seq/pos/lens are in
-// work.ints.  prefill: the rows are one or more prompts (PrefillSeg), each at
-// positions pos0..pos0+T-1 of its slot; otherwise one row per sequence (decode).
-// Projections that share their input (Q|K|V, gate|up): one tensor-core GEMM over
-// the stacked weights when it applies, else one launch per weight.
-int matmul_multi(const DevWeight* const* ws, float* const* ys, const int* ld, int nw, const float* x, int rows,
-                 cudaStream_t st, int& nl) {
-  const char* et = std::getenv("SMALLMIND_GEMM_TC");
-  if (!(et && et[0] == '0') && gemm_tc_supports_multi(ws, nw, rows))
-    return launch_gemm_tc_multi(ws, ys, ld, nw, x, rows, 0, nullptr, st, &nl);
-  for (int i = 0; i < nw; ++i) SM_TRY(launch_matmul(*ws[i], x, ys[i], rows, ld[i], 0, st, &nl));
-  return SM_OK;
-}
-
-// As matmul_multi, with x first passed through a prologue (RMSNorm or the SiLU gate,
-// XPro).  On the tensor-core GEMM the prologue runs inside its x-split pass; other
-// paths apply it into `tmp` (rows x K) and read that.
+// Projections that share their input (Q|K|V, gate|up) run as one tensor-core GEMM
+// over the stacked weights when it applies, else one launch per weight.  x first
+// passes through a prologue (RMSNorm or the SiLU gate, XPro): on the tensor-core
+// GEMM inside its x-split pass; other paths apply it into `tmp` (rows x K) and read that.
 int matmul_multi_pro(const DevWeight* const* ws, float* const* ys, const int* ld, int nw, const float* x, int rows,
                      const XPro& pro, float* tmp, int accumulate, cudaStream_t st, int& nl) {
   const char* et = std::getenv("SMALLMIND_GEMM_TC");
