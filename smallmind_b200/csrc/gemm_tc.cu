@@ -127,6 +127,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 columns of this warp's 32 TMEM lanes, without waiting (tmem_wait_ld completes them)
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // Packed bytes of one unit, loaded ahead of their decode (register prefetch).
 // Q4_K: a = block header, b = the unit's 16 code bytes.  Q6_K: a = ql, b.xy =
 // high plane words, b.z = the two int8 scales, b.w = d bits.  Q8_0: a, b = 32
@@ -802,13 +822,59 @@ __global__ void gemm_split_kernel(const float4* __restrict__ x, int64_t n4, uint
   }
 }
 
+// The prologue of four consecutive elements f of a row (elements 4 q4 .. 4 q4 + 3):
+// RMSNorm (gamma (x inv)) or the SiLU gate (silu(x) up), with the element arithmetic of
+// rmsnorm_kernel / silu_mul_kernel (ops.cu).
+__device__ __forceinline__ void prep4(float (&f)[4], const XPro& pro, float inv, const float* ur, int q4) {
+  if (pro.kind == XPRO_RMSNORM) {
+    const float4 g = ((const float4*)pro.gamma)[q4];
+    const float gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f[e] = __fmul_rn(gv[e], __fmul_rn(f[e], inv));
+  } else if (pro.kind == XPRO_SILU) {
+    const float4 uu = ((const float4*)ur)[q4];
+    const float uv[4] = {uu.x, uu.y, uu.z, uu.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = fmaxf(-20.f, fminf(f[e], 20.f));
+      const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));
+      f[e] = __fmul_rn(__fmul_rn(f[e], sig), uv[e]);
+    }
+  }
+}
+
+// fp16 pair (hi, lo) of v: hi = fp16(v), lo = fp16(v - hi)
+__device__ __forceinline__ void split_half(float v, uint32_t& h, uint32_t& l) {
+  const __half hh = __float2half_rn(v);
+  h = __half_as_ushort(hh);
+  l = __half_as_ushort(__float2half_rn(__fsub_rn(v, __half2float(hh))));
+}
+
 // One row of x per block: the prologue (RMSNorm over the row, or the SiLU gate)
-// and the fp16 hi / lo split, with the element arithmetic of rmsnorm_kernel /
-// silu_mul_kernel (ops.cu) so the planes hold the values those kernels produce.
+// and the fp16 hi / lo split, so the planes hold the values rmsnorm_kernel /
+// silu_mul_kernel would produce.  xsh / xsl (optional): fp16 hi / lo of the sums of
+// the values over each 32-element sub-block, [M][Kp].
+// TILED (the skinny GEMM's x operand, gemm_sk_kernel): hi_ receives [K / 64 chunks][hi, lo
+// plane][nbt rows][64 k] of fp16, each plane in the 128-byte-swizzled K-major layout the MMA
+// reads, so one contiguous copy brings in whole stages; within each group of 8 elements the
+// k order is 0,4,1,5,2,6,3,7 (the order of the weight operand).  The grid has nbt blocks;
+// rows M .. nbt-1 are written as zeros.
+template <bool TILED>
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int K, const XPro pro,
-                                                        uint2* __restrict__ hi, uint2* __restrict__ lo,
-                                                        __half* __restrict__ xsh, __half* __restrict__ xsl, int Kp) {
+                                                        void* __restrict__ hi_, void* __restrict__ lo_,
+                                                        __half* __restrict__ xsh, __half* __restrict__ xsl, int Kp,
+                                                        int M = 0, int nbt = 0) {
   const int row = blockIdx.x;
+  if (TILED && row >= M) {
+    uint4* t = (uint4*)hi_;
+    for (int q = threadIdx.x; q < K / 8; q += blockDim.x) {
+      const int64_t base = (int64_t)(q >> 3) * 2 * nbt * 8;
+      const uint32_t c = sw_off(row, q & 7) >> 4;
+      t[base + c] = make_uint4(0u, 0u, 0u, 0u);
+      t[base + nbt * 8 + c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
   const float* xr = x + (int64_t)row * K;
   float inv = 1.f;
   if (pro.kind == XPRO_RMSNORM) {
@@ -827,48 +893,539 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), pro.eps)));
   }
   const float* ur = pro.u ? pro.u + (int64_t)row * K : nullptr;
-  for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
-    const float4 v = ((const float4*)xr)[q];
-    float f[4] = {v.x, v.y, v.z, v.w};
-    if (pro.kind == XPRO_RMSNORM) {
-      const float4 g = ((const float4*)pro.gamma)[q];
-      const float gv[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] = __fmul_rn(gv[e], __fmul_rn(f[e], inv));
-    } else if (pro.kind == XPRO_SILU) {
-      const float4 uu = ((const float4*)ur)[q];
-      const float uv[4] = {uu.x, uu.y, uu.z, uu.w};
+  if (!TILED) {
+    uint2* hi = (uint2*)hi_;
+    uint2* lo = (uint2*)lo_;
+    for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
+      const float4 v = ((const float4*)xr)[q];
+      float f[4] = {v.x, v.y, v.z, v.w};
+      prep4(f, pro, inv, ur, q);
+      uint32_t hp[2] = {0, 0}, lp[2] = {0, 0};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float c = fmaxf(-20.f, fminf(f[e], 20.f));
-        const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-c)));
-        f[e] = __fmul_rn(__fmul_rn(f[e], sig), uv[e]);
+        uint32_t h, l;
+        split_half(f[e], h, l);
+        hp[e >> 1] |= h << (16 * (e & 1));
+        lp[e >> 1] |= l << (16 * (e & 1));
+      }
+      const int64_t o = (int64_t)row * (K / 4) + q;
+      hi[o] = make_uint2(hp[0], hp[1]);
+      lo[o] = make_uint2(lp[0], lp[1]);
+      if (xsh) {
+        // sums of the values over each 32-element sub-block (8 consecutive threads)
+        float sm = (f[0] + f[1]) + (f[2] + f[3]);
+        const unsigned act = __activemask();
+        sm += __shfl_xor_sync(act, sm, 1);
+        sm += __shfl_xor_sync(act, sm, 2);
+        sm += __shfl_xor_sync(act, sm, 4);
+        if ((q & 7) == 0) {
+          uint32_t h, l;
+          split_half(sm, h, l);
+          xsh[(int64_t)row * Kp + (q >> 3)] = __ushort_as_half((unsigned short)h);
+          xsl[(int64_t)row * Kp + (q >> 3)] = __ushort_as_half((unsigned short)l);
+        }
       }
     }
-    uint32_t hp[2] = {0, 0}, lp[2] = {0, 0};
+  } else {
+    uint4* t = (uint4*)hi_;
+    for (int q = threadIdx.x; q < K / 8; q += blockDim.x) {
+      const float4 v0 = ((const float4*)xr)[2 * q], v1 = ((const float4*)xr)[2 * q + 1];
+      float f0[4] = {v0.x, v0.y, v0.z, v0.w}, f1[4] = {v1.x, v1.y, v1.z, v1.w};
+      prep4(f0, pro, inv, ur, 2 * q);
+      prep4(f1, pro, inv, ur, 2 * q + 1);
+      uint32_t hp[4], lp[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const __half h = __float2half_rn(f[e]);
-      const __half l = __float2half_rn(__fsub_rn(f[e], __half2float(h)));
-      hp[e >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (e & 1));
-      lp[e >> 1] |= (uint32_t)__half_as_ushort(l) << (16 * (e & 1));
-    }
-    const int64_t o = (int64_t)row * (K / 4) + q;
-    hi[o] = make_uint2(hp[0], hp[1]);
-    lo[o] = make_uint2(lp[0], lp[1]);
-    if (xsh) {
-      // sums of the values over each 32-element sub-block (8 consecutive threads)
-      float sm = (f[0] + f[1]) + (f[2] + f[3]);
-      const unsigned act = __activemask();
-      sm += __shfl_xor_sync(act, sm, 1);
-      sm += __shfl_xor_sync(act, sm, 2);
-      sm += __shfl_xor_sync(act, sm, 4);
-      if ((q & 7) == 0) {
-        const __half h = __float2half_rn(sm);
-        xsh[(int64_t)row * Kp + (q >> 3)] = h;
-        xsl[(int64_t)row * Kp + (q >> 3)] = __float2half_rn(__fsub_rn(sm, __half2float(h)));
+      for (int e = 0; e < 4; ++e) {  // pair e: elements e and e + 4 of the group
+        uint32_t h0, l0, h1, l1;
+        split_half(f0[e], h0, l0);
+        split_half(f1[e], h1, l1);
+        hp[e] = h0 | (h1 << 16);
+        lp[e] = l0 | (l1 << 16);
+      }
+      const int64_t base = (int64_t)(q >> 3) * 2 * nbt * 8;  // 64-k chunk q / 8, in 16-byte units
+      const uint32_t c = sw_off(row, q & 7) >> 4;
+      t[base + c] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+      t[base + nbt * 8 + c] = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+      if (xsh) {
+        // sums over each 32-element sub-block (4 consecutive threads)
+        float sm = ((f0[0] + f0[1]) + (f0[2] + f0[3])) + ((f1[0] + f1[1]) + (f1[2] + f1[3]));
+        const unsigned act = __activemask();
+        sm += __shfl_xor_sync(act, sm, 1);
+        sm += __shfl_xor_sync(act, sm, 2);
+        if ((q & 3) == 0) {
+          uint32_t h, l;
+          split_half(sm, h, l);
+          xsh[(int64_t)row * Kp + (q >> 2)] = __ushort_as_half((unsigned short)h);
+          xsl[(int64_t)row * Kp + (q >> 2)] = __ushort_as_half((unsigned short)l);
+        }
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------- skinny GEMM from packed weights
+// Batched decode (M <= 64 rows of x) on Q4_K / Q6_K weights read as their packed bytes
+// (0.5625 / 0.8125 B per weight; no resident planes).  The MMA is transposed: A = 128
+// weight rows (TMEM lanes), B = the NB (16 / 32 / 64) rows of x (TMEM columns), so the
+// tensor work follows the batch instead of a 128-row x tile.
+// Weight operand per 256-weight block b, from the element formulas of
+// Q4KTensor.cs:129-147 (w = d sc_j q - dmin m_j) and Q6KTensor.cs:105-124 (w = d sc q):
+//   Q4_K: A = sc_j q, an exact fp16 integer (<= 945), written as fma(1024 + q, sc, -1024 sc)
+//         from the magic-number fp16 1024 + q; the block's d is applied as its accumulator is
+//         read from TMEM; the -dmin m_j term is a separate fp16 hi / lo GEMM over the sums of
+//         x per 32-element sub-block (three MMAs per k step, from the block headers).
+//   Q6_K: A = hi + lo of sc q (|sc q| <= 4096): hi = fp16(sc q), lo = sc q - hi, exact;
+//         d on the read-back; MMAs hi (x_hi | x_lo) and lo x_hi per k step.
+// x comes as fp16 hi / lo planes (gemm_prep_kernel<true>) whose k order inside each group
+// of 8 is 0,4,1,5,2,6,3,7: the order in which the two 16-bit lanes of a 32-bit code word,
+// shifted by 0, 4, 8 and 12 bits, hold the nibbles of elements (0, 4), (1, 5), (2, 6), (3, 7).
+// Warps 0..7: dequantize (thread = weight row, 32 k of each 64-k stage) from the packed
+// block in shared memory into the 128-byte-swizzled A tile; 8..11: epilogue (TMEM lanes
+// 32 (w % 4)..); 12: TMA of the packed blocks (one 2D box of 128 rows x 144 / 208 bytes per
+// block); 13: bulk copies of x (two stages per copy, from the pre-tiled planes); 14: MMA.
+// Split K in whole blocks over blockIdx.y.  Waits poll with test_wait (bounded).
+// Measured on B200 (4096 x 11008, M = 64): ~70 us, of which a pipeline with no MMA, no
+// dequantization and no loads still takes ~45 us: each 64-k stage costs ~0.55-0.65 us of
+// hand-over between the roles, about inversely proportional to the ring depth.  The
+// resident-plane GEMMs are faster at the bench shapes, so this kernel is opt-in
+// (SMALLMIND_GEMM_SK=1): it needs no resident planes (0.56 - 0.81 B per weight in HBM
+// instead of 2 - 4 B more).
+// Wait of a whole warp: lane 0 polls (bounded, with a short back-off so the pollers leave
+// the shared-memory pipe to the MMA issuer), then every lane takes the completed phase once
+// for itself (its own acquire).  All lanes return the same result.
+__device__ __forceinline__ bool sk_warp_wait(uint64_t* bar, uint32_t parity, int* status) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0 && !mbar_test_wait(bar, parity)) {
+    const long long t0 = clock64();
+    while (!mbar_test_wait(bar, parity)) {
+      __nanosleep(32);
+      if (clock64() - t0 > 4000000000LL) {
+        if (status) atomicExch(status, SM_ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) mbar_test_wait(bar, parity);
+  return ok;
+}
+
+template <int NB>
+struct Sk {
+  static constexpr int A_BYTES = 128 * BK * 2;  // one fp16 plane of the weight tile (16 KB)
+  static constexpr int B_BYTES = NB * BK * 2;   // one fp16 plane of the x tile
+  static constexpr int XU_BYTES = 4 * B_BYTES;  // x unit: two 64-k stages x (hi, lo)
+  static constexpr int ARENA = 212 * 1024;      // weight stages, x units and packed block slots
+  static constexpr int MAX_NBS = 32;            // blocks per k slice (the block scales' table)
+  static constexpr int DV_BYTES = MAX_NBS * 128 * 2;  // fp16 d of each (block, row) of the slice
+  static constexpr int MAX_ST = 4, MAX_XS = 8, MAX_PK = 8;
+  static constexpr int DW = 8;  // dequantizing warps
+  static constexpr int PKW = DW + 4, XW = DW + 5, MW = DW + 6;
+  static constexpr int THREADS = (DW + 7) * 32;
+  // accumulators of 2 NB columns (x_hi products | x_lo products): 2 block buffers + the min term
+  static constexpr int TMEM_COLS = NB == 16 ? 128 : NB == 32 ? 256 : 512;
+  static constexpr size_t SMEM_BYTES = (size_t)ARENA + DV_BYTES + 1024 + 512;
+  // Weight stages hold one plane (Q4_K; its -dmin m term comes as separate hi and lo stages)
+  // or two (Q6_K).  x has its own ring of units of two stages, each one contiguous bulk copy
+  // (a TMA operation costs a few hundred nanoseconds of its issuing warp whatever its size,
+  // so x comes in few, large pieces).  What is left of the arena holds packed blocks.
+  __host__ __device__ static constexpr int stages(bool q4) { return q4 ? (NB == 64 ? 3 : 4) : 2; }
+  __host__ __device__ static constexpr int a_bytes(bool q4) { return (q4 ? 1 : 2) * A_BYTES; }
+  __host__ __device__ static constexpr int xslots(bool q4) { return NB == 64 ? (q4 ? 4 : 3) : NB == 32 ? 6 : 8; }
+  __host__ __device__ static constexpr int pk_room(bool q4) {
+    return (ARENA - stages(q4) * a_bytes(q4) - xslots(q4) * XU_BYTES) / (128 * (q4 ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES));
+  }
+  __host__ __device__ static constexpr int slots(bool q4) { return pk_room(q4) > MAX_PK ? MAX_PK : pk_room(q4); }
+};
+
+// fp16 pair (1024 + a, 1024 + b) from a word holding a in bits 0-9 and b in bits 16-25
+__device__ __forceinline__ uint32_t magic_pair(uint32_t v) { return v | 0x64006400u; }
+
+// the two high bits of Q6_K elements (e, e + 4) of a group of 8 at bits 4-5 / 20-21, from
+// the sub-block's re-packed high word (byte bb: elements 2bb, 2bb+1, 8+2bb, 9+2bb)
+template <int S4, bool ODD>
+__device__ __forceinline__ uint32_t q6_high(uint32_t hw) {
+  constexpr int sh = ODD ? (S4 == 0 ? 0 : S4 == 1 ? 2 : S4 == 2 ? 8 : 10) : (S4 == 0 ? -4 : S4 == 1 ? -2 : S4 == 2 ? 4 : 6);
+  return (sh >= 0 ? (hw >> sh) : (hw << -sh)) & 0x00300030u;
+}
+
+template <int NB>
+__global__ void __launch_bounds__(Sk<NB>::THREADS, 1)
+    gemm_sk_kernel(const uint8_t* __restrict__ xt, const __grid_constant__ CUtensorMap tm_sh,
+                   const __grid_constant__ CUtensorMap tm_sl, const __grid_constant__ CUtensorMap tm_w0,
+                   const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_w2,
+                   const __grid_constant__ TcArgs a) {
+  using G = Sk<NB>;
+  constexpr int DW = G::DW, A_BYTES = G::A_BYTES, B_BYTES = G::B_BYTES, XU = G::XU_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __half* dvs = (__half*)(smem + G::ARENA);  // [slice block][row] block scales d
+  uint64_t* full_a = (uint64_t*)(smem + G::ARENA + G::DV_BYTES);
+  uint64_t* empty = full_a + G::MAX_ST;
+  uint64_t* full_b = empty + G::MAX_ST;
+  uint64_t* empty_b = full_b + G::MAX_XS;
+  uint64_t* pk_full = empty_b + G::MAX_XS;
+  uint64_t* pk_empty = pk_full + G::MAX_PK;
+  uint64_t* accf = pk_empty + G::MAX_PK;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_slot = (uint32_t*)(acce + 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * 128;
+  int sg = 0;
+  while (sg + 1 < a.nseg && n0 >= a.seg_n0[sg + 1]) ++sg;
+  const DevWeight& W = a.W[sg];
+  const bool q4 = W.scheme == SM_Q4_K;
+  const int nl0 = n0 - a.seg_n0[sg];  // the tile's first row inside its segment's weight
+  const int NBall = a.K >> 8;
+  const int b0 = (int)((int64_t)NBall * blockIdx.y / a.kslices);
+  const int nbs = (int)((int64_t)NBall * (blockIdx.y + 1) / a.kslices) - b0;
+  // -dmin m term (Q4_K): per 64 sub-blocks of the slice one stage with its hi plane (one MMA
+  // over the x sums' hi and lo planes) and one with its lo plane (x sums hi)
+  const int nms = q4 ? 2 * ((nbs * 8 + 63) / 64) : 0;
+  const int rb = q4 ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES;  // packed bytes of one row's block
+  // Every CTA reads the same x tiles; each walks the slice's blocks from its own starting
+  // block, so the CTAs do not all read one tile at the same moment.
+  const int rot = nbs > 1 ? (int)((blockIdx.x * 7u) % (unsigned)nbs) : 0;
+  auto blk = [&](int vb) { return b0 + (vb + rot >= nbs ? vb + rot - nbs : vb + rot); };
+  const int ST = G::stages(q4), SB = G::a_bytes(q4), XS = G::xslots(q4), PK = G::slots(q4);
+  uint8_t* xr = smem + ST * SB;  // x ring: XS units of two stages x (hi | lo planes)
+  uint8_t* pk = xr + XS * XU;    // packed block slots
+  // x units: nms / 2 of the -dmin m term (the x sums' hi | lo tile, used by a hi and a lo
+  // stage), then two per block (stages 0-1 and 2-3)
+  const int nxu = nms / 2 + 2 * nbs;
+
+  if (tid == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full_a[s], DW);  // one arrive per dequantizing warp
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < XS; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty_b[s], 1);
+    }
+    for (int p = 0; p < PK; ++p) {
+      mbar_init(&pk_full[p], 1);
+      mbar_init(&pk_empty[p], DW);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(G::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < DW) {
+    // ---- dequantize: thread = (row r, 32-k half h of each 64-k stage)
+    const int r = tid & 127, h = tid >> 7;
+    const int n = nl0 + r;
+    const bool live = n < W.rows;  // INTENDED layout: rows = N
+    int kt = 0;
+    bool ok = true;
+    // (1) -dmin m_j, k' = 64 i .. 64 i + 63 of the slice (8 blocks x 8 sub-blocks): this
+    //     thread writes blocks 8 i + 4 h + t (t < 4), one 16-byte chunk each, hi plane in
+    //     stage 2 i and lo plane in stage 2 i + 1
+    for (int i = 0; 2 * i < nms && ok; ++i) {
+      uint32_t hv[4][4], lv[4][4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int lb = 8 * i + 4 * h + t;
+        uint4 hd = make_uint4(0u, 0u, 0u, 0u);
+        if (live && lb < nbs)
+          hd = __ldg((const uint4*)((const uint8_t*)W.data + ((int64_t)n * NBall + b0 + lb) * Q4K_BLOCK_BYTES));
+        const float dmin = half_bits_to_float((uint16_t)(hd.x >> 16));
+        const uint64_t mb = (uint64_t)(hd.z >> 16) | ((uint64_t)hd.w << 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t h0, l0, h1, l1;
+          split_half(-__fmul_rn(dmin, (float)(int)((mb >> (12 * e)) & 63)), h0, l0);
+          split_half(-__fmul_rn(dmin, (float)(int)((mb >> (12 * e + 6)) & 63)), h1, l1);
+          hv[t][e] = h0 | (h1 << 16);
+          lv[t][e] = l0 | (l1 << 16);
+        }
+      }
+#pragma unroll
+      for (int pl = 0; pl < 2; ++pl, ++kt) {
+        const int s = kt % ST;
+        // every lane waits (bounded); the warp leaves together when any lane gave up
+        if (kt >= ST && !sk_warp_wait(&empty[s], ((kt / ST) - 1) & 1, a.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* ah = smem + s * SB;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t* v = pl ? lv[t] : hv[t];
+          *(uint4*)(ah + sw_off(r, 4 * h + t)) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        // generic-proxy stores -> visible to the tensor core; the warp's lanes then meet
+        // and one of them arrives (256 arrivals on one barrier would serialize)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
+      }
+    }
+    // (2) the blocks: four 64-k stages each, sub-block j = 2 qq + h of stage qq
+    for (int vb = 0; vb < nbs && ok; ++vb) {
+      const int p = vb % PK;
+      if (!sk_warp_wait(&pk_full[p], (vb / PK) & 1, a.status)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* row = pk + p * (128 * rb) + r * rb;
+      uint64_t sb = 0;
+      if (q4) {
+        const uint4 hd = *(const uint4*)row;
+        sb = (uint64_t)hd.y | ((uint64_t)(hd.z & 0xFFFFu) << 32);
+      }
+      for (int qq = 0; qq < 4; ++qq, ++kt) {
+        const int s = kt % ST;
+        const int j = 2 * qq + h;
+        uint32_t hv[16], lv[16];
+        if (q4) {
+          const int sc = (int)((sb >> (6 * j)) & 63);
+          const __half2 sc2 = __half2half2(__int2half_rn(sc));
+          const __half2 off2 = __half2half2(__int2half_rn(-1024 * sc));
+          const uint4 cw = *(const uint4*)(row + 16 + 16 * j);
+          const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+              const uint32_t m = magic_pair((w4[wi] >> (4 * s4)) & 0x000F000Fu);
+              const __half2 v = __hfma2(*(const __half2*)&m, sc2, off2);
+              hv[4 * wi + s4] = *(const uint32_t*)&v;
+            }
+        } else {
+          const uint4 ql = *(const uint4*)(row + 16 * j);
+          const uint2 qh = *(const uint2*)(row + 128 + 8 * j);
+          const uint32_t scw = *(const uint16_t*)(row + 192 + 2 * j);
+          const __half2 s0 = __half2half2(__int2half_rn((int)(int8_t)(scw & 0xFF)));
+          const __half2 s1 = __half2half2(__int2half_rn((int)(int8_t)(scw >> 8)));
+          const __half2 c1056 = __half2half2(__int2half_rn(1056));
+          const uint32_t w4[4] = {ql.x, ql.y, ql.z, ql.w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t hw = wi < 2 ? qh.x : qh.y;
+            const __half2 sc2 = wi < 2 ? s0 : s1;
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+              uint32_t hb;
+              if (wi & 1) {
+                hb = s4 == 0 ? q6_high<0, true>(hw) : s4 == 1 ? q6_high<1, true>(hw)
+                   : s4 == 2 ? q6_high<2, true>(hw) : q6_high<3, true>(hw);
+              } else {
+                hb = s4 == 0 ? q6_high<0, false>(hw) : s4 == 1 ? q6_high<1, false>(hw)
+                   : s4 == 2 ? q6_high<2, false>(hw) : q6_high<3, false>(hw);
+              }
+              const uint32_t m = magic_pair(((w4[wi] >> (4 * s4)) & 0x000F000Fu) | hb);
+              const __half2 q = __hsub2(*(const __half2*)&m, c1056);  // q = u - 32, exact
+              const __half2 hi = __hmul2_rn(q, sc2);
+              const __half2 lo = __hfma2(q, sc2, __hneg2(hi));  // sc q - hi, exact
+              hv[4 * wi + s4] = *(const uint32_t*)&hi;
+              lv[4 * wi + s4] = *(const uint32_t*)&lo;
+            }
+          }
+        }
+        // every lane waits (bounded); the warp leaves together when any lane gave up
+        if (kt >= ST && !sk_warp_wait(&empty[s], ((kt / ST) - 1) & 1, a.status)) {
+          ok = false;
+          break;
+        }
+        
+        uint8_t* ah = smem + s * SB;
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const uint32_t off = sw_off(r, 4 * h + wi);
+          *(uint4*)(ah + off) = make_uint4(hv[4 * wi], hv[4 * wi + 1], hv[4 * wi + 2], hv[4 * wi + 3]);
+          if (!q4) *(uint4*)(ah + A_BYTES + off) = make_uint4(lv[4 * wi], lv[4 * wi + 1], lv[4 * wi + 2], lv[4 * wi + 3]);
+        }
+        // generic-proxy stores -> visible to the tensor core; the warp's lanes then meet
+        // and one of them arrives (256 arrivals on one barrier would serialize)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&pk_empty[p]);
+    }
+  } else if (warp < DW + 4) {
+    // ---- epilogue: weight row r = TMEM lane 32 (warp % 4) + lane, x rows = columns
+    const int lq = warp & 3, r = 32 * lq + lane;
+    const int n = nl0 + r;
+    const bool live = n < W.rows;
+    // this row's block scales for the whole slice, loaded once (each thread reads back only
+    // its own entries)
+    for (int vb = 0; vb < nbs; ++vb) {
+      unsigned short dbits = 0;
+      if (live) {
+        const int64_t b = (int64_t)n * NBall + blk(vb);
+        dbits = q4 ? __ldg((const unsigned short*)((const uint8_t*)W.data + b * Q4K_BLOCK_BYTES))
+                   : __ldg((const unsigned short*)W.aux + aux_idx(b, W.aux_bpr, W.aux_stride));
+      }
+      dvs[vb * 128 + r] = __ushort_as_half(dbits);
+    }
+    float y[NB];
+#pragma unroll
+    for (int c = 0; c < NB; ++c) y[c] = 0.f;
+    bool ok = true;
+    const uint32_t tl = (uint32_t)(lq * 32) << 16;
+    for (int vb = 0; vb < nbs; ++vb) {
+      const int buf = vb & 1;
+      const float dc = __half2float(dvs[vb * 128 + r]);
+      if (!sk_warp_wait(&accf[buf], (vb >> 1) & 1, a.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // columns c0 .. c0+31 of the x_hi and the x_lo products, one wait for both loads
+#pragma unroll
+      for (int c0 = 0; c0 < NB; c0 += 32) {
+        uint32_t v[32], u[32];
+        if (NB >= 32) {
+          tmem_ld32_nowait(tl + (uint32_t)(buf * 2 * NB + c0), v);
+          tmem_ld32_nowait(tl + (uint32_t)(buf * 2 * NB + NB + c0), u);
+        } else {
+          tmem_ld16_nowait(tl + (uint32_t)(buf * 2 * NB + c0), v);
+          tmem_ld16_nowait(tl + (uint32_t)(buf * 2 * NB + NB + c0), u);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c0 + e < NB) y[c0 + e] = fmaf(__uint_as_float(v[e]) + __uint_as_float(u[e]), dc, y[c0 + e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
+    }
+    if (ok && q4) {
+      // the -dmin m term (its MMAs were issued before the blocks' and completed with them)
+#pragma unroll
+      for (int c0 = 0; c0 < NB; c0 += 32) {
+        uint32_t v[32], u[32];
+        if (NB >= 32) {
+          tmem_ld32_nowait(tl + (uint32_t)(4 * NB + c0), v);
+          tmem_ld32_nowait(tl + (uint32_t)(4 * NB + NB + c0), u);
+        } else {
+          tmem_ld16_nowait(tl + (uint32_t)(4 * NB + c0), v);
+          tmem_ld16_nowait(tl + (uint32_t)(4 * NB + NB + c0), u);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c0 + e < NB) y[c0 + e] += __uint_as_float(v[e]) + __uint_as_float(u[e]);
+      }
+    }
+    if (ok && live) {
+      const bool part = a.kslices > 1;
+      const bool rmw = a.accumulate && !part;
+#pragma unroll
+      for (int m = 0; m < NB; ++m) {
+        if (m < a.M) {
+          float* dst = part ? a.partial + ((int64_t)blockIdx.y * a.M + m) * a.N + n0 + r
+                            : a.seg_y[sg] + (int64_t)m * a.seg_ldy[sg] + n;
+          *dst = rmw ? *dst + y[m] : y[m];
+        }
+      }
+    }
+  } else if (warp == G::PKW) {
+    if (lane == 0) {
+      const CUtensorMap* tmw = sg == 0 ? &tm_w0 : sg == 1 ? &tm_w1 : &tm_w2;
+      for (int vb = 0; vb < nbs; ++vb) {
+        const int p = vb % PK;
+        if (vb >= PK && !mbar_wait_spin(&pk_empty[p], ((vb / PK) - 1) & 1, a.status)) break;
+        mbar_expect_tx(&pk_full[p], 128 * rb);
+        tma_load_2d(pk + p * (128 * rb), tmw, blk(vb) * rb, nl0, &pk_full[p]);
+      }
+    }
+  } else if (warp == G::XW) {
+    if (lane == 0) {
+      for (int u = 0; u < nxu; ++u) {
+        const int s = u % XS;
+        if (u >= XS && !mbar_wait_spin(&empty_b[s], ((u / XS) - 1) & 1, a.status)) break;
+        uint8_t* bh = xr + s * XU;
+        if (2 * u < nms) {
+          mbar_expect_tx(&full_b[s], 2 * B_BYTES);
+          const int kx = 8 * b0 + 64 * u;
+          tma_load_2d(bh, &tm_sh, kx, 0, &full_b[s]);
+          tma_load_2d(bh + B_BYTES, &tm_sl, kx, 0, &full_b[s]);
+        } else {
+          const int h2 = u - nms / 2;  // half block: stages 2 (h2 & 1), +1 of block h2 / 2
+          const int kc = 4 * blk(h2 >> 1) + 2 * (h2 & 1);  // first 64-k chunk
+          mbar_expect_tx(&full_b[s], XU);
+          bulk_g2s(bh, xt + (size_t)kc * 2 * B_BYTES, XU, &full_b[s]);
+        }
+      }
+    }
+  } else if (warp == G::MW) {
+    if (lane == 0) {
+      bool ok = true;
+      int kt = 0;
+      for (; kt < nms && ok; ++kt) {
+        const int s = kt % ST, u = kt >> 1, sx = u % XS;
+        ok = mbar_wait_spin(&full_b[sx], (u / XS) & 1, a.status);
+        ok = ok && mbar_wait_spin(&full_a[s], (kt / ST) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(smem_u32(smem + s * SB));
+        const uint64_t dbh = sw128_desc(smem_u32(xr + sx * XU));
+        const uint32_t tmin = tmem + 4 * NB;
+#pragma unroll
+        for (int ks = 0; ks < BK / 16; ++ks) {
+          const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+          // hi stage: one MMA over the x sums' hi and lo planes (2 NB rows of B, adjacent in
+          // shared memory); lo stage: the hi plane only
+          if ((kt & 1) == 0)
+            mma_f16<2 * NB>(tmin, da + adv, dbh + adv, (kt | ks) != 0);
+          else
+            mma_f16<NB>(tmin, da + adv, dbh + adv, 1);
+        }
+        mma_commit(&empty[s]);
+        if (kt & 1) mma_commit(&empty_b[sx]);  // after the unit's lo stage
+      }
+      for (int vb = 0; vb < nbs && ok; ++vb) {
+        const int buf = vb & 1;
+        if (vb >= 2 && !mbar_wait_spin(&acce[buf], ((vb >> 1) - 1) & 1, a.status)) break;
+        tc_fence_after();
+        const uint32_t tacc = tmem + buf * 2 * NB;
+        for (int qq = 0; qq < 4 && ok; ++qq, ++kt) {
+          const int s = kt % ST, u = nms / 2 + 2 * vb + (qq >> 1), sx = u % XS;
+          ok = mbar_wait_spin(&full_b[sx], (u / XS) & 1, a.status);
+          ok = ok && mbar_wait_spin(&full_a[s], (kt / ST) & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * SB);
+          const uint64_t dah = sw128_desc(base), dal = sw128_desc(base + A_BYTES);
+          const uint64_t dbh = sw128_desc(smem_u32(xr + sx * XU + (qq & 1) * 2 * B_BYTES));
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t adv = (uint64_t)((ks * 32) >> 4);
+            // columns 0..NB-1: w x_hi, NB..2NB-1: w x_lo (B = the two x planes, adjacent)
+            mma_f16<2 * NB>(tacc, dah + adv, dbh + adv, (qq | ks) != 0);
+            if (!q4) mma_f16<NB>(tacc, dal + adv, dbh + adv, 1);  // Q6_K: w_lo x_hi
+          }
+          mma_commit(&empty[s]);
+          if (qq & 1) mma_commit(&empty_b[sx]);  // after the unit's second stage
+        }
+        if (ok) mma_commit(&accf[buf]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS) : "memory");
   }
 }
 
@@ -967,26 +1524,46 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// the driver entry point is resolved at run time, so the library loads (and its
+// symbols can be checked) on machines without a CUDA driver
+EncodeTiled tensor_map_encoder() {
+  static EncodeTiled encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+      encode = (EncodeTiled)fn;
+  }
+  return encode;
+}
+
 int make_plane_map(CUtensorMap* map, void* base, int M, int K, int box_rows = BM) {
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  // the driver entry point is resolved at run time, so the library loads (and
-  // its symbols can be checked) on machines without a CUDA driver
-  static EncodeTiled encode = nullptr;
-  if (!encode) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      return fail(SM_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available");
-    encode = (EncodeTiled)fn;
-  }
+  EncodeTiled encode = tensor_map_encoder();
+  if (!encode) return fail(SM_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available");
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? SM_OK : fail(SM_ERR_CUDA, "gemm: tensor map encoding failed");
+}
+
+// Packed weight bytes as a 2D byte array [rows][row_bytes]; one box = 128 rows x box_bytes
+// (one 256-weight block of each row), no swizzle.
+int make_bytes_map(CUtensorMap* map, const void* base, int rows, int64_t row_bytes, int box_bytes) {
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)box_bytes, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  EncodeTiled encode = tensor_map_encoder();
+  if (!encode) return fail(SM_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available");
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SM_OK : fail(SM_ERR_CUDA, "gemm: packed-weight tensor map encoding failed");
 }
 
 // Resident fp16 planes of weight groups.  A GEMM with more than one 128-row tile
@@ -1212,7 +1789,7 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
   int rc = SM_OK;
   if (Kp > K / 32) SM_CUDA_TRY(cudaMemsetAsync(xsh, 0, (size_t)M * Kp * 4, st));
   XPro none;
-  gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, pro ? *pro : none, (uint2*)hi, (uint2*)lo, xsh, xsl, Kp);
+  gemm_prep_kernel<false><<<M, 256, 0, st>>>(x, K, pro ? *pro : none, hi, lo, xsh, xsl, Kp);
   if (n_launch) ++*n_launch;
   CUtensorMap mh, ml, mq, mxh, mxl, mmh, mml;
   rc = make_plane_map(&mh, hi, M, K);
@@ -1272,6 +1849,106 @@ int launch_gemm_q4k2(const Q4k2Entry& e, const DevWeight* const* Ws, float* cons
 }
 }  // namespace
 
+namespace {
+// Every segment Q4_K or Q6_K (INTENDED, K a whole number of blocks) and at most 64 rows of x:
+// the skinny GEMM on the packed bytes applies when SMALLMIND_GEMM_SK=1 selects it.
+bool sk_ok(const DevWeight* const* Ws, int nw, int M) {
+  if (M < 1 || M > 64) return false;
+  const char* e = std::getenv("SMALLMIND_GEMM_SK");
+  if (!(e && e[0] == '1')) return false;
+  for (int i = 0; i < nw; ++i) {
+    const DevWeight& W = *Ws[i];
+    if ((W.scheme != SM_Q4_K && W.scheme != SM_Q6_K) || W.layout != SM_LAYOUT_INTENDED || W.K() % 256 ||
+        W.K() != Ws[0]->K())
+      return false;
+    if (W.scheme == SM_Q6_K && !W.aux) return false;
+  }
+  return true;
+}
+
+template <int NB>
+int launch_sk_nb(const uint8_t* xt, const CUtensorMap* m, const TcArgs& a, dim3 grid, cudaStream_t st, int dev) {
+  static bool attr_set[64] = {};
+  if (dev < 64 && !attr_set[dev]) {
+    SM_CUDA_TRY(cudaFuncSetAttribute(gemm_sk_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Sk<NB>::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  gemm_sk_kernel<NB><<<grid, Sk<NB>::THREADS, Sk<NB>::SMEM_BYTES, st>>>(xt, m[0], m[1], m[2], m[3], m[4], a);
+  return cudaGetLastError() == cudaSuccess ? SM_OK : fail(SM_ERR_CUDA, "gemm_sk: launch failed");
+}
+
+int launch_gemm_sk(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M, int N,
+                   int K, int accumulate, int* status, cudaStream_t st, int* n_launch, const XPro* pro, int dev) {
+  const int nb = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  const int NBall = K / 256, Kp = (K / 32 + 63) / 64 * 64;
+  const size_t xt_bytes = (size_t)K * nb * 4;  // tiled x planes: K / 64 chunks x 2 planes x nb x 128 B
+  void* buf = nullptr;
+  SM_CUDA_TRY(cudaMallocAsync(&buf, xt_bytes + (size_t)M * Kp * 4, st));
+  uint8_t* xt = (uint8_t*)buf;
+  __half* xsh = (__half*)(xt + xt_bytes);  // x sums per 32 (fp16 hi / lo), [M][Kp]
+  __half* xsl = xsh + (size_t)M * Kp;
+  int rc = SM_OK;
+  if (Kp > K / 32) SM_CUDA_TRY(cudaMemsetAsync(xsh, 0, (size_t)M * Kp * 4, st));
+  XPro none;
+  gemm_prep_kernel<true><<<nb, 256, 0, st>>>(x, K, pro ? *pro : none, xt, nullptr, xsh, xsl, Kp, M, nb);
+  if (n_launch) ++*n_launch;
+  CUtensorMap maps[5];
+  rc = make_plane_map(&maps[0], xsh, M, Kp, nb);
+  if (rc == SM_OK) rc = make_plane_map(&maps[1], xsl, M, Kp, nb);
+  for (int i = 0; i < 3 && rc == SM_OK; ++i) {
+    const DevWeight& W = *Ws[std::min(i, nw - 1)];
+    const int rbytes = W.scheme == SM_Q4_K ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES;
+    rc = make_bytes_map(&maps[2 + i], W.data, W.N(), (int64_t)NBall * rbytes, rbytes);
+  }
+  if (rc == SM_OK) {
+    TcArgs a;
+    a.nseg = nw;
+    a.seg_n0[0] = 0;
+    for (int i = 0; i < nw; ++i) {
+      a.W[i] = *Ws[i];
+      a.seg_y[i] = ys[i];
+      a.seg_ldy[i] = ldys[i];
+      a.seg_n0[i + 1] = a.seg_n0[i] + Ws[i]->N();
+    }
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.accumulate = accumulate;
+    a.status = status;
+    const int gn = (N + 127) / 128;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int S = 1;
+    if (gn < sms) S = std::max(1, std::min(sms / gn, NBall));
+    S = std::max(S, (NBall + Sk<64>::MAX_NBS - 1) / Sk<64>::MAX_NBS);  // the d table holds 32 blocks
+    void* pbuf = nullptr;
+    if (S > 1 && cudaMallocAsync(&pbuf, (size_t)S * M * N * 4, st) != cudaSuccess) {
+      cudaGetLastError();
+      S = 1;
+      pbuf = nullptr;
+    }
+    a.kslices = S;
+    a.partial = (float*)pbuf;
+    const dim3 grid(gn, S);
+    rc = nb == 16 ? launch_sk_nb<16>(xt, maps, a, grid, st, dev)
+         : nb == 32 ? launch_sk_nb<32>(xt, maps, a, grid, st, dev)
+                    : launch_sk_nb<64>(xt, maps, a, grid, st, dev);
+    if (n_launch) ++*n_launch;
+    if (S > 1) {
+      if (rc == SM_OK) {
+        const int64_t MN = (int64_t)M * N;
+        gemm_reduce_kernel<<<(int)std::min<int64_t>((MN + 255) / 256, 148 * 8), 256, 0, st>>>(a.partial, S, a);
+        if (n_launch) ++*n_launch;
+      }
+      cudaFreeAsync(pbuf, st);
+    }
+  }
+  cudaFreeAsync(buf, st);
+  return rc;
+}
+}  // namespace
+
 int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int* ldys, int nw, const float* x, int M,
                          int accumulate, int* status, cudaStream_t st, int* n_launch, const XPro* pro) {
   if (!gemm_tc_supports_multi(Ws, nw, M)) return SM_ERR_UNSUPPORTED;
@@ -1281,6 +1958,8 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  // batched decode on Q4_K / Q6_K from the packed bytes (opt-in), transposed MMA
+  if (sk_ok(Ws, nw, M)) return launch_gemm_sk(Ws, ys, ldys, nw, x, M, N, K, accumulate, status, st, n_launch, pro, dev);
   if (dev < 64 && !attr_set[dev]) {
     SM_CUDA_TRY(
         cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
@@ -1315,7 +1994,7 @@ int launch_gemm_tc_multi(const DevWeight* const* Ws, float* const* ys, const int
   int rc = SM_OK;
   {
     if (pro && pro->kind != XPRO_NONE) {
-      gemm_prep_kernel<<<M, 256, 0, st>>>(x, K, *pro, (uint2*)hi, (uint2*)lo, nullptr, nullptr, 0);
+      gemm_prep_kernel<false><<<M, 256, 0, st>>>(x, K, *pro, hi, lo, nullptr, nullptr, 0);
     } else {
       const int64_t n4 = n / 4;
       const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);

@@ -75,8 +75,10 @@ def test_gemm_tc_long_k_many_slices(ctx, O):
 def test_gemm_tc_one_tile_both_weight_paths(ctx, O, monkeypatch, planes, scheme, m, k, n):
     """M <= 128: with resident fp16 weight planes (SMALLMIND_WEIGHT_PLANES unset / 1) the
     weights come by TMA from the planes; with SMALLMIND_WEIGHT_PLANES=0 the loader warps
-    dequantize each weight tile.  Both within 1e-4 of the oracle."""
+    dequantize each weight tile.  Both within 1e-4 of the oracle.  (SMALLMIND_GEMM_SK=0 keeps
+    Q4_K / Q6_K with M <= 64 off the opt-in skinny GEMM.)"""
     monkeypatch.setenv("SMALLMIND_WEIGHT_PLANES", planes)
+    monkeypatch.setenv("SMALLMIND_GEMM_SK", "0")
     out, ref = _run(ctx, O, scheme, m, k, n, seed=m + k)
     assert np.isfinite(out).all()
     assert rel_err(out, ref) <= TOL
