@@ -128,7 +128,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 // 32 columns of this warp's 32 TMEM lanes, without waiting (tmem_wait_ld completes them)
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
       "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -741,12 +741,22 @@ __global__ void __launch_bounds__(Q2<NB>::THREADS, 1)
       if (!ok) break;
       tc_fence_after();
       const float* db = dsm + vb * NB + ch;
+      // the read-back of a block gates the MMAs of the block after next: the 128-wide form
+      // (few x rows, 192 threads) has the registers for 64 columns per wait
+      constexpr int CW = NB == 128 ? 64 : 16;
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * NB + ch + c0), v);
+      for (int c0 = 0; c0 < 128; c0 += CW) {
+        uint32_t v[CW];
+        const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * NB + ch + c0);
+        if (CW == 64) {
+          tmem_ld32_nowait(ta, v);
+          tmem_ld32_nowait(ta + 32, v + 32);
+          tmem_wait_ld();
+        } else {
+          tmem_ld16(ta, *(uint32_t(*)[16])v);
+        }
 #pragma unroll
-        for (int e = 0; e < 16; ++e) y[c0 + e] = fmaf(__uint_as_float(v[e]), db[c0 + e], y[c0 + e]);
+        for (int e = 0; e < CW; ++e) y[c0 + e] = fmaf(__uint_as_float(v[e]), db[c0 + e], y[c0 + e]);
       }
       tc_fence_before();
       __syncwarp();
