@@ -888,8 +888,16 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
   const float* xr = x + (int64_t)row * K;
   float inv = 1.f;
   if (pro.kind == XPRO_RMSNORM) {
+    // sum of squares from 16-byte loads, several in flight per thread (K % 4 == 0)
     float s = 0.f;
-    for (int f = threadIdx.x; f < K; f += blockDim.x) s = fmaf(xr[f], xr[f], s);
+#pragma unroll 4
+    for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
+      const float4 v = ((const float4*)xr)[q];
+      s = fmaf(v.x, v.x, s);
+      s = fmaf(v.y, v.y, s);
+      s = fmaf(v.z, v.z, s);
+      s = fmaf(v.w, v.w, s);
+    }
     __shared__ float red[32];
     s = warp_sum(s);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
@@ -906,6 +914,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
   if (!TILED) {
     uint2* hi = (uint2*)hi_;
     uint2* lo = (uint2*)lo_;
+#pragma unroll 4
     for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
       const float4 v = ((const float4*)xr)[q];
       float f[4] = {v.x, v.y, v.z, v.w};
