@@ -866,7 +866,9 @@ def main():
     ap.add_argument("--gemv-sweep", action="store_true", help="time the M=1 GEMV on the op-sweep shapes and exit")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="time M = 8, 64, 512, 2048 on the op-sweep shapes and exit")
-    ap.add_argument("--gemv-only", default=None, help="restrict --gemv-sweep to 'SCHEME KxN' (profiling)")
+    ap.add_argument("--gemv-only", default=None,
+                    help="restrict --gemv-sweep to 'SCHEME KxN', or --gemm-sweep to 'SCHEME KxN' / 'SCHEME KxN MROWS' "
+                         "(profiling)")
     ap.add_argument("--profile-region", action="store_true",
                     help="bracket the timed decode loop (or, with --prefill-only, the timed prefill) with "
                          "cudaProfilerStart/Stop (ncu --profile-from-start off)")
